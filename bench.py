@@ -1,0 +1,544 @@
+"""Decode hot-path benchmark: paged decode attention HBM GB/s and decode tok/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|long|verify]
+                    [--impl ours|reference]
+
+One step = one decode step of one attention layer for every sequence this GPU owns:
+a one-token KV append per sequence (reshape_and_cache) followed by paged attention
+over the sequence's context including that token; with N > 1 the outputs of all ranks
+are gathered over NCCL inside the step.  Workloads (synthetic, seeded):
+
+  decode  64 sequences per GPU, context lengths uniform in [512, 8192], 32 query heads
+          over 8 KV heads, head_dim 128, block 16, pool = sequences + 10 % free blocks,
+          block tables a random permutation of the pool, Q/K/V ~ N(0,1) in bf16
+  long    32 sequences per GPU, lengths uniform in [16384, 32768], same heads
+  verify  32 sequences per GPU, lengths uniform in [1024, 4096], k = 4 drafts + 1 query
+          (5 queries, causal inside the window), 5-token append per sequence
+
+`value` is algorithmic bytes (KV read + Q read + output write + block tables + the
+append's read/write) of all ranks divided by the max-over-ranks device time of the K
+timed steps, inputs resident in HBM; the KV pool (>= 1 GB per GPU) is larger than L2, so
+no flush is needed between steps.  `e2e` repeats the step through the public Python
+API with host (pinned) inputs and a device->host read of the output every step.
+Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+HQ, HKV, D, BS = 32, 8, 128, 16
+ELEM = 2  # bf16
+
+WORKLOADS = {
+    "decode": dict(seqs=64, lo=512, hi=8192, q_len=1, config_index=1),
+    "long": dict(seqs=32, lo=16384, hi=32768, q_len=1, config_index=4),
+    "verify": dict(seqs=32, lo=1024, hi=4096, q_len=5, config_index=2),
+}
+
+
+# ------------------------------------------------------------------ workload
+def context_lengths(workload: str, world: int, seed: int = 0) -> np.ndarray:
+    """Lengths of all sequences of the job (world * seqs); rank r owns a contiguous slice."""
+    w = WORKLOADS[workload]
+    rng = np.random.default_rng(seed)
+    return rng.integers(w["lo"], w["hi"] + 1, size=w["seqs"] * world)
+
+
+def step_bytes(ctx_lens, q_len: int) -> dict:
+    """Algorithmic bytes of one step for sequences whose context (after the append) is
+    ctx_lens: K and V of every visible key, query read, output write, block-table and
+    context-length reads, and the append (read new K/V, write them to the pool, slots)."""
+    ctx = np.asarray(ctx_lens, dtype=np.int64)
+    b = ctx.size
+    pages = (ctx + BS - 1) // BS
+    attn = int(ctx.sum()) * HKV * D * ELEM * 2 + b * q_len * HQ * D * ELEM * 2 \
+        + int(pages.sum()) * 4 + b * 4
+    append = b * q_len * HKV * D * ELEM * 2 * 2 + b * q_len * 8
+    return {"attention": attn, "append": append, "total": attn + append}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self) -> None:
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "", 1).isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "", 1).isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d.get("hbm_gbs"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def ncu_traffic(workload: str) -> float | None:
+    """DRAM bytes per attention launch from the committed ncu summary, if present."""
+    f = REPO / "profiles" / f"paged_attention_{workload}.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch_full_size:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------ our arm
+class DeviceWorkload:
+    """One rank's share of the workload, resident on its GPU."""
+
+    def __init__(self, workload: str, rank: int, world: int, device: torch.device) -> None:
+        w = WORKLOADS[workload]
+        self.q_len = w["q_len"]
+        all_lens = context_lengths(workload, world)
+        self.base = all_lens[rank * w["seqs"]:(rank + 1) * w["seqs"]].astype(np.int64)
+        self.b = self.base.size
+        # context after the append = base + q_len (the appended tokens sit at base .. )
+        self.ctx = self.base + self.q_len
+        pages = (self.ctx + BS - 1) // BS
+        self.num_blocks = int(math.ceil(1.1 * pages.sum()))
+        g = torch.Generator(device=device).manual_seed(1234 + rank)
+        shape = (self.num_blocks, HKV, BS, D)
+        self.kc = torch.randn(shape, generator=g, device=device, dtype=torch.bfloat16)
+        self.vc = torch.randn(shape, generator=g, device=device, dtype=torch.bfloat16)
+        gc = torch.Generator().manual_seed(99 + rank)
+        perm = torch.randperm(self.num_blocks, generator=gc).numpy()
+        width = int(pages.max())
+        bt = np.zeros((self.b, width), dtype=np.int32)
+        s = 0
+        for i, p in enumerate(pages.tolist()):
+            bt[i, :p] = perm[s:s + p]
+            s += p
+        self.bt_host = bt
+        self.bt = torch.from_numpy(bt).to(device)
+        self.cl = torch.from_numpy(self.ctx.astype(np.int32)).to(device)
+        slots = []
+        for i in range(self.b):
+            for j in range(self.q_len):
+                pos = int(self.base[i]) + j
+                slots.append(int(bt[i, pos // BS]) * BS + pos % BS)
+        self.slots = torch.tensor(slots, dtype=torch.int64, device=device)
+        self.q = torch.randn(self.b, self.q_len, HQ, D, generator=g, device=device,
+                             dtype=torch.bfloat16)
+        self.k_new = torch.randn(self.b * self.q_len, HKV, D, generator=g, device=device,
+                                 dtype=torch.bfloat16)
+        self.v_new = torch.randn_like(self.k_new)
+        self.out = torch.empty_like(self.q)
+        self.max_ctx = int(self.ctx.max())
+        self.bytes = step_bytes(self.ctx, self.q_len)
+
+
+def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
+    import torch.distributed as dist
+
+    from inferd_b200 import _lib
+    from inferd_b200.paged_attn import paged_attention_batched
+
+    lib = _lib.load()
+    wl = DeviceWorkload(args.workload, rank, world, device)
+    stream = torch.cuda.current_stream(device)
+    err = _lib.error_word(device)
+    gathered = torch.empty((world * wl.b,) + tuple(wl.out.shape[1:]), dtype=wl.out.dtype,
+                           device=device) if world > 1 else None
+
+    def append():
+        st = lib.inferd_reshape_and_cache(
+            wl.k_new.data_ptr(), wl.v_new.data_ptr(), wl.k_new.stride(0), wl.k_new.stride(1),
+            wl.v_new.stride(0), wl.v_new.stride(1), wl.kc.data_ptr(), wl.vc.data_ptr(),
+            wl.slots.data_ptr(), wl.slots.numel(), HKV, D, BS, wl.num_blocks, 2,
+            err.data_ptr(), stream.cuda_stream)
+        _lib.check(st, "reshape_and_cache")
+
+    def attend():
+        paged_attention_batched(wl.q, wl.kc, wl.vc, wl.bt, wl.cl, max_context_len=wl.max_ctx,
+                                out=wl.out)
+
+    def step(ev=None):
+        append()
+        if ev is not None:
+            ev[0].record(stream)
+        attend()
+        if ev is not None:
+            ev[1].record(stream)
+        if gathered is not None:
+            dist.all_gather_into_tensor(gathered, wl.out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    _lib.raise_device_errors(device)
+
+    k = args.steps
+    attn_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(k)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(device.index if device.index is not None else 0)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    sampler.start()
+    time.sleep(0.25)  # let the sampler attach before the timed region
+    t0.record(stream)
+    for i in range(k):
+        step(attn_ev[i])
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    clocks = sampler.stop()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    attn_ms = sum(a.elapsed_time(b) for a, b in attn_ev) / k
+    _lib.raise_device_errors(device)
+
+    # max over ranks of the timed region; bytes summed over ranks
+    stats = torch.tensor([elapsed_ms, attn_ms, float(wl.bytes["total"]),
+                          float(wl.bytes["attention"]), float(wl.b)], dtype=torch.float64,
+                         device=device)
+    if world > 1:
+        mx = stats.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = stats.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        elapsed_ms, attn_ms = float(mx[0]), float(mx[1])
+        total_bytes, attn_bytes, seqs = float(sm[2]), float(sm[3]), float(sm[4])
+    else:
+        total_bytes, attn_bytes, seqs = float(stats[2]), float(stats[3]), float(stats[4])
+    ms_per_step = elapsed_ms / k
+    value_gbs = total_bytes / (ms_per_step * 1e-3) / 1e9
+
+    e2e = run_e2e(args, wl, rank, world, device)
+
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    achieved = wl.bytes["attention"] / (attn_ms * 1e-3) / 1e9  # this rank's kernel
+    traffic = ncu_traffic(args.workload)
+    line = {
+        "metric": "paged-decode attn HBM GB/s (% of peak) & decode tok/s at 1/2/4/8 B200",
+        "value": round(value_gbs, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": k,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) Q/K/V in bf16, seeded uniform context lengths, "
+                "randomly permuted block tables)",
+        "config": {
+            "workload": {"decode": "config 2: batched paged decode",
+                         "long": "config 5: long-context sharded decode",
+                         "verify": "config 3: speculative verify"}[args.workload],
+            "seqs_per_gpu": wl.b, "context_lo": WORKLOADS[args.workload]["lo"],
+            "context_hi": WORKLOADS[args.workload]["hi"], "q_len": wl.q_len,
+            "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "block_size": BS,
+            "pool_blocks_per_gpu": wl.num_blocks,
+            "parallelism": f"sequence shards x{world}, outputs all-gathered over NCCL"
+            if world > 1 else "single GPU",
+            "l2": "no flush: each step reads >= %.2f GB of KV per GPU (L2 is 126 MB)"
+                  % (wl.bytes["attention"] / 1e9),
+        },
+        "decode_tok_s": round(seqs * wl.q_len / (ms_per_step * 1e-3), 1),
+        "attention_ms": round(attn_ms, 5),
+        "attention_gbs_per_gpu": round(achieved, 1),
+        "pct_of_hbm_peak": round(100.0 * achieved / peaks["hbm_gbs"], 2),
+        "roofline": {
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+            "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+            "traffic": traffic, "peak_source": peaks["source"],
+            "kernel": "paged_attn_tc_kernel",
+        },
+        "clocks": clocks,
+        "e2e": e2e,
+        "gpu_launches": 2 * k,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.workload, budget_s=args.cpu_budget)
+    return line
+
+
+def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.device) -> dict:
+    """Same step through the public API with pinned host inputs and a host read of the
+    result every step: PagedKVCache.append_tokens_batched -> decode_metadata ->
+    paged_attention_batched -> (all-gather) -> device-to-host copy."""
+    import torch.distributed as dist
+
+    from inferd_b200.paged_attn import paged_attention_batched
+    from inferd_b200.paged_cache import PagedKVCache
+
+    ql = dwl.q_len
+    cache = PagedKVCache(num_layers=1, num_blocks=dwl.num_blocks, block_size=BS,
+                         num_kv_heads=HKV, head_dim=D, dtype=torch.bfloat16, device=device)
+    cache.key_cache[0] = dwl.kc
+    cache.value_cache[0] = dwl.vc
+    used = set()
+    ids = list(range(dwl.b))
+    for i in ids:
+        t = cache.create_sequence(i)
+        p = (int(dwl.base[i]) + BS - 1) // BS
+        t.blocks = dwl.bt_host[i, :p].tolist()
+        t.length = int(dwl.base[i])
+        used.update(t.blocks)
+    cache.allocator._allocated = set(used)
+    cache.allocator._free = [x for x in cache.allocator._free if x not in used]
+    q_h = dwl.q.cpu().pin_memory()
+    k_h = dwl.k_new.cpu().pin_memory()
+    v_h = dwl.v_new.cpu().pin_memory()
+    out_rows = dwl.b * world
+    out_h = torch.empty((out_rows, ql, HQ, D), dtype=torch.bfloat16).pin_memory()
+    gathered = torch.empty((out_rows, ql, HQ, D), dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+    steps = max(1, min(args.steps, args.e2e_steps))
+    h2d = d2h = 0
+    total_bytes = 0.0
+
+    def one_step():
+        nonlocal h2d, d2h, total_bytes
+        q = q_h.to(device, non_blocking=True)
+        k = k_h.to(device, non_blocking=True)
+        v = v_h.to(device, non_blocking=True)
+        cache.append_tokens_batched(ids, [k], [v])
+        bt, cl, mx = cache.decode_metadata(ids)
+        out = paged_attention_batched(q, cache.key_cache[0], cache.value_cache[0], bt, cl,
+                                      max_context_len=mx)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+            res = gathered
+        else:
+            res = out
+        out_h[: res.shape[0]].copy_(res, non_blocking=True)
+        stream.synchronize()
+        ctx = [cache.sequence_length(i) for i in ids]
+        total_bytes += step_bytes(ctx, ql)["total"]
+        h2d = (q.numel() + k.numel() + v.numel()) * ELEM + dwl.b * ql * 8 \
+            + bt.numel() * 4 + cl.numel() * 4
+        d2h = res.numel() * ELEM
+
+    one_step()  # warm the path (pinned staging, workspace)
+    total_bytes = 0.0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        one_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms, total_bytes], dtype=torch.float64, device=device)
+    if world > 1:
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms, total_bytes = float(mx[0]), float(sm[1])
+    return {"value": round(total_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "steps": steps, "ms_per_step": round(ms / steps, 5),
+            "note": "contexts grow by the appended tokens each step; bytes counted per step"}
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle)
+class CpuWork:
+    """The oracle (numpy restatement of the reference's per-sequence gather + attention)
+    on a sample of the workload's sequences, bf16 data widened to fp32 like the reference's
+    fp32 path."""
+
+    def __init__(self, workload: str, max_seqs: int = 8) -> None:
+        w = WORKLOADS[workload]
+        lens = context_lengths(workload, 1)[:max_seqs].astype(np.int64) + w["q_len"]
+        self.q_len = w["q_len"]
+        self.lens = lens
+        pages = (lens + BS - 1) // BS
+        nb = int(pages.sum())
+        rng = np.random.default_rng(7)
+        self.kc = rng.standard_normal((nb, HKV, BS, D), dtype=np.float32)
+        self.vc = rng.standard_normal((nb, HKV, BS, D), dtype=np.float32)
+        perm = rng.permutation(nb)
+        self.tables, s = [], 0
+        for p in pages.tolist():
+            self.tables.append(perm[s:s + p])
+            s += p
+        self.q = rng.standard_normal((lens.size, self.q_len, HQ, D), dtype=np.float32)
+
+    def run_seq(self, i: int) -> int:
+        import oracle
+
+        L = int(self.lens[i])
+        if self.q_len == 1:
+            oracle.paged_attention(self.q[i, 0], self.kc, self.vc, self.tables[i], L)
+        else:
+            k, v = oracle.gather_paged_kv(self.kc, self.vc, self.tables[i], L)
+            oracle.verify_attention(self.q[i], k, v)
+        return step_bytes([L], self.q_len)["total"]
+
+
+def cpu_baseline(workload: str, budget_s: float = 15.0) -> dict:
+    work = CpuWork(workload)
+    t0 = time.perf_counter()
+    done = 0
+    nbytes = 0
+    i = 0
+    while time.perf_counter() - t0 < budget_s or done == 0:
+        nbytes += work.run_seq(i % work.lens.size)
+        done += 1
+        i += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": _cpu_threads(),
+            "kind": "port",
+            "sample": f"{done} single-sequence decode steps (oracle: per-sequence gather + "
+                      f"GQA attention in numpy fp32, cycling over {work.lens.size} sequences of "
+                      f"the workload), {dt:.1f} s"}
+
+
+def _cpu_threads() -> int:
+    try:
+        import threadpoolctl
+
+        info = threadpoolctl.threadpool_info()
+        n = max((d.get("num_threads", 1) for d in info), default=1)
+        return int(n)
+    except Exception:  # pragma: no cover - informational only
+        return os.cpu_count() or 1
+
+
+def run_reference(args, rank: int, world: int) -> dict | None:
+    """Reference arm: the oracle port of the reference's CPU path, timed on host cores.
+    Each step is one sequence of the workload (cycling), all host threads available."""
+    if rank != 0:
+        return None
+    work = CpuWork(args.workload)
+    for i in range(args.warmup):
+        work.run_seq(i % work.lens.size)
+    t0 = time.perf_counter()
+    nbytes = 0
+    for i in range(args.steps):
+        nbytes += work.run_seq(i % work.lens.size)
+    dt = time.perf_counter() - t0
+    v = round(nbytes / dt / 1e9, 3)
+    return {
+        "metric": "paged-decode attn HBM GB/s (% of peak) & decode tok/s at 1/2/4/8 B200",
+        "impl": "reference", "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": args.workload, "q_heads": HQ,
+                                        "kv_heads": HKV, "head_dim": D, "block_size": BS},
+        "cpu_baseline": {"value": v, "unit": "GB/s", "cores": _cpu_threads(), "kind": "port",
+                         "sample": "one sequence of the workload per step, cycling over the "
+                                   f"first {work.lens.size} sequences"},
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ------------------------------------------------------------------ main
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=device,
+                                timeout=datetime.timedelta(seconds=120))
+    try:
+        line = run_ours(args, rank, world, device)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

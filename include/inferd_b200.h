@@ -1,0 +1,143 @@
+/*
+ * inferd_b200.h -- C ABI of the sm_100a decode hot path (libinferd_sm100a.so).
+ *
+ * Every entry point takes raw device pointers, sizes and a cudaStream_t passed as
+ * `void*`, enqueues its kernels on that stream and returns an `int` status from
+ * inferd_status_t without synchronising.  No torch or CUDA types appear in the
+ * signatures, so the library can be bound from ctypes, cgo, JNI or N-API alike.
+ *
+ * Tensor layouts (all contiguous in the innermost dimension):
+ *   KV pool      key_cache / value_cache : [num_blocks, num_kv_heads, block_size, head_dim]
+ *                (core/paged_cache.py:131-137 of the reference)
+ *   query / out  [num_seqs, q_len, num_q_heads, head_dim]
+ *   block table  [num_seqs, block_table_stride] of int32 or int64 block ids
+ *   slot mapping [num_tokens] int64, slot = block * block_size + offset; slot < 0 skips
+ *
+ * Device-detected errors (a block id or slot outside the pool, a bounded wait that
+ * expired) never trap: the kernel records the first error code in *error_word
+ * (when error_word is non-NULL), skips or clamps the offending access and finishes.
+ * The caller reads the word whenever it chooses to synchronise.
+ */
+#ifndef INFERD_B200_H
+#define INFERD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define INFERD_API __attribute__((visibility("default")))
+#else
+#define INFERD_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  INFERD_OK = 0,
+  INFERD_ERR_INVALID_ARGUMENT = 1, /* shape / argument error (Python: ValueError)          */
+  INFERD_ERR_UNSUPPORTED = 2,      /* combination of dtype / sizes not built                 */
+  INFERD_ERR_WORKSPACE = 3,        /* workspace missing, misaligned or too small             */
+  INFERD_ERR_CUDA = 4,             /* launch or runtime failure                              */
+  INFERD_ERR_DEVICE_INDEX = 5,     /* device side: block id / slot outside the pool (IndexError) */
+  INFERD_ERR_DEVICE_TIMEOUT = 6    /* device side: a bounded wait expired                    */
+} inferd_status_t;
+
+typedef enum {
+  INFERD_F32 = 0,
+  INFERD_F16 = 1,
+  INFERD_BF16 = 2,
+  INFERD_E4M3 = 3
+} inferd_dtype_t;
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+INFERD_API int inferd_version(void);
+
+/* Static description of a status code. */
+INFERD_API const char* inferd_status_string(int status);
+
+/* Last CUDA error string recorded by a failing call on this thread ("" if none). */
+INFERD_API const char* inferd_last_cuda_error(void);
+
+/*
+ * reshape_and_cache: write num_tokens new K/V rows into their pool slots.
+ * Replaces the write loop of PagedKVCache.append_tokens, core/paged_cache.py:177-183
+ * (key_cache[layer][block, :, offset, :] = layer_keys[layer][rel_pos]); the page-table
+ * bookkeeping of :164-176,184-189 stays on the host.  key/value element (t, h, d) is at
+ * key[t * key_token_stride + h * key_head_stride + d] (strides in elements).
+ * Bit-exact copy for every dtype.
+ */
+INFERD_API int inferd_reshape_and_cache(const void* key, const void* value,
+                             int64_t key_token_stride, int64_t key_head_stride,
+                             int64_t value_token_stride, int64_t value_head_stride,
+                             void* key_cache, void* value_cache,
+                             const int64_t* slot_mapping, int64_t num_tokens,
+                             int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                             int64_t num_blocks, int32_t dtype,
+                             int32_t* error_word, void* stream);
+
+/*
+ * gather_paged_kv: copy one sequence's pages back to contiguous [seq_len, num_kv_heads,
+ * head_dim] tensors.  Replaces core/paged_attn.py:20-61 (gather_paged_kv) and
+ * core/paged_cache.py:191-205 (PagedKVCache.gather_layer).  Bit-exact.
+ * block_table_bytes is 4 (int32) or 8 (int64).
+ */
+INFERD_API int inferd_gather_paged_kv(void* key_out, void* value_out,
+                           const void* key_cache, const void* value_cache,
+                           const void* block_table, int32_t block_table_bytes,
+                           int64_t seq_len, int32_t num_kv_heads, int32_t head_dim,
+                           int32_t block_size, int64_t num_blocks, int32_t dtype,
+                           int32_t* error_word, void* stream);
+
+/*
+ * Paged attention over the block-table pool, batched over sequences.
+ *   q_len == 1 : decode attention, replaces core/paged_attn.py:147-167 paged_attention
+ *                (-> paged_attention_reference :134-144 -> gather :20-61 + dense :64-106).
+ *   q_len  > 1 : causal multi-query verify attention of speculative decoding, replacing the
+ *                target verify forward core/spec_decode.py:135 (HF eager attention over
+ *                contiguous KV).  Query i of sequence b sits at absolute position
+ *                context_lens[b] - q_len + i and sees keys 0 .. that position; the q_len
+ *                window's own K/V must already be in the pool (reshape_and_cache first).
+ * GQA: query head hq reads kv head hq / (num_q_heads / num_kv_heads), the
+ * repeat_interleave order of core/paged_attn.py:99-100.
+ * context_lens: [num_seqs] int32 on the device, or NULL for "every sequence has
+ * max_context_len keys".  max_context_len is a host-side upper bound used for grid sizing.
+ * A sequence with no visible keys gets an all-zero output row (softmax over nothing).
+ * workspace: >= inferd_paged_attention_workspace_bytes(...) bytes, 256-byte aligned; its
+ * first inferd_paged_attention_counter_bytes(...) bytes must be zero before the first
+ * call and are left zero by every completed call.  Calls that share a workspace must be
+ * ordered on one stream.
+ */
+INFERD_API int inferd_paged_attention(void* out, const void* query,
+                           const void* key_cache, const void* value_cache,
+                           const void* block_tables, int32_t block_table_bytes,
+                           int64_t block_table_stride, const int32_t* context_lens,
+                           int32_t num_seqs, int32_t q_len, int32_t num_q_heads,
+                           int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                           int64_t num_blocks, int32_t max_context_len, float scale,
+                           int32_t dtype, void* workspace, size_t workspace_bytes,
+                           int32_t* error_word, void* stream);
+
+INFERD_API size_t inferd_paged_attention_workspace_bytes(int32_t num_seqs, int32_t q_len,
+                                              int32_t num_q_heads, int32_t num_kv_heads,
+                                              int32_t head_dim, int32_t device);
+
+INFERD_API size_t inferd_paged_attention_counter_bytes(int32_t num_seqs, int32_t num_kv_heads);
+
+/*
+ * Dense (contiguous) attention: query [q_len, num_q_heads, head_dim] against key/value
+ * [seq_len, num_kv_heads, head_dim].  q_len == 1 is core/paged_attn.py:64-106
+ * dense_attention (no mask); q_len > 1 applies the same causal rule as
+ * inferd_paged_attention.  Accumulates in fp32.
+ */
+INFERD_API int inferd_dense_attention(void* out, const void* query, const void* key, const void* value,
+                           int64_t seq_len, int32_t q_len, int32_t num_q_heads,
+                           int32_t num_kv_heads, int32_t head_dim, float scale, int32_t dtype,
+                           void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INFERD_B200_H */

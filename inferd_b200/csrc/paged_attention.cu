@@ -1,0 +1,970 @@
+// paged_attention.cu -- paged GQA attention over the block-table KV pool.
+//
+// Fast path (bf16/f16, head_dim 128, block_size 16, q_len * group <= 32):
+//   A persistent, page-balanced kernel.  The (sequence, kv-head) page lists are laid end
+//   to end into one global page axis of T = num_kv_heads * sum_b ceil(L_b / 16) pages,
+//   and CTA c of G streams pages [c*T/G, (c+1)*T/G), so every CTA moves the same number
+//   of bytes however uneven the context lengths are.  A CTA range that cuts a
+//   (sequence, kv-head) segment produces a partial (m, l, O) for it; the CTA that
+//   finishes a segment last (atomic ticket, no spinning) merges the partials.
+//
+//   Per CTA: one producer warp streams 4 KiB K and V pages into an 8-stage shared-memory
+//   ring with TMA 2-D tiled loads (128-byte swizzle, evict-first), four consumer warps
+//   each own every fourth page: S = K Q^T and O^T += V^T P^T on mma.sync m16n8k16 with
+//   fp32 accumulators, online softmax in base 2 with warp-shuffle row maxima, and the
+//   P fragment moved from accumulator to operand layout with movmatrix.  All q-rows that
+//   share a kv head (group heads x q_len queries) ride in the MMA's N dimension, so each
+//   K/V byte is read from HBM once.
+//
+// Generic path (fp32 and any other size): one CTA per (sequence, query row), fp32 CUDA
+// core arithmetic.  Used for fp32 pools and small head dims such as the reference's
+// own unit tests; it is not tuned.
+//
+// Numerics follow core/paged_attn.py:64-106 (GQA through repeat_interleave order,
+// default scale 1/sqrt(head_dim), fp32 softmax, probabilities rounded to the working
+// dtype before P.V) except that Q.K is accumulated in fp32 rather than rounded to the
+// working dtype.
+#include <type_traits>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "runtime.cuh"
+
+namespace inferd {
+namespace {
+
+constexpr int kHeadDim = 128;
+constexpr int kPage = 16;                    // tokens per KV block
+constexpr int kHalfBytes = 2048;             // one TMA box: 16 rows x 64 elements x 2 B
+constexpr int kStageBytes = 4 * kHalfBytes;  // K lo/hi, V lo/hi halves of one page
+constexpr int kQRowBytes = 272;              // 256 B + 16 B pad: conflict-free ldmatrix
+constexpr int kConsumerWarps = 4;
+constexpr int kStages = 8;  // multiple of kConsumerWarps: stage s is owned by warp s % 4
+constexpr int kCtasPerSm = 2;
+constexpr int kMaxSeqsFast = 4096;
+constexpr int kMaxRowsFast = 32;  // q_len * group rows per (sequence, kv head)
+constexpr float kLog2e = 1.4426950408889634f;
+
+static_assert(kStages % kConsumerWarps == 0, "stage ownership needs kStages % warps == 0");
+
+struct FastParams {
+  void* out;
+  const void* query;
+  const void* block_tables;
+  int64_t bt_stride;
+  int32_t bt_bytes;
+  const int32_t* context_lens;
+  int32_t max_context_len;
+  int32_t num_seqs, q_len, num_q_heads, num_kv_heads, group, nq;
+  int64_t num_blocks;
+  float scale_log2;
+  int32_t* counters;
+  float* part_ml;
+  float* part_o;
+  int32_t* error_word;
+};
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+// Context length of sequence b, clamped to what its block-table row can address.
+__device__ __forceinline__ int seq_len_of(const FastParams& p, int b, bool report) {
+  int L = p.context_lens != nullptr ? __ldg(p.context_lens + b) : p.max_context_len;
+  if (L < 0) L = 0;
+  const int64_t cap = p.bt_stride * kPage;
+  if (L > cap) {
+    if (report) report_error(p.error_word, INFERD_ERR_DEVICE_INDEX);
+    L = static_cast<int>(cap);
+  }
+  return L;
+}
+
+__device__ __forceinline__ int64_t block_id(const FastParams& p, int b, int page) {
+  const int64_t i = static_cast<int64_t>(b) * p.bt_stride + page;
+  return p.bt_bytes == 8 ? __ldg(static_cast<const int64_t*>(p.block_tables) + i)
+                         : static_cast<int64_t>(__ldg(static_cast<const int32_t*>(p.block_tables) + i));
+}
+
+// Largest b in [0, B) with prefix[b] <= q.
+__device__ __forceinline__ int find_seq(const int* prefix, int B, int64_t q) {
+  int lo = 0, hi = B - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= q) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// CTA whose balanced range [c*T/G, (c+1)*T/G) contains global page g.
+__device__ __forceinline__ int cta_of(int64_t g, int64_t T, int G) {
+  int64_t c = ((g + 1) * G + T - 1) / T - 1;
+  if (c < 0) c = 0;
+  if (c > G - 1) c = G - 1;
+  return static_cast<int>(c);
+}
+
+template <bool kBf16, int NT>
+__global__ void __launch_bounds__((kConsumerWarps + 1) * 32, kCtasPerSm)
+    paged_attn_tc_kernel(const __grid_constant__ CUtensorMap kmap,
+                         const __grid_constant__ CUtensorMap vmap, const FastParams p) {
+  using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
+  constexpr int NQP = NT * 8;
+  constexpr int kThreads = (kConsumerWarps + 1) * 32;
+  constexpr int kConsumerThreads = kConsumerWarps * 32;
+  constexpr bool kQInRegs = NT <= 2;
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int warp_tot[kConsumerWarps + 1];
+  __shared__ int flags[4];  // [0] abort, [1] last-ticket
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* stages = smem;
+  uint8_t* qtile = stages + kStages * kStageBytes;
+  float* merge = reinterpret_cast<float*>(qtile + NQP * kQRowBytes);  // [NQP][128]
+  float* ml = merge + NQP * kHeadDim;                                 // [warps][NQP][2]
+  float* colstat = ml + kConsumerWarps * NQP * 2;                     // [NQP][2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(colstat + NQP * 2);
+  uint64_t* empty = full + kStages;
+  int* prefix = reinterpret_cast<int*>(empty + kStages);  // [B + 1]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int B = p.num_seqs, Hkv = p.num_kv_heads;
+
+  // ---- pages per sequence, exclusive prefix over sequences (block scan)
+  {
+    const int chunk = (B + kThreads - 1) / kThreads;
+    const int b0 = min(B, tid * chunk), b1 = min(B, b0 + chunk);
+    int local = 0;
+    for (int b = b0; b < b1; ++b) local += (seq_len_of(p, b, true) + kPage - 1) / kPage;
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    if (tid == 0) { flags[0] = 0; flags[1] = 0; }
+    __syncthreads();
+    int run = incl - local;
+    int total = 0;
+    for (int w = 0; w <= kConsumerWarps; ++w) {
+      if (w < warp) run += warp_tot[w];
+      total += warp_tot[w];
+    }
+    for (int b = b0; b < b1; ++b) {
+      prefix[b] = run;
+      run += (seq_len_of(p, b, false) + kPage - 1) / kPage;
+    }
+    if (tid == 0) prefix[B] = total;
+    __syncthreads();
+  }
+
+  const int64_t T_pages = static_cast<int64_t>(Hkv) * prefix[B];
+  const int G = static_cast<int>(min64(static_cast<int64_t>(gridDim.x), max64(T_pages, 1)));
+  if (static_cast<int>(blockIdx.x) >= G) return;
+
+  // Sequences without keys: softmax over an empty set -> zero output rows.
+  for (int b = blockIdx.x; b < B; b += G) {
+    if (prefix[b + 1] != prefix[b]) continue;
+    const int64_t n16 = static_cast<int64_t>(p.q_len) * p.num_q_heads * kHeadDim / 8;
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out) +
+                                          static_cast<int64_t>(b) * p.q_len * p.num_q_heads * kHeadDim);
+    for (int64_t i = tid; i < n16; i += kThreads) dst[i] = make_uint4(0, 0, 0, 0);
+  }
+  if (T_pages == 0) return;
+
+  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * T_pages / G;
+  const int64_t g1 = static_cast<int64_t>(blockIdx.x + 1) * T_pages / G;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  volatile int* vflags = flags;
+
+  if (warp == kConsumerWarps) {
+    // ======================= producer warp: block ids -> TMA page loads ==============
+    if (lane == 0) {
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+    }
+    const uint64_t policy = l2_policy_evict_first();
+    auto row_of = [&](int64_t g) -> int32_t {
+      const int b = find_seq(prefix, B, g / Hkv);
+      const int pb = prefix[b + 1] - prefix[b];
+      const int64_t off = g - static_cast<int64_t>(Hkv) * prefix[b];
+      const int h = static_cast<int>(off / pb);
+      const int page = static_cast<int>(off - static_cast<int64_t>(h) * pb);
+      int64_t blk = block_id(p, b, page);
+      if (blk < 0 || blk >= p.num_blocks) {
+        report_error(p.error_word, INFERD_ERR_DEVICE_INDEX);
+        blk = 0;
+      }
+      return static_cast<int32_t>((blk * Hkv + h) * kPage);
+    };
+    int64_t issued = 0;
+    bool stop = false;
+    int32_t row_cur = (g0 + lane < g1) ? row_of(g0 + lane) : 0;
+    for (int64_t base = g0; base < g1 && !stop; base += 32) {
+      const int32_t row_next = (base + 32 + lane < g1) ? row_of(base + 32 + lane) : 0;
+      const int n = static_cast<int>(min64(32, g1 - base));
+      for (int j = 0; j < n; ++j) {
+        const int32_t r = __shfl_sync(0xffffffffu, row_cur, j);
+        if (lane == 0 && !stop) {
+          const int64_t local = base + j - g0;
+          const int stage = static_cast<int>(local % kStages);
+          const uint32_t round = static_cast<uint32_t>(local / kStages);
+          if (vflags[0] != 0) {
+            stop = true;
+          } else if (round > 0 && !mbar_wait(&empty[stage], (round - 1) & 1u)) {
+            report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+            vflags[0] = 1;
+            stop = true;
+          } else {
+            uint8_t* st = stages + stage * kStageBytes;
+            mbar_arrive_expect_tx(&full[stage], kStageBytes);
+            tma_load_2d(st, &kmap, 0, r, &full[stage], policy);
+            tma_load_2d(st + kHalfBytes, &kmap, 64, r, &full[stage], policy);
+            tma_load_2d(st + 2 * kHalfBytes, &vmap, 0, r, &full[stage], policy);
+            tma_load_2d(st + 3 * kHalfBytes, &vmap, 64, r, &full[stage], policy);
+            ++issued;
+          }
+        }
+        stop = __shfl_sync(0xffffffffu, stop ? 1 : 0, 0) != 0;
+      }
+      row_cur = row_next;
+    }
+    // Drain: never leave the CTA with a TMA write still in flight into its smem.
+    if (lane == 0) {
+      for (int s = 0; s < kStages; ++s) {
+        if (s >= issued) break;
+        const int64_t rounds = (issued - s + kStages - 1) / kStages;
+        if (!mbar_wait(&full[s], static_cast<uint32_t>((rounds - 1) & 1))) {
+          report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+        }
+      }
+    }
+    return;
+  }
+
+  // ========================== consumer warps ==========================================
+  const int cw = warp;
+  const int mrow = lane & 7, msel = lane >> 3;
+  const uint32_t qbase = smem_u32(qtile);
+  const T* qptr = static_cast<const T*>(p.query);
+  T* optr = static_cast<T*>(p.out);
+
+  int64_t g = g0;
+  while (g < g1) {
+    // ---- locate the (sequence, kv head) segment that page g belongs to
+    const int b = find_seq(prefix, B, g / Hkv);
+    const int pb = prefix[b + 1] - prefix[b];
+    const int64_t seg0 = static_cast<int64_t>(Hkv) * prefix[b];
+    const int h = static_cast<int>((g - seg0) / pb);
+    const int64_t seg_start = seg0 + static_cast<int64_t>(h) * pb;
+    const int64_t seg_end = seg_start + pb;
+    const int64_t piece_end = min64(g1, seg_end);
+    const int L = seq_len_of(p, b, false);
+
+    // ---- stage Q rows of this segment (row c = qi * group + gi) and clear the merge area
+    for (int i = tid; i < NQP * 16; i += kConsumerThreads) {
+      const int c = i >> 4, ch = i & 15;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (c < p.nq) {
+        const int qi = c / p.group, gi = c - qi * p.group;
+        const T* src = qptr + ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads +
+                               h * p.group + gi) * kHeadDim + ch * 8;
+        v = *reinterpret_cast<const uint4*>(src);
+      }
+      *reinterpret_cast<uint4*>(qtile + c * kQRowBytes + ch * 16) = v;
+    }
+    for (int i = tid; i < NQP * kHeadDim; i += kConsumerThreads) merge[i] = 0.f;
+    named_barrier_sync(1, kConsumerThreads);
+
+    // Last key position each of this thread's columns may see (-1 for padding columns).
+    int lim[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int c = nt * 8 + 2 * (lane & 3) + j;
+        lim[nt][j] = c < p.nq ? L - p.q_len + c / p.group : -1;
+      }
+
+    uint32_t qf[kQInRegs ? 8 : 1][kQInRegs ? NT : 1][2];
+    if constexpr (kQInRegs) {
+#pragma unroll
+      for (int kk = 0; kk < 8; kk += 2)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          uint32_t r4[4];
+          const int n = nt * 8 + mrow;
+          const int d = (kk + (msel >> 1)) * 16 + (msel & 1) * 8;
+          ldmatrix_x4(r4, qbase + n * kQRowBytes + d * 2);
+          qf[kk][nt][0] = r4[0];
+          qf[kk][nt][1] = r4[1];
+          qf[kk + 1][nt][0] = r4[2];
+          qf[kk + 1][nt][1] = r4[3];
+        }
+    }
+
+    float m[NT][2], l[NT][2], o[8][NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      m[nt][0] = m[nt][1] = -INFINITY;
+      l[nt][0] = l[nt][1] = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.f;
+    }
+
+    // ---- this warp's pages of the piece: local index (gg - g0) % 4 == cw
+    const int64_t first = g + ((cw - (g - g0) % kConsumerWarps) + kConsumerWarps) % kConsumerWarps;
+    for (int64_t gg = first; gg < piece_end; gg += kConsumerWarps) {
+      const int64_t local = gg - g0;
+      const int stage = static_cast<int>(local % kStages);
+      const uint32_t round = static_cast<uint32_t>(local / kStages);
+      bool ok = vflags[0] == 0;
+      if (ok && !mbar_wait(&full[stage], round & 1u)) {
+        if (lane == 0) {
+          report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+          vflags[0] = 1;
+        }
+        ok = false;
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (ok) {
+        const uint32_t kbase = smem_u32(stages + stage * kStageBytes);
+        const uint32_t vbase = kbase + 2 * kHalfBytes;
+        const int tok0 = static_cast<int>(gg - seg_start) * kPage;
+
+        // S[token][col] = K Q^T (fp32)
+        float s[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const int tok = ((msel & 1) << 3) + mrow;
+          const int ch = ((kk & 3) << 1) + (msel >> 1);
+          uint32_t a[4];
+          ldmatrix_x4(a, kbase + (kk >> 2) * kHalfBytes + tok * 128 + ((ch ^ (tok & 7)) << 4));
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            uint32_t b0, b1;
+            if constexpr (kQInRegs) {
+              b0 = qf[kk][nt][0];
+              b1 = qf[kk][nt][1];
+            } else {
+              uint32_t r2[2];
+              const int n = nt * 8 + mrow;
+              const int d = kk * 16 + (msel & 1) * 8;
+              ldmatrix_x2(r2, qbase + n * kQRowBytes + d * 2);
+              b0 = r2[0];
+              b1 = r2[1];
+            }
+            mma_16816<kBf16>(s[nt], a, b0, b1);
+          }
+        }
+
+        // scale to base 2, causal / length mask
+        const bool need_mask = tok0 + kPage - 1 > L - p.q_len;
+        const int t_lo = tok0 + (lane >> 2);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float v = s[nt][e] * p.scale_log2;
+            if (need_mask) {
+              const int t = t_lo + ((e >> 1) << 3);
+              if (t > lim[nt][e & 1]) v = -INFINITY;
+            }
+            s[nt][e] = v;
+          }
+
+        // online softmax: column max over the 16 tokens (lanes sharing lane & 3)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            float mx = fmaxf(s[nt][j], s[nt][j + 2]);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mnew = fmaxf(m[nt][j], mx);
+            const float mref = mnew == -INFINITY ? 0.f : mnew;
+            const float alpha = ex2(m[nt][j] - mref);
+            m[nt][j] = mnew;
+            const float p0 = ex2(s[nt][j] - mref), p1 = ex2(s[nt][j + 2] - mref);
+            s[nt][j] = p0;
+            s[nt][j + 2] = p1;
+            l[nt][j] = l[nt][j] * alpha + p0 + p1;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+              o[mt][nt][j] *= alpha;
+              o[mt][nt][j + 2] *= alpha;
+            }
+          }
+
+        // P^T fragments (tokens x cols) in the working dtype
+        uint32_t pf[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          pf[nt][0] = movmatrix_trans(pack2<kBf16>(s[nt][0], s[nt][1]));
+          pf[nt][1] = movmatrix_trans(pack2<kBf16>(s[nt][2], s[nt][3]));
+        }
+
+        // O^T[d][col] += V^T P^T ; rows of V past the sequence end hold stale pool bytes
+        const bool vmask = tok0 + kPage > L;
+        const int ta = tok0 + 2 * (lane & 3);
+        const uint32_t m01 = (ta < L ? 0x0000ffffu : 0u) | (ta + 1 < L ? 0xffff0000u : 0u);
+        const uint32_t m23 = (ta + 8 < L ? 0x0000ffffu : 0u) | (ta + 9 < L ? 0xffff0000u : 0u);
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int tok = ((msel >> 1) << 3) + mrow;
+          const int ch = ((mt & 3) << 1) + (msel & 1);
+          uint32_t a[4];
+          ldmatrix_x4_trans(a, vbase + (mt >> 2) * kHalfBytes + tok * 128 + ((ch ^ (tok & 7)) << 4));
+          if (vmask) {
+            a[0] &= m01;
+            a[1] &= m01;
+            a[2] &= m23;
+            a[3] &= m23;
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma_16816<kBf16>(o[mt][nt], a, pf[nt][0], pf[nt][1]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+    }
+
+    // ---- merge the four warps' (m, l, O) for this piece
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float v = l[nt][j];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        l[nt][j] = v;
+        if (lane < 4) {
+          const int c = nt * 8 + 2 * lane + j;
+          ml[(cw * NQP + c) * 2 + 0] = m[nt][j];
+          ml[(cw * NQP + c) * 2 + 1] = v;
+        }
+      }
+    named_barrier_sync(1, kConsumerThreads);
+    if (tid < NQP) {
+      float M = -INFINITY;
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml[(w * NQP + tid) * 2]);
+      const float Mref = M == -INFINITY ? 0.f : M;
+      float Ls = 0.f;
+      for (int w = 0; w < kConsumerWarps; ++w)
+        Ls += ml[(w * NQP + tid) * 2 + 1] * ex2(ml[(w * NQP + tid) * 2] - Mref);
+      colstat[tid * 2 + 0] = M;
+      colstat[tid * 2 + 1] = Ls;
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int c = nt * 8 + 2 * (lane & 3) + j;
+        float M = -INFINITY;
+        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml[(w * NQP + c) * 2]);
+        const float f = ex2(m[nt][j] - (M == -INFINITY ? 0.f : M));
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int d = mt * 16 + (lane >> 2);
+          atomicAdd(&merge[c * kHeadDim + d], o[mt][nt][j] * f);
+          atomicAdd(&merge[c * kHeadDim + d + 8], o[mt][nt][j + 2] * f);
+        }
+      }
+    named_barrier_sync(1, kConsumerThreads);
+
+    const int c_first = cta_of(seg_start, T_pages, G);
+    const int c_last = cta_of(seg_end - 1, T_pages, G);
+    const int seg_id = b * Hkv + h;
+    if (c_first == c_last) {
+      // whole segment inside this CTA: normalise and store
+      for (int i = tid; i < p.nq * 16; i += kConsumerThreads) {
+        const int c = i >> 4, ch = i & 15;
+        const float Ls = colstat[c * 2 + 1];
+        const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+        const float* src = merge + c * kHeadDim + ch * 8;
+        uint4 v;
+        v.x = pack2<kBf16>(src[0] * inv, src[1] * inv);
+        v.y = pack2<kBf16>(src[2] * inv, src[3] * inv);
+        v.z = pack2<kBf16>(src[4] * inv, src[5] * inv);
+        v.w = pack2<kBf16>(src[6] * inv, src[7] * inv);
+        const int qi = c / p.group, gi = c - qi * p.group;
+        T* dst = optr + ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) *
+                            kHeadDim + ch * 8;
+        *reinterpret_cast<uint4*>(dst) = v;
+      }
+    } else {
+      // partial for a segment shared with other CTAs: publish, take a ticket
+      const int64_t slot = static_cast<int64_t>(blockIdx.x) + seg_id;
+      float* po = p.part_o + slot * NQP * kHeadDim;
+      for (int i = tid; i < p.nq * kHeadDim / 4; i += kConsumerThreads)
+        reinterpret_cast<float4*>(po)[i] = reinterpret_cast<const float4*>(merge)[i];
+      if (tid < p.nq) {
+        p.part_ml[(slot * NQP + tid) * 2 + 0] = colstat[tid * 2 + 0];
+        p.part_ml[(slot * NQP + tid) * 2 + 1] = colstat[tid * 2 + 1];
+      }
+      __threadfence();
+      named_barrier_sync(1, kConsumerThreads);
+      if (tid == 0) {
+        const int prev = atomicAdd(p.counters + seg_id, 1);
+        vflags[1] = (prev == c_last - c_first) ? 1 : 0;
+      }
+      named_barrier_sync(1, kConsumerThreads);
+      if (vflags[1] != 0) {
+        __threadfence();
+        for (int i = tid; i < p.nq * kHeadDim; i += kConsumerThreads) {
+          const int c = i / kHeadDim, d = i - c * kHeadDim;
+          float M = -INFINITY;
+          for (int cc = c_first; cc <= c_last; ++cc)
+            M = fmaxf(M, __ldcg(p.part_ml + ((static_cast<int64_t>(cc) + seg_id) * NQP + c) * 2));
+          const float Mref = M == -INFINITY ? 0.f : M;
+          float Ls = 0.f, acc = 0.f;
+          for (int cc = c_first; cc <= c_last; ++cc) {
+            const int64_t sl = static_cast<int64_t>(cc) + seg_id;
+            const float f = ex2(__ldcg(p.part_ml + (sl * NQP + c) * 2) - Mref);
+            Ls += __ldcg(p.part_ml + (sl * NQP + c) * 2 + 1) * f;
+            acc += __ldcg(p.part_o + (sl * NQP + c) * kHeadDim + d) * f;
+          }
+          const int qi = c / p.group, gi = c - qi * p.group;
+          optr[((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) *
+                   kHeadDim + d] = from_f32<T>(Ls > 0.f ? acc / Ls : 0.f);
+        }
+        if (tid == 0) p.counters[seg_id] = 0;
+      }
+    }
+    named_barrier_sync(1, kConsumerThreads);
+    g = piece_end;
+  }
+}
+
+// ------------------------------------------------------------------ generic path
+struct GenericParams {
+  void* out;
+  const void* query;
+  const void* key;    // pool base (or contiguous K)
+  const void* value;  // pool base (or contiguous V)
+  int64_t s_blk, s_head, s_tok;  // element strides of block, kv head, token-in-block
+  int32_t block_size;
+  const void* block_tables;  // nullptr: block index = token / block_size (contiguous K/V)
+  int32_t bt_bytes;
+  int64_t bt_stride;
+  const int32_t* context_lens;
+  int32_t max_context_len;
+  int32_t q_len, num_q_heads, num_kv_heads, head_dim;
+  int64_t num_blocks;
+  float scale;
+  int32_t* error_word;
+};
+
+constexpr int kGenThreads = 128;
+constexpr int kGenMaxDim = 512;
+
+// One CTA per (query row, sequence): fp32 online softmax over the visible keys.
+template <typename T>
+__global__ void __launch_bounds__(kGenThreads) attn_generic_kernel(const GenericParams p) {
+  __shared__ float qs[kGenMaxDim];
+  __shared__ float ps[kGenThreads];
+  __shared__ int64_t rowoff[kGenThreads];
+  __shared__ float red[kGenThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r = blockIdx.x;  // qi * Hq + hq
+  const int b = blockIdx.y;
+  const int qi = r / p.num_q_heads, hq = r - qi * p.num_q_heads;
+  const int group = p.num_q_heads / p.num_kv_heads;
+  const int h = hq / group;
+  const int D = p.head_dim;
+
+  int64_t L = p.context_lens != nullptr ? p.context_lens[b] : p.max_context_len;
+  if (L < 0) L = 0;
+  if (p.block_tables != nullptr && L > p.bt_stride * p.block_size) {
+    if (tid == 0) report_error(p.error_word, INFERD_ERR_DEVICE_INDEX);
+    L = p.bt_stride * p.block_size;
+  }
+  const int64_t limit = L - p.q_len + qi;  // last visible key position
+  const int64_t nvis = limit + 1 < L ? (limit + 1 > 0 ? limit + 1 : 0) : L;
+
+  const T* q = static_cast<const T*>(p.query) + ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + hq) * D;
+  for (int d = tid; d < D; d += kGenThreads) qs[d] = to_f32<T>(q[d]) * p.scale;
+  __syncthreads();
+
+  const T* K = static_cast<const T*>(p.key);
+  const T* V = static_cast<const T*>(p.value);
+  float acc[kGenMaxDim / kGenThreads];
+#pragma unroll
+  for (int i = 0; i < kGenMaxDim / kGenThreads; ++i) acc[i] = 0.f;
+  float m = -INFINITY, lsum = 0.f;
+
+  for (int64_t t0 = 0; t0 < nvis; t0 += kGenThreads) {
+    const int64_t t = t0 + tid;
+    float s = -INFINITY;
+    int64_t off = -1;
+    if (t < nvis) {
+      const int64_t page = t / p.block_size;
+      const int64_t in = t - page * p.block_size;
+      int64_t blk = page;
+      if (p.block_tables != nullptr) {
+        const int64_t i = static_cast<int64_t>(b) * p.bt_stride + page;
+        blk = p.bt_bytes == 8 ? static_cast<const int64_t*>(p.block_tables)[i]
+                              : static_cast<int64_t>(static_cast<const int32_t*>(p.block_tables)[i]);
+      }
+      if (blk < 0 || blk >= p.num_blocks) {
+        report_error(p.error_word, INFERD_ERR_DEVICE_INDEX);
+      } else {
+        off = blk * p.s_blk + h * p.s_head + in * p.s_tok;
+        float acc_s = 0.f;
+        for (int d = 0; d < D; ++d) acc_s += qs[d] * to_f32<T>(K[off + d]);
+        s = acc_s;
+      }
+    }
+    rowoff[tid] = off;
+    // block max
+    float mx = s;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int w = 1; w < kGenThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+    const float mnew = fmaxf(m, mx);
+    const float mref = mnew == -INFINITY ? 0.f : mnew;
+    const float alpha = expf(m - mref);
+    const float pv = (off >= 0) ? expf(s - mref) : 0.f;
+    ps[tid] = pv;
+    __syncthreads();  // red reuse + ps visible
+    float sum = pv;
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < kGenThreads / 32; ++w) tot += red[w];
+    lsum = lsum * alpha + tot;
+    m = mnew;
+    const int n = static_cast<int>(min64(kGenThreads, nvis - t0));
+#pragma unroll
+    for (int i = 0; i < kGenMaxDim / kGenThreads; ++i) {
+      const int d = tid + i * kGenThreads;
+      if (d < D) {
+        float a = acc[i] * alpha;
+        for (int j = 0; j < n; ++j) {
+          const int64_t ro = rowoff[j];
+          if (ro >= 0) a += ps[j] * to_f32<T>(V[ro + d]);
+        }
+        acc[i] = a;
+      }
+    }
+    __syncthreads();  // before rowoff / ps / red are overwritten
+  }
+  T* out = static_cast<T*>(p.out) + ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + hq) * D;
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+#pragma unroll
+  for (int i = 0; i < kGenMaxDim / kGenThreads; ++i) {
+    const int d = tid + i * kGenThreads;
+    if (d < D) out[d] = from_f32<T>(acc[i] * inv);
+  }
+}
+
+int launch_generic(const GenericParams& gp, int32_t dtype, int32_t num_seqs, cudaStream_t s) {
+  dim3 grid(gp.q_len * gp.num_q_heads, num_seqs);
+  if (dtype == INFERD_F32) attn_generic_kernel<float><<<grid, kGenThreads, 0, s>>>(gp);
+  else if (dtype == INFERD_F16) attn_generic_kernel<__half><<<grid, kGenThreads, 0, s>>>(gp);
+  else attn_generic_kernel<__nv_bfloat16><<<grid, kGenThreads, 0, s>>>(gp);
+  return launch_status();
+}
+
+// ------------------------------------------------------------------ fast-path host side
+inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+inline int nq_pad(int nq) { return ((nq + 7) / 8) * 8; }
+
+struct WorkspaceLayout {
+  size_t counters, ml, o, total;
+};
+
+inline WorkspaceLayout workspace_layout(int num_seqs, int num_kv_heads, int nqp, int grid) {
+  WorkspaceLayout w;
+  const size_t segs = static_cast<size_t>(num_seqs) * num_kv_heads;
+  const size_t slots = static_cast<size_t>(grid) + segs;
+  w.counters = 0;
+  w.ml = align256(segs * sizeof(int32_t));
+  w.o = w.ml + align256(slots * nqp * 2 * sizeof(float));
+  w.total = w.o + align256(slots * nqp * kHeadDim * sizeof(float));
+  return w;
+}
+
+inline int fast_grid(int sm_count) { return sm_count * kCtasPerSm; }
+
+inline size_t fast_smem_bytes(int nqp, int num_seqs) {
+  return 1024 + static_cast<size_t>(kStages) * kStageBytes + nqp * kQRowBytes +
+         nqp * kHeadDim * 4 + kConsumerWarps * nqp * 2 * 4 + nqp * 2 * 4 + 2 * kStages * 8 +
+         (num_seqs + 1) * 4;
+}
+
+// Tensor map over one pool viewed as [num_blocks * num_kv_heads * 16 rows, 128 elements]
+// with a 64 x 16 box (128 B rows) and 128-byte swizzle.
+struct MapCache {
+  std::mutex mu;
+  struct Entry {
+    const void* ptr;
+    int64_t rows;
+    int dev;
+    CUtensorMap map;
+  } e[16];
+  int n = 0, next = 0;
+};
+MapCache g_maps;
+
+int pool_map(const void* pool, int64_t rows, CUtensorMap* out) {
+  const int dev = current_device();
+  {
+    std::lock_guard<std::mutex> lock(g_maps.mu);
+    for (int i = 0; i < g_maps.n; ++i)
+      if (g_maps.e[i].ptr == pool && g_maps.e[i].rows == rows && g_maps.e[i].dev == dev) {
+        *out = g_maps.e[i].map;
+        return INFERD_OK;
+      }
+  }
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (enc == nullptr) return INFERD_ERR_CUDA;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHeadDim * 2)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kPage)};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMap map;
+  CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(pool), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return INFERD_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_maps.mu);
+  MapCache::Entry& e = g_maps.e[g_maps.next];
+  e.ptr = pool;
+  e.rows = rows;
+  e.dev = dev;
+  e.map = map;
+  g_maps.next = (g_maps.next + 1) % 16;
+  if (g_maps.n < 16) ++g_maps.n;
+  *out = map;
+  return INFERD_OK;
+}
+
+template <bool kBf16, int NT>
+int launch_fast_t(const CUtensorMap& km, const CUtensorMap& vm, const FastParams& fp, int grid,
+                  size_t smem, cudaStream_t s) {
+  static bool configured[64] = {false};
+  const int dev = current_device();
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(paged_attn_tc_kernel<kBf16, NT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return cuda_status(e);
+    configured[dev] = true;
+  }
+  paged_attn_tc_kernel<kBf16, NT><<<grid, (kConsumerWarps + 1) * 32, smem, s>>>(km, vm, fp);
+  return launch_status();
+}
+
+template <bool kBf16>
+int launch_fast(const CUtensorMap& km, const CUtensorMap& vm, const FastParams& fp, int nt,
+                int grid, size_t smem, cudaStream_t s) {
+  switch (nt) {
+    case 1: return launch_fast_t<kBf16, 1>(km, vm, fp, grid, smem, s);
+    case 2: return launch_fast_t<kBf16, 2>(km, vm, fp, grid, smem, s);
+    case 3: return launch_fast_t<kBf16, 3>(km, vm, fp, grid, smem, s);
+    default: return launch_fast_t<kBf16, 4>(km, vm, fp, grid, smem, s);
+  }
+}
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+}  // namespace
+}  // namespace inferd
+
+using namespace inferd;
+
+extern "C" size_t inferd_paged_attention_counter_bytes(int32_t num_seqs, int32_t num_kv_heads) {
+  if (num_seqs <= 0 || num_kv_heads <= 0) return 0;
+  return align256(static_cast<size_t>(num_seqs) * num_kv_heads * sizeof(int32_t));
+}
+
+extern "C" size_t inferd_paged_attention_workspace_bytes(int32_t num_seqs, int32_t q_len,
+                                                         int32_t num_q_heads, int32_t num_kv_heads,
+                                                         int32_t head_dim, int32_t device) {
+  if (num_seqs <= 0 || q_len <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return 0;
+  int sms = 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      sms <= 0) {
+    cudaGetLastError();
+    sms = 148;
+  }
+  const int group = num_q_heads / (num_kv_heads > 0 ? num_kv_heads : 1);
+  const int nqp = nq_pad(q_len * (group > 0 ? group : 1));
+  const int chunk = num_seqs < kMaxSeqsFast ? num_seqs : kMaxSeqsFast;
+  return workspace_layout(chunk, num_kv_heads, nqp, fast_grid(sms)).total;
+}
+
+extern "C" int inferd_paged_attention(void* out, const void* query, const void* key_cache,
+                                      const void* value_cache, const void* block_tables,
+                                      int32_t block_table_bytes, int64_t block_table_stride,
+                                      const int32_t* context_lens, int32_t num_seqs,
+                                      int32_t q_len, int32_t num_q_heads, int32_t num_kv_heads,
+                                      int32_t head_dim, int32_t block_size, int64_t num_blocks,
+                                      int32_t max_context_len, float scale, int32_t dtype,
+                                      void* workspace, size_t workspace_bytes,
+                                      int32_t* error_word, void* stream) {
+  if (num_seqs < 0 || q_len <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
+      block_size <= 0 || num_blocks <= 0 || max_context_len < 0 || block_table_stride < 0)
+    return INFERD_ERR_INVALID_ARGUMENT;
+  if (num_q_heads % num_kv_heads != 0) return INFERD_ERR_INVALID_ARGUMENT;
+  if (block_table_bytes != 4 && block_table_bytes != 8) return INFERD_ERR_INVALID_ARGUMENT;
+  if (dtype != INFERD_F32 && dtype != INFERD_F16 && dtype != INFERD_BF16)
+    return INFERD_ERR_UNSUPPORTED;
+  if (num_seqs == 0) return INFERD_OK;
+  if (!out || !query || !key_cache || !value_cache || !block_tables)
+    return INFERD_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int group = num_q_heads / num_kv_heads;
+  const int nq = q_len * group;
+  const int64_t rows = num_blocks * num_kv_heads * kPage;
+
+  const bool fast = (dtype == INFERD_BF16 || dtype == INFERD_F16) && head_dim == kHeadDim &&
+                    block_size == kPage && nq <= kMaxRowsFast && rows < (int64_t{1} << 31) &&
+                    aligned(key_cache, 16) && aligned(value_cache, 16) && aligned(query, 16) &&
+                    aligned(out, 16);
+  if (!fast) {
+    if (head_dim > kGenMaxDim) return INFERD_ERR_UNSUPPORTED;
+    if (static_cast<int64_t>(q_len) * num_q_heads > 65535 * 1024) return INFERD_ERR_UNSUPPORTED;
+    GenericParams gp;
+    gp.out = out;
+    gp.query = query;
+    gp.key = key_cache;
+    gp.value = value_cache;
+    gp.s_tok = head_dim;
+    gp.s_head = static_cast<int64_t>(block_size) * head_dim;
+    gp.s_blk = static_cast<int64_t>(num_kv_heads) * block_size * head_dim;
+    gp.block_size = block_size;
+    gp.block_tables = block_tables;
+    gp.bt_bytes = block_table_bytes;
+    gp.bt_stride = block_table_stride;
+    gp.context_lens = context_lens;
+    gp.max_context_len = max_context_len;
+    gp.q_len = q_len;
+    gp.num_q_heads = num_q_heads;
+    gp.num_kv_heads = num_kv_heads;
+    gp.head_dim = head_dim;
+    gp.num_blocks = num_blocks;
+    gp.scale = scale;
+    gp.error_word = error_word;
+    // gridDim.y is limited to 65535 sequences per launch
+    for (int32_t b0 = 0; b0 < num_seqs; b0 += 65535) {
+      const int32_t nb = num_seqs - b0 < 65535 ? num_seqs - b0 : 65535;
+      GenericParams g2 = gp;
+      const int es = dtype_bytes(dtype);
+      g2.out = static_cast<uint8_t*>(out) + static_cast<int64_t>(b0) * q_len * num_q_heads * head_dim * es;
+      g2.query = static_cast<const uint8_t*>(query) + static_cast<int64_t>(b0) * q_len * num_q_heads * head_dim * es;
+      g2.block_tables = static_cast<const uint8_t*>(block_tables) + b0 * block_table_stride * block_table_bytes;
+      g2.context_lens = context_lens ? context_lens + b0 : nullptr;
+      const int st = launch_generic(g2, dtype, nb, s);
+      if (st != INFERD_OK) return st;
+    }
+    return INFERD_OK;
+  }
+
+  const int nqp = nq_pad(nq);
+  const int grid = fast_grid(current_sm_count());
+  const int chunk_max = kMaxSeqsFast;
+  const WorkspaceLayout wl = workspace_layout(num_seqs < chunk_max ? num_seqs : chunk_max,
+                                              num_kv_heads, nqp, grid);
+  if (workspace == nullptr || !aligned(workspace, 256) || workspace_bytes < wl.total)
+    return INFERD_ERR_WORKSPACE;
+
+  CUtensorMap km, vm;
+  int st = pool_map(key_cache, rows, &km);
+  if (st != INFERD_OK) return st;
+  st = pool_map(value_cache, rows, &vm);
+  if (st != INFERD_OK) return st;
+
+  const int es = dtype_bytes(dtype);
+  for (int32_t b0 = 0; b0 < num_seqs; b0 += chunk_max) {
+    const int32_t nb = num_seqs - b0 < chunk_max ? num_seqs - b0 : chunk_max;
+    FastParams fp;
+    fp.out = static_cast<uint8_t*>(out) + static_cast<int64_t>(b0) * q_len * num_q_heads * kHeadDim * es;
+    fp.query = static_cast<const uint8_t*>(query) + static_cast<int64_t>(b0) * q_len * num_q_heads * kHeadDim * es;
+    fp.block_tables = static_cast<const uint8_t*>(block_tables) + b0 * block_table_stride * block_table_bytes;
+    fp.bt_stride = block_table_stride;
+    fp.bt_bytes = block_table_bytes;
+    fp.context_lens = context_lens ? context_lens + b0 : nullptr;
+    fp.max_context_len = max_context_len;
+    fp.num_seqs = nb;
+    fp.q_len = q_len;
+    fp.num_q_heads = num_q_heads;
+    fp.num_kv_heads = num_kv_heads;
+    fp.group = group;
+    fp.nq = nq;
+    fp.num_blocks = num_blocks;
+    fp.scale_log2 = scale * kLog2e;
+    fp.counters = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + wl.counters);
+    fp.part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + wl.ml);
+    fp.part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + wl.o);
+    fp.error_word = error_word;
+    // grid: persistent, but no more CTAs than pages can feed (upper bound from the host)
+    const int64_t pages_ub = static_cast<int64_t>(nb) * num_kv_heads *
+                             ((static_cast<int64_t>(max_context_len) + kPage - 1) / kPage);
+    int g = grid;
+    if (pages_ub < g) g = pages_ub > 0 ? static_cast<int>(pages_ub) : 1;
+    const size_t smem = fast_smem_bytes(nqp, nb);
+    st = dtype == INFERD_BF16 ? launch_fast<true>(km, vm, fp, nqp / 8, g, smem, s)
+                              : launch_fast<false>(km, vm, fp, nqp / 8, g, smem, s);
+    if (st != INFERD_OK) return st;
+  }
+  return INFERD_OK;
+}
+
+extern "C" int inferd_dense_attention(void* out, const void* query, const void* key,
+                                      const void* value, int64_t seq_len, int32_t q_len,
+                                      int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                      float scale, int32_t dtype, void* stream) {
+  if (seq_len < 0 || q_len <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return INFERD_ERR_INVALID_ARGUMENT;
+  if (num_q_heads % num_kv_heads != 0) return INFERD_ERR_INVALID_ARGUMENT;
+  if (dtype != INFERD_F32 && dtype != INFERD_F16 && dtype != INFERD_BF16)
+    return INFERD_ERR_UNSUPPORTED;
+  if (head_dim > kGenMaxDim) return INFERD_ERR_UNSUPPORTED;
+  if (seq_len > INT32_MAX) return INFERD_ERR_UNSUPPORTED;
+  if (!out || !query || (seq_len > 0 && (!key || !value))) return INFERD_ERR_INVALID_ARGUMENT;
+  GenericParams gp;
+  gp.out = out;
+  gp.query = query;
+  gp.key = key;
+  gp.value = value;
+  gp.s_tok = static_cast<int64_t>(num_kv_heads) * head_dim;
+  gp.s_head = head_dim;
+  gp.s_blk = 0;
+  gp.block_size = seq_len > 0 ? static_cast<int32_t>(seq_len) : 1;
+  gp.block_tables = nullptr;
+  gp.bt_bytes = 4;
+  gp.bt_stride = 1;
+  gp.context_lens = nullptr;
+  gp.max_context_len = static_cast<int32_t>(seq_len);
+  gp.q_len = q_len;
+  gp.num_q_heads = num_q_heads;
+  gp.num_kv_heads = num_kv_heads;
+  gp.head_dim = head_dim;
+  gp.num_blocks = 1;
+  gp.scale = scale;
+  gp.error_word = nullptr;
+  return launch_generic(gp, dtype, 1, static_cast<cudaStream_t>(stream));
+}

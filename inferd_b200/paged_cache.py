@@ -1,0 +1,451 @@
+"""Paged KV cache: block allocator, page tables and KV pools (drop-in for core/paged_cache.py).
+
+Host bookkeeping (LIFO block allocator, per-sequence page tables, transactional
+allocation with rollback) keeps the reference's exact semantics
+(core/paged_cache.py:27-92,139-252), because callers and tests depend on the block
+reuse order.  Every byte that moves between token tensors and the pools goes through
+the sm_100a kernels: `append_tokens` computes the slot of every new token on the host
+and issues one reshape_and_cache launch per layer (the reference's Python token x layer
+loop of :177-183), and `gather_layer` is one gather launch (:191-205).
+
+Pools are laid out [num_blocks, num_kv_heads, block_size, head_dim] per layer, exactly as
+in the reference, so a pool written here can be read by the reference code and vice
+versa.  Bookkeeping-only use (create/free sequences, page tables) works on any device;
+moving K/V needs the pools on a CUDA device.
+"""
+
+from __future__ import annotations
+
+import copy
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib
+from .paged_attn import gather_paged_kv
+
+
+class BlockAllocator:
+    """LIFO allocator for fixed-size KV blocks (core/paged_cache.py:27-64).
+
+    The free list starts as [num_blocks-1 .. 0], so a fresh allocator hands out
+    0, 1, 2, ...; freed blocks are reused last-freed-first.
+    """
+
+    def __init__(self, num_blocks: int) -> None:
+        if num_blocks <= 0:
+            raise ValueError("num_blocks must be positive")
+        self.num_blocks = num_blocks
+        self._free: list[int] = list(range(num_blocks - 1, -1, -1))
+        self._allocated: set[int] = set()
+
+    @property
+    def free_count(self) -> int:
+        return len(self._free)
+
+    @property
+    def allocated_count(self) -> int:
+        return len(self._allocated)
+
+    def allocate(self, n: int = 1) -> list[int]:
+        if n < 0:
+            raise ValueError("cannot allocate a negative number of blocks")
+        if n > len(self._free):
+            raise MemoryError(f"requested {n} blocks, only {len(self._free)} free")
+        blocks = [self._free.pop() for _ in range(n)]
+        self._allocated.update(blocks)
+        return blocks
+
+    def free(self, blocks: list[int]) -> None:
+        seen: set[int] = set()
+        for block in blocks:
+            if block in seen:
+                raise ValueError(f"duplicate block in free request: {block}")
+            if block not in self._allocated:
+                raise ValueError(f"block is not allocated: {block}")
+            seen.add(block)
+        for block in blocks:
+            self._allocated.remove(block)
+            self._free.append(block)
+
+
+@dataclass
+class SequencePageTable:
+    """Logical -> physical page mapping of one sequence (core/paged_cache.py:67-92)."""
+
+    seq_id: int
+    block_size: int
+    blocks: list[int] = field(default_factory=list)
+    length: int = 0
+
+    @property
+    def block_count(self) -> int:
+        return len(self.blocks)
+
+    @property
+    def capacity_tokens(self) -> int:
+        return len(self.blocks) * self.block_size
+
+    @property
+    def free_slots(self) -> int:
+        return self.capacity_tokens - self.length
+
+    def block_for_pos(self, pos: int) -> tuple[int, int]:
+        if pos < 0 or pos >= self.length:
+            raise IndexError(f"position {pos} outside sequence length {self.length}")
+        page_idx, offset = divmod(pos, self.block_size)
+        return self.blocks[page_idx], offset
+
+    def slots(self, start: int, n: int) -> list[int]:
+        """Pool slots (block * block_size + offset) of positions start .. start+n-1."""
+        bs = self.block_size
+        return [self.blocks[p // bs] * bs + p % bs for p in range(start, start + n)]
+
+
+class PagedKVCache:
+    """Per-layer K/V block pools plus per-sequence page tables (core/paged_cache.py:95-252)."""
+
+    def __init__(
+        self,
+        *,
+        num_layers: int,
+        num_blocks: int,
+        block_size: int = 16,
+        num_kv_heads: int,
+        head_dim: int,
+        dtype: torch.dtype = torch.bfloat16,
+        device: str | torch.device = "cpu",
+    ) -> None:
+        if num_layers <= 0:
+            raise ValueError("num_layers must be positive")
+        if block_size <= 0:
+            raise ValueError("block_size must be positive")
+        if num_kv_heads <= 0 or head_dim <= 0:
+            raise ValueError("num_kv_heads and head_dim must be positive")
+
+        self.num_layers = num_layers
+        self.num_blocks = num_blocks
+        self.block_size = block_size
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        self.dtype = dtype
+        self.device = torch.device(device)
+        self.allocator = BlockAllocator(num_blocks)
+        self.sequences: dict[int, SequencePageTable] = {}
+
+        shape = (num_blocks, num_kv_heads, block_size, head_dim)
+        self.key_cache = [
+            torch.empty(shape, dtype=dtype, device=self.device) for _ in range(num_layers)
+        ]
+        self.value_cache = [
+            torch.empty(shape, dtype=dtype, device=self.device) for _ in range(num_layers)
+        ]
+
+    # ------------------------------------------------------------ bookkeeping
+    def create_sequence(self, seq_id: int) -> SequencePageTable:
+        if seq_id in self.sequences:
+            raise ValueError(f"sequence already exists: {seq_id}")
+        table = SequencePageTable(seq_id=seq_id, block_size=self.block_size)
+        self.sequences[seq_id] = table
+        return table
+
+    def free_sequence(self, seq_id: int) -> None:
+        table = self._table(seq_id)
+        self.allocator.free(table.blocks)
+        del self.sequences[seq_id]
+
+    def _reserve(self, table: SequencePageTable, n_tokens: int) -> list[int]:
+        """Extend a page table to hold n_tokens more tokens (core/paged_cache.py:170-176)."""
+        needed_capacity = table.length + n_tokens
+        needed_blocks = (needed_capacity + self.block_size - 1) // self.block_size
+        extra = needed_blocks - len(table.blocks)
+        new_blocks = self.allocator.allocate(extra) if extra > 0 else []
+        table.blocks.extend(new_blocks)
+        return new_blocks
+
+    def _rollback(self, table: SequencePageTable, new_blocks: list[int]) -> None:
+        if new_blocks:
+            del table.blocks[-len(new_blocks):]
+            self.allocator.free(new_blocks)
+
+    # ------------------------------------------------------------ K/V movement
+    def append_tokens(
+        self,
+        seq_id: int,
+        layer_keys: list[torch.Tensor],
+        layer_values: list[torch.Tensor],
+    ) -> None:
+        """Append one or more logical tokens for every layer (core/paged_cache.py:151-189).
+
+        layer_keys / layer_values hold num_layers tensors [num_tokens, num_kv_heads,
+        head_dim].  The page table is extended before any write, so an allocation
+        failure (MemoryError) leaves the cache unchanged; any later failure frees the
+        blocks this call allocated and re-raises.  The writes are one reshape_and_cache
+        launch per layer, bit-exact.
+        """
+        table = self._table(seq_id)
+        self._validate_layers(layer_keys, layer_values)
+        n_tokens = int(layer_keys[0].shape[0])
+        if n_tokens == 0:
+            return
+        new_blocks = self._reserve(table, n_tokens)
+        try:
+            slots = self._slot_tensor(table.slots(table.length, n_tokens))
+            for layer in range(self.num_layers):
+                self._write(layer, layer_keys[layer], layer_values[layer], slots)
+            table.length += n_tokens
+        except Exception:
+            self._rollback(table, new_blocks)
+            raise
+
+    def append_tokens_batched(
+        self,
+        seq_ids: list[int],
+        layer_keys: list[torch.Tensor],
+        layer_values: list[torch.Tensor],
+    ) -> None:
+        """Append tokens_per_seq tokens to each of several sequences in one launch per layer.
+
+        layer_keys[layer]: [len(seq_ids) * tokens_per_seq, num_kv_heads, head_dim], the
+        tokens of seq_ids[0] first.  Same all-or-nothing allocation as append_tokens.
+        """
+        if not seq_ids:
+            return
+        tables = [self._table(s) for s in seq_ids]
+        if len(set(seq_ids)) != len(seq_ids):
+            raise ValueError("duplicate sequence in batched append")
+        self._validate_layers(layer_keys, layer_values)
+        total = int(layer_keys[0].shape[0])
+        if total % len(seq_ids) != 0:
+            raise ValueError("token count must be a multiple of the number of sequences")
+        per = total // len(seq_ids)
+        if per == 0:
+            return
+        reserved: list[tuple[SequencePageTable, list[int]]] = []
+        try:
+            for t in tables:
+                reserved.append((t, self._reserve(t, per)))
+            slot_list: list[int] = []
+            for t in tables:
+                slot_list.extend(t.slots(t.length, per))
+            slots = self._slot_tensor(slot_list)
+            for layer in range(self.num_layers):
+                self._write(layer, layer_keys[layer], layer_values[layer], slots)
+            for t in tables:
+                t.length += per
+        except Exception:
+            for t, nb in reversed(reserved):
+                self._rollback(t, nb)
+            raise
+
+    def _slot_tensor(self, slots: list[int]) -> torch.Tensor:
+        host = torch.from_numpy(np.asarray(slots, dtype=np.int64))
+        if self.device.type != "cuda":
+            return host
+        return host.pin_memory().to(self.device, non_blocking=True)
+
+    def _write(self, layer: int, keys: torch.Tensor, values: torch.Tensor,
+               slots: torch.Tensor) -> None:
+        kc, vc = self.key_cache[layer], self.value_cache[layer]
+        dev = _lib.require_cuda(kc, vc, keys, values)
+        if keys.dtype != self.dtype or values.dtype != self.dtype:
+            raise ValueError(f"tensor dtype must be the cache dtype {self.dtype}")
+        if keys.stride(2) != 1:
+            keys = keys.contiguous()
+        if values.stride(2) != 1:
+            values = values.contiguous()
+        lib = _lib.load()
+        st = lib.inferd_reshape_and_cache(
+            keys.data_ptr(), values.data_ptr(), keys.stride(0), keys.stride(1),
+            values.stride(0), values.stride(1), kc.data_ptr(), vc.data_ptr(), slots.data_ptr(),
+            slots.numel(), self.num_kv_heads, self.head_dim, self.block_size, self.num_blocks,
+            _lib.dtype_code(self.dtype), _lib.error_word(dev).data_ptr(), _lib.stream_of(dev))
+        _lib.check(st, "reshape_and_cache")
+
+    def gather_layer(self, seq_id: int, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Contiguous K/V [seq_len, num_kv_heads, head_dim] of one layer (one gather launch)."""
+        table = self._table(seq_id)
+        self._check_layer(layer)
+        if table.length == 0:
+            empty = torch.empty((0, self.num_kv_heads, self.head_dim), dtype=self.dtype,
+                                device=self.device)
+            return empty, empty.clone()
+        return gather_paged_kv(self.key_cache[layer], self.value_cache[layer],
+                               self.block_table(seq_id), table.length)
+
+    # ------------------------------------------------------------ tables
+    def block_table(self, seq_id: int, *, device: str | torch.device | None = None) -> torch.Tensor:
+        table = self._table(seq_id)
+        out_device = self.device if device is None else device
+        return torch.tensor(table.blocks, dtype=torch.int64, device=out_device)
+
+    def decode_metadata(
+        self, seq_ids: list[int], *, extra_tokens: int = 0, pad_pages: int | None = None,
+        device: str | torch.device | None = None,
+    ) -> tuple[torch.Tensor, torch.Tensor, int]:
+        """Packed batch metadata for the batched attention kernels.
+
+        Returns (block_tables int32 [B, P], context_lens int32 [B], max_context_len)
+        built from the host page tables and copied to the device in one transfer.
+        extra_tokens is added to every length (for a verify window appended after this
+        call); P defaults to the widest table.
+        """
+        tables = [self._table(s) for s in seq_ids]
+        lens = [t.length + extra_tokens for t in tables]
+        width = max([len(t.blocks) for t in tables] + [1])
+        if pad_pages is not None:
+            if pad_pages < width:
+                raise ValueError("pad_pages is narrower than the widest page table")
+            width = pad_pages
+        host = np.zeros((len(tables), width), dtype=np.int32)
+        for i, t in enumerate(tables):
+            host[i, :len(t.blocks)] = t.blocks
+        packed = torch.from_numpy(np.concatenate(
+            [host.reshape(-1), np.asarray(lens, dtype=np.int32)]))
+        dev = self.device if device is None else torch.device(device)
+        if dev.type == "cuda":
+            packed = packed.pin_memory().to(dev, non_blocking=True)
+        bt = packed[: len(tables) * width].view(len(tables), width)
+        cl = packed[len(tables) * width:]
+        return bt, cl, max(lens + [0])
+
+    def sequence_length(self, seq_id: int) -> int:
+        return self._table(seq_id).length
+
+    def _table(self, seq_id: int) -> SequencePageTable:
+        try:
+            return self.sequences[seq_id]
+        except KeyError:
+            raise KeyError(f"unknown sequence: {seq_id}") from None
+
+    def _check_layer(self, layer: int) -> None:
+        if layer < 0 or layer >= self.num_layers:
+            raise IndexError(f"layer {layer} outside [0, {self.num_layers})")
+
+    def _validate_layers(
+        self, layer_keys: list[torch.Tensor], layer_values: list[torch.Tensor]
+    ) -> None:
+        if len(layer_keys) != self.num_layers or len(layer_values) != self.num_layers:
+            raise ValueError("layer key/value lists must match num_layers")
+        expected_shape = layer_keys[0].shape
+        if len(expected_shape) != 3:
+            raise ValueError("layer tensors must be [tokens, kv_heads, head_dim]")
+        if expected_shape[1:] != (self.num_kv_heads, self.head_dim):
+            raise ValueError(
+                f"expected [tokens, {self.num_kv_heads}, {self.head_dim}], "
+                f"got {tuple(expected_shape)}"
+            )
+        for tensor in [*layer_keys, *layer_values]:
+            if tensor.shape != expected_shape:
+                raise ValueError("all layer tensors must have the same shape")
+            if tensor.device != self.device:
+                raise ValueError(f"tensor device {tensor.device} != cache device {self.device}")
+
+    def assert_consistent(self) -> None:
+        owned = [block for table in self.sequences.values() for block in table.blocks]
+        if len(owned) != len(set(owned)):
+            raise AssertionError("a physical block is owned by multiple sequences")
+        if len(owned) != self.allocator.allocated_count:
+            raise AssertionError("allocator/table allocation counts disagree")
+        for block in owned:
+            if block < 0 or block >= self.num_blocks:
+                raise AssertionError(f"invalid block id: {block}")
+
+
+@dataclass
+class PagedHybridCache:
+    """Paged form of Qwen3.5's hybrid cache (core/paged_cache.py:255-363).
+
+    Full-attention K/V live in `attention` (a PagedKVCache); the linear-attention conv /
+    recurrent states are fixed-size tensors and are carried as clones.
+    """
+
+    attention: PagedKVCache
+    layer_to_cache: dict[int, int]
+    conv_states: list[torch.Tensor | None]
+    recurrent_states: list[torch.Tensor | None]
+    layer_types: list[str] | None
+    transformer_layers: list[int]
+    seq_id: int = 0
+
+    @classmethod
+    def from_qwen_cache(cls, kv, *, block_size: int = 16, seq_id: int = 0) -> "PagedHybridCache":
+        """Convert a batch=1 Qwen3.5 dynamic cache into paged attention blocks."""
+        transformer_layers = list(getattr(kv, "transformer_layers", []))
+        if not transformer_layers:
+            transformer_layers = [
+                i for i, k in enumerate(kv.key_cache)
+                if k is not None and k.ndim == 4 and k.shape[-2] > 0
+            ]
+        if not transformer_layers:
+            raise ValueError("cache contains no full-attention layers")
+
+        first = kv.key_cache[transformer_layers[0]]
+        if first.shape[0] != 1:
+            raise ValueError("PagedHybridCache currently supports batch=1 caches only")
+        _, num_kv_heads, seq_len, head_dim = first.shape
+        num_blocks = (seq_len + block_size - 1) // block_size
+        attention = PagedKVCache(
+            num_layers=len(transformer_layers),
+            num_blocks=max(num_blocks, 1),
+            block_size=block_size,
+            num_kv_heads=num_kv_heads,
+            head_dim=head_dim,
+            dtype=first.dtype,
+            device=first.device,
+        )
+        attention.create_sequence(seq_id)
+
+        layer_keys, layer_values, layer_to_cache = [], [], {}
+        for cache_layer, original_layer in enumerate(transformer_layers):
+            key = kv.key_cache[original_layer]
+            value = kv.value_cache[original_layer]
+            if key is None or value is None:
+                raise ValueError(f"missing key/value cache for layer {original_layer}")
+            if key.shape != value.shape:
+                raise ValueError(f"key/value shape mismatch at layer {original_layer}")
+            if key.shape[0] != 1:
+                raise ValueError("PagedHybridCache currently supports batch=1 caches only")
+            if key.shape[1:] != (num_kv_heads, seq_len, head_dim):
+                raise ValueError("all attention layers must share KV shape")
+            layer_to_cache[original_layer] = cache_layer
+            # [1, heads, seq, dim] -> [seq, heads, dim] as a strided view: the append
+            # kernel takes token / head strides, so no transposed copy is made.
+            layer_keys.append(key[0].transpose(0, 1))
+            layer_values.append(value[0].transpose(0, 1))
+        attention.append_tokens(seq_id, layer_keys, layer_values)
+
+        return cls(
+            attention=attention,
+            layer_to_cache=layer_to_cache,
+            conv_states=_clone_optional_tensors(kv.conv_states),
+            recurrent_states=_clone_optional_tensors(kv.recurrent_states),
+            layer_types=list(getattr(kv, "layer_types", [])) or None,
+            transformer_layers=transformer_layers,
+            seq_id=seq_id,
+        )
+
+    def to_qwen_cache_like(self, template):
+        """Rebuild an HF-style cache with the same class/attributes as `template`."""
+        out = copy.copy(template)
+        out.conv_states = _clone_optional_tensors(self.conv_states)
+        out.recurrent_states = _clone_optional_tensors(self.recurrent_states)
+        out.key_cache = [None for _ in template.key_cache]
+        out.value_cache = [None for _ in template.value_cache]
+        if hasattr(template, "layer_types"):
+            out.layer_types = list(template.layer_types)
+        if hasattr(template, "transformer_layers"):
+            out.transformer_layers = list(template.transformer_layers)
+        if hasattr(template, "last_linear_layer"):
+            out.last_linear_layer = template.last_linear_layer
+
+        for original_layer, cache_layer in self.layer_to_cache.items():
+            key, value = self.attention.gather_layer(self.seq_id, cache_layer)
+            out.key_cache[original_layer] = key.transpose(0, 1).unsqueeze(0).contiguous()
+            out.value_cache[original_layer] = value.transpose(0, 1).unsqueeze(0).contiguous()
+        return out
+
+
+def _clone_optional_tensors(items):
+    return [item.clone() if item is not None else None for item in items]

@@ -1,0 +1,179 @@
+"""Host-side logic of inferd_b200 on CPU: allocator, page tables, validation, rollback.
+
+The allocator and page-table semantics are pinned to a trace recorded from the
+reference's PagedKVCache (tests/golden/cache_trace.json, made by
+tests/golden/make_golden.py).  K/V writes are replaced by a recording stub here; the
+kernels themselves are covered by the gpu-marked tests.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from inferd_b200.paged_cache import BlockAllocator, PagedKVCache, SequencePageTable
+
+
+class RecordingCache(PagedKVCache):
+    """PagedKVCache whose K/V writes are recorded instead of launched."""
+
+    def __init__(self, *a, fail_write=False, **k):
+        super().__init__(*a, **k)
+        self.writes = []
+        self.fail_write = fail_write
+
+    def _write(self, layer, keys, values, slots):
+        if self.fail_write:
+            raise RuntimeError("injected write failure")
+        self.writes.append((layer, slots.tolist()))
+
+
+def test_allocator_lifo_and_errors():
+    a = BlockAllocator(4)
+    assert a.allocate(2) == [0, 1]
+    a.free([1, 0])
+    assert a.allocate(2) == [0, 1]
+    with pytest.raises(MemoryError):
+        a.allocate(3)
+    with pytest.raises(ValueError):
+        a.allocate(-1)
+    with pytest.raises(ValueError):
+        a.free([0, 0])
+    with pytest.raises(ValueError):
+        a.free([3])
+    with pytest.raises(ValueError):
+        BlockAllocator(0)
+
+
+def test_reuse_order_matches_reference(cache_trace):
+    cache = RecordingCache(num_layers=1, num_blocks=4, block_size=2, num_kv_heads=1, head_dim=1,
+                           dtype=torch.float32)
+    cache.create_sequence(1)
+    cache.create_sequence(2)
+    one = [torch.ones(3, 1, 1)]
+    cache.append_tokens(1, one, one)
+    first = list(cache.sequences[1].blocks)
+    cache.free_sequence(1)
+    cache.append_tokens(2, one, one)
+    assert first == cache_trace["reuse"]["first"]
+    assert cache.sequences[2].blocks == cache_trace["reuse"]["second"] == first[::-1]
+
+
+def test_random_trace_matches_reference(cache_trace):
+    cache = RecordingCache(num_layers=2, num_blocks=cache_trace["num_blocks"],
+                           block_size=cache_trace["block_size"], num_kv_heads=1, head_dim=2,
+                           dtype=torch.float32)
+    for op in cache_trace["ops"]:
+        if op["op"] == "create":
+            cache.create_sequence(op["seq"])
+        elif op["op"] == "append":
+            kv = [torch.zeros(op["n"], 1, 2) for _ in range(2)]
+            try:
+                cache.append_tokens(op["seq"], kv, kv)
+                res = "ok"
+            except MemoryError:
+                res = "MemoryError"
+            assert res == op["result"]
+            t = cache.sequences[op["seq"]]
+            assert t.blocks == op["blocks"]
+            assert t.length == op["length"]
+            assert cache.allocator.free_count == op["free"]
+        else:
+            cache.free_sequence(op["seq"])
+            assert cache.allocator.free_count == op["free"]
+        cache.assert_consistent()
+
+
+def test_slots_follow_page_table():
+    cache = RecordingCache(num_layers=2, num_blocks=8, block_size=4, num_kv_heads=1, head_dim=2,
+                           dtype=torch.float32)
+    cache.create_sequence(0)
+    cache.create_sequence(1)
+    cache.append_tokens(1, [torch.zeros(2, 1, 2)] * 2, [torch.zeros(2, 1, 2)] * 2)
+    cache.append_tokens(0, [torch.zeros(6, 1, 2)] * 2, [torch.zeros(6, 1, 2)] * 2)
+    # seq 1 owns block 0, seq 0 owns blocks 1, 2: slot = block * 4 + offset
+    assert cache.writes[-1] == (1, [4, 5, 6, 7, 8, 9])
+    assert cache.sequences[0].slots(4, 2) == [8, 9]
+    assert cache.sequences[0].block_for_pos(5) == (2, 1)
+    with pytest.raises(IndexError):
+        cache.sequences[0].block_for_pos(6)
+
+
+def test_batched_append_is_all_or_nothing():
+    cache = RecordingCache(num_layers=1, num_blocks=3, block_size=2, num_kv_heads=1, head_dim=1,
+                           dtype=torch.float32)
+    for s in range(3):
+        cache.create_sequence(s)
+    kv = [torch.zeros(6, 1, 1)]   # 2 tokens each -> one block each
+    cache.append_tokens_batched([0, 1, 2], kv, kv)
+    assert [cache.sequence_length(s) for s in range(3)] == [2, 2, 2]
+    assert cache.writes[-1][1] == [0, 1, 2, 3, 4, 5]
+    with pytest.raises(MemoryError):   # needs 3 more blocks, none free
+        cache.append_tokens_batched([0, 1, 2], kv, kv)
+    assert [len(cache.sequences[s].blocks) for s in range(3)] == [1, 1, 1]
+    assert cache.allocator.free_count == 0
+    cache.assert_consistent()
+
+
+def test_write_failure_rolls_back_new_blocks():
+    cache = RecordingCache(num_layers=1, num_blocks=4, block_size=2, num_kv_heads=1, head_dim=1,
+                           dtype=torch.float32, fail_write=True)
+    cache.create_sequence(0)
+    with pytest.raises(RuntimeError):
+        cache.append_tokens(0, [torch.zeros(3, 1, 1)], [torch.zeros(3, 1, 1)])
+    assert cache.sequences[0].blocks == [] and cache.sequence_length(0) == 0
+    assert cache.allocator.free_count == 4
+
+
+def test_cpu_cache_has_no_cpu_fallback():
+    cache = PagedKVCache(num_layers=1, num_blocks=4, block_size=2, num_kv_heads=1, head_dim=1,
+                         dtype=torch.float32)
+    cache.create_sequence(0)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        cache.append_tokens(0, [torch.zeros(3, 1, 1)], [torch.zeros(3, 1, 1)])
+    assert cache.sequences[0].blocks == [] and cache.allocator.free_count == 4
+
+
+def test_validation_errors_match_reference():
+    cache = RecordingCache(num_layers=2, num_blocks=4, block_size=2, num_kv_heads=2, head_dim=3,
+                           dtype=torch.float32)
+    cache.create_sequence(0)
+    with pytest.raises(ValueError):
+        cache.create_sequence(0)
+    with pytest.raises(KeyError):
+        cache.append_tokens(9, [], [])
+    with pytest.raises(ValueError):
+        cache.append_tokens(0, [torch.zeros(1, 2, 3)], [torch.zeros(1, 2, 3)])
+    with pytest.raises(ValueError):
+        cache.append_tokens(0, [torch.zeros(1, 2, 4)] * 2, [torch.zeros(1, 2, 4)] * 2)
+    with pytest.raises(ValueError):
+        cache.append_tokens(0, [torch.zeros(1, 2, 3), torch.zeros(2, 2, 3)],
+                            [torch.zeros(1, 2, 3)] * 2)
+    with pytest.raises(IndexError):
+        cache.gather_layer(0, 2)
+    for bad in (dict(num_layers=0), dict(block_size=0), dict(num_kv_heads=0)):
+        kw = dict(num_layers=1, num_blocks=4, block_size=2, num_kv_heads=1, head_dim=1)
+        kw.update(bad)
+        with pytest.raises(ValueError):
+            PagedKVCache(**kw)
+    cache.append_tokens(0, [torch.zeros(0, 2, 3)] * 2, [torch.zeros(0, 2, 3)] * 2)
+    assert cache.writes == []
+
+
+def test_decode_metadata_packing():
+    cache = RecordingCache(num_layers=1, num_blocks=16, block_size=4, num_kv_heads=1, head_dim=1,
+                           dtype=torch.float32)
+    for s, n in [(0, 5), (1, 1), (2, 12)]:
+        cache.create_sequence(s)
+        cache.append_tokens(s, [torch.zeros(n, 1, 1)], [torch.zeros(n, 1, 1)])
+    bt, cl, mx = cache.decode_metadata([2, 0, 1])
+    assert bt.dtype == torch.int32 and cl.dtype == torch.int32
+    assert bt.tolist() == [[3, 4, 5], [0, 1, 0], [2, 0, 0]]
+    assert cl.tolist() == [12, 5, 1] and mx == 12
+    bt, cl, mx = cache.decode_metadata([1], extra_tokens=3, pad_pages=4)
+    assert bt.shape == (1, 4) and cl.tolist() == [4] and mx == 4
+
+
+def test_sequence_page_table_properties():
+    t = SequencePageTable(seq_id=0, block_size=4, blocks=[3, 1], length=5)
+    assert t.block_count == 2 and t.capacity_tokens == 8 and t.free_slots == 3
