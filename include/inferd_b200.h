@@ -104,10 +104,13 @@ INFERD_API int inferd_gather_paged_kv(void* key_out, void* value_out,
  * context_lens: [num_seqs] int32 on the device, or NULL for "every sequence has
  * max_context_len keys".  max_context_len is a host-side upper bound used for grid sizing.
  * A sequence with no visible keys gets an all-zero output row (softmax over nothing).
- * workspace: >= inferd_paged_attention_workspace_bytes(...) bytes, 256-byte aligned; its
- * first inferd_paged_attention_counter_bytes(...) bytes must be zero before the first
- * call and are left zero by every completed call.  Calls that share a workspace must be
- * ordered on one stream.
+ * workspace: >= inferd_paged_attention_workspace_bytes(...) bytes, 256-byte aligned.  It
+ * starts with a fixed 2 MiB ticket-counter region (partials are stored after it, whatever
+ * the call's shape); the first inferd_paged_attention_counter_bytes(num_seqs,
+ * num_kv_heads) bytes of that region are used by a call, must be zero before it, and are
+ * left zero by every completed call -- zero the region once when the workspace is
+ * allocated and it can be shared by calls of any shape.  Calls that share a workspace
+ * must be ordered on one stream.
  */
 INFERD_API int inferd_paged_attention(void* out, const void* query,
                            const void* key_cache, const void* value_cache,

@@ -42,7 +42,8 @@ constexpr int kQRowBytes = 272;              // 256 B + 16 B pad: conflict-free 
 constexpr int kConsumerWarps = 4;
 constexpr int kStages = 8;  // multiple of kConsumerWarps: stage s is owned by warp s % 4
 constexpr int kCtasPerSm = 2;
-constexpr int kMaxSeqsFast = 4096;
+constexpr int kMaxSeqsFast = 4096;      // sequences per launch (larger batches are chunked)
+constexpr int kMaxKvHeadsFast = 128;
 constexpr int kMaxRowsFast = 32;  // q_len * group rows per (sequence, kv head)
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -284,7 +285,6 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, kCtasPerSm)
       }
       *reinterpret_cast<uint4*>(qtile + c * kQRowBytes + ch * 16) = v;
     }
-    for (int i = tid; i < NQP * kHeadDim; i += kConsumerThreads) merge[i] = 0.f;
     named_barrier_sync(1, kConsumerThreads);
 
     // Last key position each of this thread's columns may see (-1 for padding columns).
@@ -472,6 +472,9 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, kCtasPerSm)
       colstat[tid * 2 + 0] = M;
       colstat[tid * 2 + 1] = Ls;
     }
+    // Rescale this warp's O to the common maximum, then sum the warps into `merge` in a
+    // fixed warp order (warp 0 stores, warps 1..3 add), so results are reproducible.
+    float fw[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -479,15 +482,24 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, kCtasPerSm)
         const int c = nt * 8 + 2 * (lane & 3) + j;
         float M = -INFINITY;
         for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml[(w * NQP + c) * 2]);
-        const float f = ex2(m[nt][j] - (M == -INFINITY ? 0.f : M));
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          const int d = mt * 16 + (lane >> 2);
-          atomicAdd(&merge[c * kHeadDim + d], o[mt][nt][j] * f);
-          atomicAdd(&merge[c * kHeadDim + d + 8], o[mt][nt][j + 2] * f);
-        }
+        fw[nt][j] = ex2(m[nt][j] - (M == -INFINITY ? 0.f : M));
       }
-    named_barrier_sync(1, kConsumerThreads);
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      if (cw == w) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int c = nt * 8 + 2 * (lane & 3) + (e & 1);
+              const int d = mt * 16 + (lane >> 2) + ((e >> 1) << 3);
+              const float v = o[mt][nt][e] * fw[nt][e & 1];
+              merge[c * kHeadDim + d] = (w == 0) ? v : merge[c * kHeadDim + d] + v;
+            }
+      }
+      named_barrier_sync(1, kConsumerThreads);
+    }
 
     const int c_first = cta_of(seg_start, T_pages, G);
     const int c_last = cta_of(seg_end - 1, T_pages, G);
@@ -695,12 +707,19 @@ struct WorkspaceLayout {
   size_t counters, ml, o, total;
 };
 
+// Workspace: [ticket counters: fixed kCounterRegionBytes][partial (m, l)][partial O].
+// The counter region has the same size for every call, so calls of different shapes can
+// share one workspace: partials of one call never land on another call's counters, and
+// every completed call leaves the counters it used at zero.
+constexpr size_t kCounterRegionBytes =
+    static_cast<size_t>(kMaxSeqsFast) * kMaxKvHeadsFast * sizeof(int32_t);
+
 inline WorkspaceLayout workspace_layout(int num_seqs, int num_kv_heads, int nqp, int grid) {
   WorkspaceLayout w;
   const size_t segs = static_cast<size_t>(num_seqs) * num_kv_heads;
   const size_t slots = static_cast<size_t>(grid) + segs;
   w.counters = 0;
-  w.ml = align256(segs * sizeof(int32_t));
+  w.ml = kCounterRegionBytes;
   w.o = w.ml + align256(slots * nqp * 2 * sizeof(float));
   w.total = w.o + align256(slots * nqp * kHeadDim * sizeof(float));
   return w;
@@ -842,6 +861,7 @@ extern "C" int inferd_paged_attention(void* out, const void* query, const void* 
 
   const bool fast = (dtype == INFERD_BF16 || dtype == INFERD_F16) && head_dim == kHeadDim &&
                     block_size == kPage && nq <= kMaxRowsFast && rows < (int64_t{1} << 31) &&
+                    num_kv_heads <= kMaxKvHeadsFast &&
                     aligned(key_cache, 16) && aligned(value_cache, 16) && aligned(query, 16) &&
                     aligned(out, 16);
   if (!fast) {

@@ -202,6 +202,18 @@ def test_int64_block_tables_and_repeat_calls(cuda_device):
     assert_bf16_close(outs[0].float().cpu().numpy(), ref, "int64 tables")
 
 
+def test_workspace_shared_across_call_shapes(cuda_device):
+    # one workspace serves calls of different (num_seqs, q_len) in sequence; a call's
+    # partials must never land on the next call's ticket counters
+    rng = np.random.default_rng(40)
+    shapes = [([12000], 1), (rng.integers(600, 3000, 16).tolist(), 5),
+              (rng.integers(100, 5000, 40).tolist(), 1), ([9000, 7000, 8000], 2),
+              ([20000], 1)]
+    for i, (lens, q_len) in enumerate(shapes):
+        out, ref = run_batched(cuda_device, lens, q_len, 32, 8, torch.bfloat16, seed=40 + i)
+        assert_bf16_close(out, ref, f"shape {i}")
+
+
 def test_bad_block_id_raises_index_error(cuda_device):
     kb = torch.zeros(4, 8, 16, 128, dtype=torch.bfloat16, device=cuda_device)
     q = torch.zeros(32, 128, dtype=torch.bfloat16, device=cuda_device)
