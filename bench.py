@@ -135,6 +135,7 @@ def ncu_traffic(workload: str) -> float | None:
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
+        line = line.strip()
         if line.startswith("dram_bytes_per_launch_full_size:"):
             try:
                 return float(line.split(":", 1)[1].split()[0])
