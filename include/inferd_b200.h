@@ -129,6 +129,30 @@ INFERD_API size_t inferd_paged_attention_workspace_bytes(int32_t num_seqs, int32
 INFERD_API size_t inferd_paged_attention_counter_bytes(int32_t num_seqs, int32_t num_kv_heads);
 
 /*
+ * inferd_paged_attention without a caller-provided workspace: same arguments, results
+ * and status codes as inferd_paged_attention minus (workspace, workspace_bytes).
+ * No counterpart in the reference; it exists for callers that cannot allocate device
+ * memory at call time (FFI hosts without a device allocator, serving loops whose device
+ * memory budget is fixed at start-up).  It calls no cudaMalloc/cudaFree and no
+ * allocating library routine.
+ * Scratch: a 16 MiB static device array inside the library, held by every GPU that loads
+ * the library until the process exits.  A call whose needs exceed it
+ * (inferd_paged_attention_workspace_bytes(...) > 16 MiB) returns INFERD_ERR_WORKSPACE.
+ * The first call on a device looks up the array's device address (once per device, with
+ * that device current); make that first call before any stream capture.  Every call
+ * clears the ticket counters itself; all calls share the array, so calls that overlap on
+ * the GPU race -- order them on one stream.
+ */
+INFERD_API int inferd_paged_attention_noalloc(void* out, const void* query,
+                           const void* key_cache, const void* value_cache,
+                           const void* block_tables, int32_t block_table_bytes,
+                           int64_t block_table_stride, const int32_t* context_lens,
+                           int32_t num_seqs, int32_t q_len, int32_t num_q_heads,
+                           int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                           int64_t num_blocks, int32_t max_context_len, float scale,
+                           int32_t dtype, int32_t* error_word, void* stream);
+
+/*
  * Dense (contiguous) attention: query [q_len, num_q_heads, head_dim] against key/value
  * [seq_len, num_kv_heads, head_dim].  q_len == 1 is core/paged_attn.py:64-106
  * dense_attention (no mask); q_len > 1 applies the same causal rule as

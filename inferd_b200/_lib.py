@@ -55,6 +55,9 @@ _SIGNATURES = {
         _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i64, _c_void_p, _i32,
         _i32, _i32, _i32, _i32, _i32, _i64, _i32, _f32, _i32, _c_void_p, _sz, _c_void_p,
         _c_void_p]),
+    "inferd_paged_attention_noalloc": (ctypes.c_int, [
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i64, _c_void_p, _i32,
+        _i32, _i32, _i32, _i32, _i32, _i64, _i32, _f32, _i32, _c_void_p, _c_void_p]),
     "inferd_paged_attention_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "inferd_paged_attention_counter_bytes": (_sz, [_i32, _i32]),
     "inferd_dense_attention": (ctypes.c_int, [

@@ -23,7 +23,8 @@ LIB_DIR = PKG_DIR / "lib"
 LIB_PATH = LIB_DIR / "libinferd_sm100a.so"
 INCLUDE_DIR = REPO_DIR / "include"
 
-SOURCES = ["runtime.cu", "cache_ops.cu", "paged_attention.cu", "fp8_linear.cu"]
+SOURCES = ["runtime.cu", "cache_ops.cu", "paged_attention.cu", "paged_attention_noalloc.cu",
+           "fp8_linear.cu"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
