@@ -373,6 +373,10 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
         stream.synchronize()
         ctx = [cache.sequence_length(i) for i in ids]
         total_bytes += step_bytes(ctx, ql)["total"]
+        if ql > 1:
+            # speculative verify: keep one accepted token, roll the rest of the window back
+            for i, n in zip(ids, ctx):
+                cache.truncate_sequence(i, n - ql + 1)
         h2d = (q.numel() + k.numel() + v.numel()) * ELEM + dwl.b * ql * 8 \
             + bt.numel() * 4 + cl.numel() * 4
         d2h = res.numel() * ELEM
@@ -399,7 +403,8 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
     return {"value": round(total_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "steps": steps, "ms_per_step": round(ms / steps, 5),
-            "note": "contexts grow by the appended tokens each step; bytes counted per step"}
+            "note": "contexts grow by one token per step (verify: the window is appended, "
+                    "verified, and all but one token rolled back); bytes counted per step"}
 
 
 # ------------------------------------------------------------------ CPU baseline (oracle)

@@ -135,9 +135,9 @@ INFERD_API size_t inferd_paged_attention_counter_bytes(int32_t num_seqs, int32_t
  * memory at call time (FFI hosts without a device allocator, serving loops whose device
  * memory budget is fixed at start-up).  It calls no cudaMalloc/cudaFree and no
  * allocating library routine.
- * Scratch: a 16 MiB static device array inside the library, held by every GPU that loads
+ * Scratch: a 32 MiB static device array inside the library, held by every GPU that loads
  * the library until the process exits.  A call whose needs exceed it
- * (inferd_paged_attention_workspace_bytes(...) > 16 MiB) returns INFERD_ERR_WORKSPACE.
+ * (inferd_paged_attention_workspace_bytes(...) > 32 MiB) returns INFERD_ERR_WORKSPACE.
  * The first call on a device looks up the array's device address (once per device, with
  * that device current); make that first call before any stream capture.  Every call
  * clears the ticket counters itself; all calls share the array, so calls that overlap on

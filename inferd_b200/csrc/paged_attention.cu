@@ -1,20 +1,24 @@
 // paged_attention.cu -- paged GQA attention over the block-table KV pool.
 //
 // Fast path (bf16/f16, head_dim 128, block_size 16, q_len * group <= 32):
-//   A persistent, page-balanced kernel.  The (sequence, kv-head) page lists are laid end
-//   to end into one global page axis of T = num_kv_heads * sum_b ceil(L_b / 16) pages,
-//   and CTA c of G streams pages [c*T/G, (c+1)*T/G), so every CTA moves the same number
-//   of bytes however uneven the context lengths are.  A CTA range that cuts a
-//   (sequence, kv-head) segment produces a partial (m, l, O) for it; the CTA that
-//   finishes a segment last (atomic ticket, no spinning) merges the partials.
+//   A persistent kernel of independent warps.  The (sequence, kv-head) page lists are
+//   laid end to end into one page axis of T = num_kv_heads * sum_b ceil(L_b / 16) pages,
+//   and warp w of the U warps in the grid streams pages [w*T/U, (w+1)*T/U), so every warp
+//   moves the same number of bytes however uneven the context lengths are.
 //
-//   Per CTA: one producer warp streams 4 KiB K and V pages into an 8-stage shared-memory
-//   ring with TMA 2-D tiled loads (128-byte swizzle, evict-first), four consumer warps
-//   each own every fourth page: S = K Q^T and O^T += V^T P^T on mma.sync m16n8k16 with
-//   fp32 accumulators, online softmax in base 2 with warp-shuffle row maxima, and the
-//   P fragment moved from accumulator to operand layout with movmatrix.  All q-rows that
+//   Each warp feeds itself: it reads 32 block ids at a time with one coalesced load
+//   (prefetching the next 32), lane 0 issues TMA 2-D tiled loads (128-byte swizzle,
+//   evict-first L2 policy) of 4 KiB K and V pages into the warp's own 3-stage shared-
+//   memory ring, and the warp computes S = K Q^T and O^T += V^T P^T on mma.sync m16n8k16
+//   with fp32 accumulators, an online softmax in base 2 with warp-shuffle column maxima,
+//   and movmatrix to turn the P accumulator into an MMA operand.  All query rows that
 //   share a kv head (group heads x q_len queries) ride in the MMA's N dimension, so each
-//   K/V byte is read from HBM once.
+//   K/V byte is read from HBM once.  Warps never wait for one another: there is no
+//   block-level barrier after set-up.
+//
+//   A (sequence, kv head) segment that lies inside one warp's range is normalised and
+//   stored directly.  A segment cut by warp ranges gets one partial (m, l, O) per warp;
+//   the warp that finishes the segment last (atomic ticket, no spinning) merges them.
 //
 // Generic path (fp32 and any other size): one CTA per (sequence, query row), fp32 CUDA
 // core arithmetic.  Used for fp32 pools and small head dims such as the reference's
@@ -38,16 +42,17 @@ constexpr int kHeadDim = 128;
 constexpr int kPage = 16;                    // tokens per KV block
 constexpr int kHalfBytes = 2048;             // one TMA box: 16 rows x 64 elements x 2 B
 constexpr int kStageBytes = 4 * kHalfBytes;  // K lo/hi, V lo/hi halves of one page
-constexpr int kQRowBytes = 272;              // 256 B + 16 B pad: conflict-free ldmatrix
-constexpr int kConsumerWarps = 4;
-constexpr int kStages = 8;  // multiple of kConsumerWarps: stage s is owned by warp s % 4
+constexpr int kWarps = 4;                    // warps per CTA
 constexpr int kCtasPerSm = 2;
-constexpr int kMaxSeqsFast = 4096;      // sequences per launch (larger batches are chunked)
+constexpr int kMaxSeqsFast = 1024;  // sequences per launch (larger batches are chunked)
 constexpr int kMaxKvHeadsFast = 128;
-constexpr int kMaxRowsFast = 32;  // q_len * group rows per (sequence, kv head)
+constexpr int kMaxRowsFast = 32;    // q_len * group rows per (sequence, kv head)
 constexpr float kLog2e = 1.4426950408889634f;
 
-static_assert(kStages % kConsumerWarps == 0, "stage ownership needs kStages % warps == 0");
+#ifndef INFERD_STAGES_PER_WARP
+#define INFERD_STAGES_PER_WARP 3  // pages in flight per warp (3 x 8 KiB)
+#endif
+constexpr int kStagesPerWarp = INFERD_STAGES_PER_WARP;
 
 struct FastParams {
   void* out;
@@ -60,9 +65,9 @@ struct FastParams {
   int32_t num_seqs, q_len, num_q_heads, num_kv_heads, group, nq;
   int64_t num_blocks;
   float scale_log2;
-  int32_t* counters;
-  float* part_ml;
-  float* part_o;
+  int32_t* counters;  // per (sequence, kv head) ticket counters, 0 between launches
+  float* part_ml;     // [slot][NQP][2]    (m, l) per query row
+  float* part_o;      // [slot][128][NQP]  unnormalised O, query row fastest
   int32_t* error_word;
 };
 
@@ -97,37 +102,48 @@ __device__ __forceinline__ int find_seq(const int* prefix, int B, int64_t q) {
   return lo;
 }
 
-// CTA whose balanced range [c*T/G, (c+1)*T/G) contains global page g.
-__device__ __forceinline__ int cta_of(int64_t g, int64_t T, int G) {
-  int64_t c = ((g + 1) * G + T - 1) / T - 1;
-  if (c < 0) c = 0;
-  if (c > G - 1) c = G - 1;
-  return static_cast<int>(c);
+// Unit (warp) whose balanced range [u*T/U, (u+1)*T/U) contains global page g.
+__device__ __forceinline__ int unit_of(int64_t g, int64_t T, int U) {
+  int64_t u = ((g + 1) * U + T - 1) / T - 1;
+  if (u < 0) u = 0;
+  if (u > U - 1) u = U - 1;
+  return static_cast<int>(u);
 }
 
-template <bool kBf16, int NT>
-__global__ void __launch_bounds__((kConsumerWarps + 1) * 32, kCtasPerSm)
+// Query-row fragments (MMA B operand, d x rows) of one segment, read from global memory:
+// b0 = rows n = nt*8 + lane/4, d = kk*16 + 2*(lane%4) + {0,1}; b1 = the same at d + 8.
+template <typename T, int NT>
+__device__ __forceinline__ void load_q_frags(uint32_t (&qf)[8][NT][2], const T* qptr,
+                                             const FastParams& p, int b, int h, int lane) {
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int c = nt * 8 + (lane >> 2);
+    const bool live = c < p.nq;
+    const int qi = live ? c / p.group : 0, gi = live ? c - qi * p.group : 0;
+    const uint32_t* row = reinterpret_cast<const uint32_t*>(
+        qptr + ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) * kHeadDim);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      qf[kk][nt][0] = live ? __ldg(row + kk * 8 + (lane & 3)) : 0u;
+      qf[kk][nt][1] = live ? __ldg(row + kk * 8 + 4 + (lane & 3)) : 0u;
+    }
+  }
+}
+
+template <bool kBf16, int NT, int STAGES>
+__global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
     paged_attn_tc_kernel(const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap, const FastParams p) {
   using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
   constexpr int NQP = NT * 8;
-  constexpr int kThreads = (kConsumerWarps + 1) * 32;
-  constexpr int kConsumerThreads = kConsumerWarps * 32;
-  constexpr bool kQInRegs = NT <= 2;
+  constexpr int kThreads = kWarps * 32;
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ int warp_tot[kConsumerWarps + 1];
-  __shared__ int flags[4];  // [0] abort, [1] last-ticket
+  __shared__ int warp_tot[kWarps];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* stages = smem;
-  uint8_t* qtile = stages + kStages * kStageBytes;
-  float* merge = reinterpret_cast<float*>(qtile + NQP * kQRowBytes);  // [NQP][128]
-  float* ml = merge + NQP * kHeadDim;                                 // [warps][NQP][2]
-  float* colstat = ml + kConsumerWarps * NQP * 2;                     // [NQP][2]
-  uint64_t* full = reinterpret_cast<uint64_t*>(colstat + NQP * 2);
-  uint64_t* empty = full + kStages;
-  int* prefix = reinterpret_cast<int*>(empty + kStages);  // [B + 1]
+  uint64_t* bars_all = reinterpret_cast<uint64_t*>(smem + kWarps * STAGES * kStageBytes);
+  int* prefix = reinterpret_cast<int*>(bars_all + kWarps * STAGES);  // [B + 1]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int B = p.num_seqs, Hkv = p.num_kv_heads;
@@ -145,11 +161,10 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, kCtasPerSm)
       if (lane >= o) incl += v;
     }
     if (lane == 31) warp_tot[warp] = incl;
-    if (tid == 0) { flags[0] = 0; flags[1] = 0; }
     __syncthreads();
     int run = incl - local;
     int total = 0;
-    for (int w = 0; w <= kConsumerWarps; ++w) {
+    for (int w = 0; w < kWarps; ++w) {
       if (w < warp) run += warp_tot[w];
       total += warp_tot[w];
     }
@@ -160,292 +175,114 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, kCtasPerSm)
     if (tid == 0) prefix[B] = total;
     __syncthreads();
   }
+  // No block-level synchronisation below this point: every warp runs on its own.
 
   const int64_t T_pages = static_cast<int64_t>(Hkv) * prefix[B];
-  const int G = static_cast<int>(min64(static_cast<int64_t>(gridDim.x), max64(T_pages, 1)));
-  if (static_cast<int>(blockIdx.x) >= G) return;
+  const int U = static_cast<int>(min64(static_cast<int64_t>(gridDim.x) * kWarps, max64(T_pages, 1)));
+  const int w = blockIdx.x * kWarps + warp;
+  if (w >= U) return;
 
   // Sequences without keys: softmax over an empty set -> zero output rows.
-  for (int b = blockIdx.x; b < B; b += G) {
+  for (int b = w; b < B; b += U) {
     if (prefix[b + 1] != prefix[b]) continue;
     const int64_t n16 = static_cast<int64_t>(p.q_len) * p.num_q_heads * kHeadDim / 8;
     uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out) +
                                           static_cast<int64_t>(b) * p.q_len * p.num_q_heads * kHeadDim);
-    for (int64_t i = tid; i < n16; i += kThreads) dst[i] = make_uint4(0, 0, 0, 0);
+    for (int64_t i = lane; i < n16; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
   }
   if (T_pages == 0) return;
 
-  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * T_pages / G;
-  const int64_t g1 = static_cast<int64_t>(blockIdx.x + 1) * T_pages / G;
-
-  if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
+  const int64_t g0 = static_cast<int64_t>(w) * T_pages / U;
+  const int64_t g1 = static_cast<int64_t>(w + 1) * T_pages / U;
+  const int n_pages = static_cast<int>(g1 - g0);
+  uint8_t* stages = smem + warp * STAGES * kStageBytes;
+  uint64_t* full = bars_all + warp * STAGES;
+  if (lane == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
   }
-  __syncthreads();
+  __syncwarp();
 
-  volatile int* vflags = flags;
-
-  if (warp == kConsumerWarps) {
-    // ======================= producer warp: block ids -> TMA page loads ==============
-    if (lane == 0) {
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
-    }
-    const uint64_t policy = l2_policy_evict_first();
-    auto row_of = [&](int64_t g) -> int32_t {
-      const int b = find_seq(prefix, B, g / Hkv);
-      const int pb = prefix[b + 1] - prefix[b];
-      const int64_t off = g - static_cast<int64_t>(Hkv) * prefix[b];
-      const int h = static_cast<int>(off / pb);
-      const int page = static_cast<int>(off - static_cast<int64_t>(h) * pb);
-      int64_t blk = block_id(p, b, page);
-      if (blk < 0 || blk >= p.num_blocks) {
-        report_error(p.error_word, INFERD_ERR_DEVICE_INDEX);
-        blk = 0;
-      }
-      return static_cast<int32_t>((blk * Hkv + h) * kPage);
-    };
-    int64_t issued = 0;
-    bool stop = false;
-    int32_t row_cur = (g0 + lane < g1) ? row_of(g0 + lane) : 0;
-    for (int64_t base = g0; base < g1 && !stop; base += 32) {
-      const int32_t row_next = (base + 32 + lane < g1) ? row_of(base + 32 + lane) : 0;
-      const int n = static_cast<int>(min64(32, g1 - base));
-      for (int j = 0; j < n; ++j) {
-        const int32_t r = __shfl_sync(0xffffffffu, row_cur, j);
-        if (lane == 0 && !stop) {
-          const int64_t local = base + j - g0;
-          const int stage = static_cast<int>(local % kStages);
-          const uint32_t round = static_cast<uint32_t>(local / kStages);
-          if (vflags[0] != 0) {
-            stop = true;
-          } else if (round > 0 && !mbar_wait(&empty[stage], (round - 1) & 1u)) {
-            report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
-            vflags[0] = 1;
-            stop = true;
-          } else {
-            uint8_t* st = stages + stage * kStageBytes;
-            mbar_arrive_expect_tx(&full[stage], kStageBytes);
-            tma_load_2d(st, &kmap, 0, r, &full[stage], policy);
-            tma_load_2d(st + kHalfBytes, &kmap, 64, r, &full[stage], policy);
-            tma_load_2d(st + 2 * kHalfBytes, &vmap, 0, r, &full[stage], policy);
-            tma_load_2d(st + 3 * kHalfBytes, &vmap, 64, r, &full[stage], policy);
-            ++issued;
-          }
-        }
-        stop = __shfl_sync(0xffffffffu, stop ? 1 : 0, 0) != 0;
-      }
-      row_cur = row_next;
-    }
-    // Drain: never leave the CTA with a TMA write still in flight into its smem.
-    if (lane == 0) {
-      for (int s = 0; s < kStages; ++s) {
-        if (s >= issued) break;
-        const int64_t rounds = (issued - s + kStages - 1) / kStages;
-        if (!mbar_wait(&full[s], static_cast<uint32_t>((rounds - 1) & 1))) {
-          report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
-        }
-      }
-    }
-    return;
-  }
-
-  // ========================== consumer warps ==========================================
-  const int cw = warp;
-  const int mrow = lane & 7, msel = lane >> 3;
-  const uint32_t qbase = smem_u32(qtile);
+  const uint64_t policy = l2_policy_evict_first();
   const T* qptr = static_cast<const T*>(p.query);
   T* optr = static_cast<T*>(p.out);
+  const int mrow = lane & 7, msel = lane >> 3;
 
-  int64_t g = g0;
-  while (g < g1) {
-    // ---- locate the (sequence, kv head) segment that page g belongs to
+  // pool row (block * Hkv + head) * 16 of global page g
+  auto row_of = [&](int64_t g) -> int32_t {
     const int b = find_seq(prefix, B, g / Hkv);
     const int pb = prefix[b + 1] - prefix[b];
-    const int64_t seg0 = static_cast<int64_t>(Hkv) * prefix[b];
-    const int h = static_cast<int>((g - seg0) / pb);
-    const int64_t seg_start = seg0 + static_cast<int64_t>(h) * pb;
-    const int64_t seg_end = seg_start + pb;
-    const int64_t piece_end = min64(g1, seg_end);
-    const int L = seq_len_of(p, b, false);
-
-    // ---- stage Q rows of this segment (row c = qi * group + gi) and clear the merge area
-    for (int i = tid; i < NQP * 16; i += kConsumerThreads) {
-      const int c = i >> 4, ch = i & 15;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (c < p.nq) {
-        const int qi = c / p.group, gi = c - qi * p.group;
-        const T* src = qptr + ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads +
-                               h * p.group + gi) * kHeadDim + ch * 8;
-        v = *reinterpret_cast<const uint4*>(src);
-      }
-      *reinterpret_cast<uint4*>(qtile + c * kQRowBytes + ch * 16) = v;
+    const int64_t off = g - static_cast<int64_t>(Hkv) * prefix[b];
+    const int h = static_cast<int>(off / pb);
+    const int page = static_cast<int>(off - static_cast<int64_t>(h) * pb);
+    int64_t blk = block_id(p, b, page);
+    if (blk < 0 || blk >= p.num_blocks) {
+      report_error(p.error_word, INFERD_ERR_DEVICE_INDEX);
+      blk = 0;
     }
-    named_barrier_sync(1, kConsumerThreads);
+    return static_cast<int32_t>((blk * Hkv + h) * kPage);
+  };
+  // Block ids of this warp's pages, 32 per register batch: rows_cur holds pages
+  // [32k, 32k+32) of the warp's range, rows_next the following 32.
+  int32_t rows_cur = lane < n_pages ? row_of(g0 + lane) : 0;
+  int32_t rows_next = 32 + lane < n_pages ? row_of(g0 + 32 + lane) : 0;
+  bool abort = false;
 
-    // Last key position each of this thread's columns may see (-1 for padding columns).
-    int lim[NT][2];
+  // Issue local page j (all lanes call; rows looked up by shuffle; lane 0 issues).
+  auto issue_page = [&](int j, int cur_batch) {
+    const int32_t rc = __shfl_sync(0xffffffffu, rows_cur, j & 31);
+    const int32_t rn = __shfl_sync(0xffffffffu, rows_next, j & 31);
+    const int32_t r = (j >> 5) == cur_batch ? rc : rn;
+    if (lane == 0) {
+      const int s = j % STAGES;
+      uint8_t* st = stages + s * kStageBytes;
+      mbar_arrive_expect_tx(&full[s], kStageBytes);
+      tma_load_2d(st, &kmap, 0, r, &full[s], policy);
+      tma_load_2d(st + kHalfBytes, &kmap, 64, r, &full[s], policy);
+      tma_load_2d(st + 2 * kHalfBytes, &vmap, 0, r, &full[s], policy);
+      tma_load_2d(st + 3 * kHalfBytes, &vmap, 64, r, &full[s], policy);
+    }
+  };
+  int issued = 0;
+  for (; issued < STAGES && issued < n_pages; ++issued) issue_page(issued, 0);
+
+  // ---- current segment (sequence b, kv head h) and its state
+  int b = find_seq(prefix, B, g0 / Hkv);
+  int pb = prefix[b + 1] - prefix[b];
+  int64_t seg_start = static_cast<int64_t>(Hkv) * prefix[b];
+  int h = static_cast<int>((g0 - seg_start) / pb);
+  seg_start += static_cast<int64_t>(h) * pb;
+  int64_t seg_end = seg_start + pb;
+  int L = seq_len_of(p, b, false);
+  int64_t piece_start = g0;
+
+  uint32_t qf[8][NT][2];
+  int lim[NT][2];
+  float m[NT][2], l[NT][2], o[8][NT][4];
+
+  auto begin_segment = [&]() {
+    load_q_frags<T, NT>(qf, qptr, p, b, h, lane);
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int c = nt * 8 + 2 * (lane & 3) + j;
         lim[nt][j] = c < p.nq ? L - p.q_len + c / p.group : -1;
+        m[nt][j] = -INFINITY;
+        l[nt][j] = 0.f;
       }
-
-    uint32_t qf[kQInRegs ? 8 : 1][kQInRegs ? NT : 1][2];
-    if constexpr (kQInRegs) {
-#pragma unroll
-      for (int kk = 0; kk < 8; kk += 2)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          uint32_t r4[4];
-          const int n = nt * 8 + mrow;
-          const int d = (kk + (msel >> 1)) * 16 + (msel & 1) * 8;
-          ldmatrix_x4(r4, qbase + n * kQRowBytes + d * 2);
-          qf[kk][nt][0] = r4[0];
-          qf[kk][nt][1] = r4[1];
-          qf[kk + 1][nt][0] = r4[2];
-          qf[kk + 1][nt][1] = r4[3];
-        }
-    }
-
-    float m[NT][2], l[NT][2], o[8][NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      m[nt][0] = m[nt][1] = -INFINITY;
-      l[nt][0] = l[nt][1] = 0.f;
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) o[mt][nt][e] = 0.f;
     }
+  };
 
-    // ---- this warp's pages of the piece: local index (gg - g0) % 4 == cw
-    const int64_t first = g + ((cw - (g - g0) % kConsumerWarps) + kConsumerWarps) % kConsumerWarps;
-    for (int64_t gg = first; gg < piece_end; gg += kConsumerWarps) {
-      const int64_t local = gg - g0;
-      const int stage = static_cast<int>(local % kStages);
-      const uint32_t round = static_cast<uint32_t>(local / kStages);
-      bool ok = vflags[0] == 0;
-      if (ok && !mbar_wait(&full[stage], round & 1u)) {
-        if (lane == 0) {
-          report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
-          vflags[0] = 1;
-        }
-        ok = false;
-      }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      if (ok) {
-        const uint32_t kbase = smem_u32(stages + stage * kStageBytes);
-        const uint32_t vbase = kbase + 2 * kHalfBytes;
-        const int tok0 = static_cast<int>(gg - seg_start) * kPage;
-
-        // S[token][col] = K Q^T (fp32)
-        float s[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const int tok = ((msel & 1) << 3) + mrow;
-          const int ch = ((kk & 3) << 1) + (msel >> 1);
-          uint32_t a[4];
-          ldmatrix_x4(a, kbase + (kk >> 2) * kHalfBytes + tok * 128 + ((ch ^ (tok & 7)) << 4));
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            uint32_t b0, b1;
-            if constexpr (kQInRegs) {
-              b0 = qf[kk][nt][0];
-              b1 = qf[kk][nt][1];
-            } else {
-              uint32_t r2[2];
-              const int n = nt * 8 + mrow;
-              const int d = kk * 16 + (msel & 1) * 8;
-              ldmatrix_x2(r2, qbase + n * kQRowBytes + d * 2);
-              b0 = r2[0];
-              b1 = r2[1];
-            }
-            mma_16816<kBf16>(s[nt], a, b0, b1);
-          }
-        }
-
-        // scale to base 2, causal / length mask
-        const bool need_mask = tok0 + kPage - 1 > L - p.q_len;
-        const int t_lo = tok0 + (lane >> 2);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float v = s[nt][e] * p.scale_log2;
-            if (need_mask) {
-              const int t = t_lo + ((e >> 1) << 3);
-              if (t > lim[nt][e & 1]) v = -INFINITY;
-            }
-            s[nt][e] = v;
-          }
-
-        // online softmax: column max over the 16 tokens (lanes sharing lane & 3)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            float mx = fmaxf(s[nt][j], s[nt][j + 2]);
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-            const float mnew = fmaxf(m[nt][j], mx);
-            const float mref = mnew == -INFINITY ? 0.f : mnew;
-            const float alpha = ex2(m[nt][j] - mref);
-            m[nt][j] = mnew;
-            const float p0 = ex2(s[nt][j] - mref), p1 = ex2(s[nt][j + 2] - mref);
-            s[nt][j] = p0;
-            s[nt][j + 2] = p1;
-            l[nt][j] = l[nt][j] * alpha + p0 + p1;
-#pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
-              o[mt][nt][j] *= alpha;
-              o[mt][nt][j + 2] *= alpha;
-            }
-          }
-
-        // P^T fragments (tokens x cols) in the working dtype
-        uint32_t pf[NT][2];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          pf[nt][0] = movmatrix_trans(pack2<kBf16>(s[nt][0], s[nt][1]));
-          pf[nt][1] = movmatrix_trans(pack2<kBf16>(s[nt][2], s[nt][3]));
-        }
-
-        // O^T[d][col] += V^T P^T ; rows of V past the sequence end hold stale pool bytes
-        const bool vmask = tok0 + kPage > L;
-        const int ta = tok0 + 2 * (lane & 3);
-        const uint32_t m01 = (ta < L ? 0x0000ffffu : 0u) | (ta + 1 < L ? 0xffff0000u : 0u);
-        const uint32_t m23 = (ta + 8 < L ? 0x0000ffffu : 0u) | (ta + 9 < L ? 0xffff0000u : 0u);
-#pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          const int tok = ((msel >> 1) << 3) + mrow;
-          const int ch = ((mt & 3) << 1) + (msel & 1);
-          uint32_t a[4];
-          ldmatrix_x4_trans(a, vbase + (mt >> 2) * kHalfBytes + tok * 128 + ((ch ^ (tok & 7)) << 4));
-          if (vmask) {
-            a[0] &= m01;
-            a[1] &= m01;
-            a[2] &= m23;
-            a[3] &= m23;
-          }
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma_16816<kBf16>(o[mt][nt], a, pf[nt][0], pf[nt][1]);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
-    }
-
-    // ---- merge the four warps' (m, l, O) for this piece
+  // Finish the piece [piece_start, piece_end) of the current segment: store the output
+  // if the piece is the whole segment, else publish a partial and maybe merge.
+  auto end_piece = [&](int64_t piece_end) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -455,113 +292,274 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, kCtasPerSm)
         v += __shfl_xor_sync(0xffffffffu, v, 8);
         v += __shfl_xor_sync(0xffffffffu, v, 16);
         l[nt][j] = v;
-        if (lane < 4) {
-          const int c = nt * 8 + 2 * lane + j;
-          ml[(cw * NQP + c) * 2 + 0] = m[nt][j];
-          ml[(cw * NQP + c) * 2 + 1] = v;
-        }
       }
-    named_barrier_sync(1, kConsumerThreads);
-    if (tid < NQP) {
-      float M = -INFINITY;
-      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml[(w * NQP + tid) * 2]);
-      const float Mref = M == -INFINITY ? 0.f : M;
-      float Ls = 0.f;
-      for (int w = 0; w < kConsumerWarps; ++w)
-        Ls += ml[(w * NQP + tid) * 2 + 1] * ex2(ml[(w * NQP + tid) * 2] - Mref);
-      colstat[tid * 2 + 0] = M;
-      colstat[tid * 2 + 1] = Ls;
+    const int seg_id = b * Hkv + h;
+    if (piece_start == seg_start && piece_end == seg_end) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = nt * 8 + 2 * (lane & 3) + (e & 1);
+          if (c >= p.nq) continue;
+          const float lv = l[nt][e & 1];
+          const float inv = lv > 0.f ? 1.f / lv : 0.f;
+          const int qi = c / p.group, gi = c - qi * p.group;
+          T* dst = optr + ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) * kHeadDim;
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt)
+            dst[mt * 16 + (lane >> 2) + ((e >> 1) << 3)] = from_f32<T>(o[mt][nt][e] * inv);
+        }
+      return;
     }
-    // Rescale this warp's O to the common maximum, then sum the warps into `merge` in a
-    // fixed warp order (warp 0 stores, warps 1..3 add), so results are reproducible.
-    float fw[NT][2];
+    // partial: slot = unit + segment id is unique (units and segments are both monotone
+    // along the page axis), at most U + segments slots
+    const int64_t slot = static_cast<int64_t>(w) + seg_id;
+    float* po = p.part_o + slot * kHeadDim * NQP;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int c = nt * 8 + 2 * (lane & 3) + j;
-        float M = -INFINITY;
-        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml[(w * NQP + c) * 2]);
-        fw[nt][j] = ex2(m[nt][j] - (M == -INFINITY ? 0.f : M));
-      }
-    for (int w = 0; w < kConsumerWarps; ++w) {
-      if (cw == w) {
+      for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int mt = 0; mt < 8; ++mt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int c = nt * 8 + 2 * (lane & 3) + (e & 1);
-              const int d = mt * 16 + (lane >> 2) + ((e >> 1) << 3);
-              const float v = o[mt][nt][e] * fw[nt][e & 1];
-              merge[c * kHeadDim + d] = (w == 0) ? v : merge[c * kHeadDim + d] + v;
-            }
-      }
-      named_barrier_sync(1, kConsumerThreads);
-    }
-
-    const int c_first = cta_of(seg_start, T_pages, G);
-    const int c_last = cta_of(seg_end - 1, T_pages, G);
-    const int seg_id = b * Hkv + h;
-    if (c_first == c_last) {
-      // whole segment inside this CTA: normalise and store
-      for (int i = tid; i < p.nq * 16; i += kConsumerThreads) {
-        const int c = i >> 4, ch = i & 15;
-        const float Ls = colstat[c * 2 + 1];
-        const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-        const float* src = merge + c * kHeadDim + ch * 8;
-        uint4 v;
-        v.x = pack2<kBf16>(src[0] * inv, src[1] * inv);
-        v.y = pack2<kBf16>(src[2] * inv, src[3] * inv);
-        v.z = pack2<kBf16>(src[4] * inv, src[5] * inv);
-        v.w = pack2<kBf16>(src[6] * inv, src[7] * inv);
-        const int qi = c / p.group, gi = c - qi * p.group;
-        T* dst = optr + ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) *
-                            kHeadDim + ch * 8;
-        *reinterpret_cast<uint4*>(dst) = v;
-      }
-    } else {
-      // partial for a segment shared with other CTAs: publish, take a ticket
-      const int64_t slot = static_cast<int64_t>(blockIdx.x) + seg_id;
-      float* po = p.part_o + slot * NQP * kHeadDim;
-      for (int i = tid; i < p.nq * kHeadDim / 4; i += kConsumerThreads)
-        reinterpret_cast<float4*>(po)[i] = reinterpret_cast<const float4*>(merge)[i];
-      if (tid < p.nq) {
-        p.part_ml[(slot * NQP + tid) * 2 + 0] = colstat[tid * 2 + 0];
-        p.part_ml[(slot * NQP + tid) * 2 + 1] = colstat[tid * 2 + 1];
-      }
-      __threadfence();
-      named_barrier_sync(1, kConsumerThreads);
-      if (tid == 0) {
-        const int prev = atomicAdd(p.counters + seg_id, 1);
-        vflags[1] = (prev == c_last - c_first) ? 1 : 0;
-      }
-      named_barrier_sync(1, kConsumerThreads);
-      if (vflags[1] != 0) {
-        __threadfence();
-        for (int i = tid; i < p.nq * kHeadDim; i += kConsumerThreads) {
-          const int c = i / kHeadDim, d = i - c * kHeadDim;
-          float M = -INFINITY;
-          for (int cc = c_first; cc <= c_last; ++cc)
-            M = fmaxf(M, __ldcg(p.part_ml + ((static_cast<int64_t>(cc) + seg_id) * NQP + c) * 2));
-          const float Mref = M == -INFINITY ? 0.f : M;
-          float Ls = 0.f, acc = 0.f;
-          for (int cc = c_first; cc <= c_last; ++cc) {
-            const int64_t sl = static_cast<int64_t>(cc) + seg_id;
-            const float f = ex2(__ldcg(p.part_ml + (sl * NQP + c) * 2) - Mref);
-            Ls += __ldcg(p.part_ml + (sl * NQP + c) * 2 + 1) * f;
-            acc += __ldcg(p.part_o + (sl * NQP + c) * kHeadDim + d) * f;
-          }
-          const int qi = c / p.group, gi = c - qi * p.group;
-          optr[((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) *
-                   kHeadDim + d] = from_f32<T>(Ls > 0.f ? acc / Ls : 0.f);
+        for (int hi = 0; hi < 2; ++hi) {
+          const int d = mt * 16 + (lane >> 2) + hi * 8;
+          *reinterpret_cast<float2*>(po + d * NQP + nt * 8 + 2 * (lane & 3)) =
+              make_float2(o[mt][nt][2 * hi], o[mt][nt][2 * hi + 1]);
         }
-        if (tid == 0) p.counters[seg_id] = 0;
+    if (lane < 4) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int c = nt * 8 + 2 * lane + j;
+          *reinterpret_cast<float2*>(p.part_ml + (slot * NQP + c) * 2) = make_float2(m[nt][j], l[nt][j]);
+        }
+    }
+    __threadfence();
+    __syncwarp();
+    const int u_first = unit_of(seg_start, T_pages, U);
+    const int u_last = unit_of(seg_end - 1, T_pages, U);
+    int last = 0;
+    if (lane == 0) last = atomicAdd(p.counters + seg_id, 1) == u_last - u_first;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    // ---- merge the segment's partials (this warp finished it last)
+    const int np = u_last - u_first + 1;
+    for (int nt = 0; nt < NT; ++nt) {
+      // column maxima and normalisers over all pieces, 8 columns of this n-tile
+      float M[8], Ls[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) M[c] = -INFINITY, Ls[c] = 0.f;
+      for (int p0 = 0; p0 < np; p0 += 32) {
+        if (p0 + lane < np) {
+          const float* ml = p.part_ml + ((static_cast<int64_t>(u_first) + p0 + lane + seg_id) * NQP + nt * 8) * 2;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) M[c] = fmaxf(M[c], __ldcg(ml + 2 * c));
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) M[c] = fmaxf(M[c], __shfl_xor_sync(0xffffffffu, M[c], o2));
+      // each lane: the two columns 2*(lane&3), +1 of this n-tile and rows d = k*8 + lane/4
+      float2 acc[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) acc[k] = make_float2(0.f, 0.f);
+      const int cp = 2 * (lane & 3);
+      for (int p0 = 0; p0 < np; p0 += 32) {
+        // lane q of the chunk holds piece p0+q's weights exp2(m - M) for all 8 columns
+        float fq[8];
+        const bool have = p0 + lane < np;
+        const float* ml = p.part_ml + ((static_cast<int64_t>(u_first) + p0 + lane + seg_id) * NQP + nt * 8) * 2;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float mc = have ? __ldcg(ml + 2 * c) : -INFINITY;
+          const float lc = have ? __ldcg(ml + 2 * c + 1) : 0.f;
+          fq[c] = ex2(mc - (M[c] == -INFINITY ? 0.f : M[c]));
+          Ls[c] += lc * fq[c];
+        }
+        const int nq_chunk = min(32, np - p0);
+        for (int q = 0; q < nq_chunk; ++q) {
+          float f0 = 0.f, f1 = 0.f;
+#pragma unroll
+          for (int c = 0; c < 8; c += 2) {
+            const float a0 = __shfl_sync(0xffffffffu, fq[c], q);
+            const float a1 = __shfl_sync(0xffffffffu, fq[c + 1], q);
+            if (c == cp) { f0 = a0; f1 = a1; }
+          }
+          const float* po2 = p.part_o + (static_cast<int64_t>(u_first) + p0 + q + seg_id) * kHeadDim * NQP + nt * 8 + cp;
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(po2 + (k * 8 + (lane >> 2)) * NQP));
+            acc[k].x += f0 * v.x;
+            acc[k].y += f1 * v.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) Ls[c] += __shfl_xor_sync(0xffffffffu, Ls[c], o2);
+      float L0 = 0.f, L1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; c += 2)
+        if (c == cp) { L0 = Ls[c]; L1 = Ls[c + 1]; }
+      const float i0 = L0 > 0.f ? 1.f / L0 : 0.f, i1 = L1 > 0.f ? 1.f / L1 : 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int c = nt * 8 + cp + j;
+        if (c >= p.nq) continue;
+        const int qi = c / p.group, gi = c - qi * p.group;
+        T* dst = optr + ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) * kHeadDim;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          dst[k * 8 + (lane >> 2)] = from_f32<T>(j == 0 ? acc[k].x * i0 : acc[k].y * i1);
       }
     }
-    named_barrier_sync(1, kConsumerThreads);
-    g = piece_end;
+    if (lane == 0) p.counters[seg_id] = 0;
+  };
+
+  begin_segment();
+  int cur_batch = 0;
+  for (int j = 0; j < n_pages; ++j) {
+    const int64_t g = g0 + j;
+    if (g == seg_end) {
+      // next segment: close this piece, advance (sequence, head)
+      end_piece(g);
+      ++h;
+      if (h == Hkv) {
+        h = 0;
+        do { ++b; } while (prefix[b + 1] == prefix[b]);
+        L = seq_len_of(p, b, false);
+      }
+      pb = prefix[b + 1] - prefix[b];
+      seg_start = g;
+      seg_end = g + pb;
+      piece_start = g;
+      begin_segment();
+    }
+    if ((j >> 5) != cur_batch) {  // rotate the block-id batches
+      cur_batch = j >> 5;
+      rows_cur = rows_next;
+      const int nxt = (cur_batch + 1) * 32 + lane;
+      rows_next = nxt < n_pages ? row_of(g0 + nxt) : 0;
+    }
+    const int s = j % STAGES;
+    bool ok = !abort;
+    if (ok && !mbar_wait(&full[s], (j / STAGES) & 1u)) ok = false;
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (!ok) {
+      if (!abort && lane == 0) report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+      abort = true;
+    } else {
+      const uint32_t kbase = smem_u32(stages + s * kStageBytes);
+      const uint32_t vbase = kbase + 2 * kHalfBytes;
+      const int tok0 = static_cast<int>(g - seg_start) * kPage;
+
+      // S[token][col] = K Q^T (fp32); even and odd k-steps in separate accumulators
+      float sa[NT][4], sb[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sa[nt][e] = sb[nt][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int tok = ((msel & 1) << 3) + mrow;
+        const int ch = ((kk & 3) << 1) + (msel >> 1);
+        uint32_t a[4];
+        ldmatrix_x4(a, kbase + (kk >> 2) * kHalfBytes + tok * 128 + ((ch ^ (tok & 7)) << 4));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          if (kk & 1) mma_16816<kBf16>(sb[nt], a, qf[kk][nt][0], qf[kk][nt][1]);
+          else mma_16816<kBf16>(sa[nt], a, qf[kk][nt][0], qf[kk][nt][1]);
+        }
+      }
+
+      // scale to base 2, causal / length mask
+      const bool need_mask = tok0 + kPage - 1 > L - p.q_len;
+      const int t_lo = tok0 + (lane >> 2);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float v = (sa[nt][e] + sb[nt][e]) * p.scale_log2;
+          if (need_mask) {
+            const int t = t_lo + ((e >> 1) << 3);
+            if (t > lim[nt][e & 1]) v = -INFINITY;
+          }
+          sa[nt][e] = v;
+        }
+
+      // online softmax: column max over the 16 tokens (lanes sharing lane & 3)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          float mx = fmaxf(sa[nt][jj], sa[nt][jj + 2]);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float mnew = fmaxf(m[nt][jj], mx);
+          const float mref = mnew == -INFINITY ? 0.f : mnew;
+          const float alpha = ex2(m[nt][jj] - mref);
+          m[nt][jj] = mnew;
+          const float p0 = ex2(sa[nt][jj] - mref), p1 = ex2(sa[nt][jj + 2] - mref);
+          sa[nt][jj] = p0;
+          sa[nt][jj + 2] = p1;
+          l[nt][jj] = l[nt][jj] * alpha + p0 + p1;
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            o[mt][nt][jj] *= alpha;
+            o[mt][nt][jj + 2] *= alpha;
+          }
+        }
+
+      // P^T fragments (tokens x cols) in the working dtype
+      uint32_t pf[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        pf[nt][0] = movmatrix_trans(pack2<kBf16>(sa[nt][0], sa[nt][1]));
+        pf[nt][1] = movmatrix_trans(pack2<kBf16>(sa[nt][2], sa[nt][3]));
+      }
+
+      // O^T[d][col] += V^T P^T ; rows of V past the sequence end hold stale pool bytes
+      const bool vmask = tok0 + kPage > L;
+      const int ta = tok0 + 2 * (lane & 3);
+      const uint32_t m01 = (ta < L ? 0x0000ffffu : 0u) | (ta + 1 < L ? 0xffff0000u : 0u);
+      const uint32_t m23 = (ta + 8 < L ? 0x0000ffffu : 0u) | (ta + 9 < L ? 0xffff0000u : 0u);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int tok = ((msel >> 1) << 3) + mrow;
+        const int ch = ((mt & 3) << 1) + (msel & 1);
+        uint32_t a[4];
+        ldmatrix_x4_trans(a, vbase + (mt >> 2) * kHalfBytes + tok * 128 + ((ch ^ (tok & 7)) << 4));
+        if (vmask) {
+          a[0] &= m01;
+          a[1] &= m01;
+          a[2] &= m23;
+          a[3] &= m23;
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_16816<kBf16>(o[mt][nt], a, pf[nt][0], pf[nt][1]);
+      }
+    }
+    // refill the stage just consumed with page j + STAGES (the warp's reads of it are
+    // complete: every ldmatrix result has been consumed by an MMA above)
+    __syncwarp();
+    if (!abort && issued < n_pages) {
+      issue_page(issued, cur_batch);
+      ++issued;
+    }
+  }
+  // (also after an abort, so the ticket counters return to zero)
+  end_piece(g1);
+
+  // Drain: never leave the warp with a TMA write still in flight into its smem.
+  if (abort && lane == 0) {
+    for (int s = 0; s < STAGES && s < issued; ++s) {
+      const int rounds = (issued - s + STAGES - 1) / STAGES;
+      mbar_wait(&full[s], static_cast<uint32_t>((rounds - 1) & 1));
+    }
   }
 }
 
@@ -717,7 +715,8 @@ constexpr size_t kCounterRegionBytes =
 inline WorkspaceLayout workspace_layout(int num_seqs, int num_kv_heads, int nqp, int grid) {
   WorkspaceLayout w;
   const size_t segs = static_cast<size_t>(num_seqs) * num_kv_heads;
-  const size_t slots = static_cast<size_t>(grid) + segs;
+  // one partial slot per (warp unit, segment) index pair that can occur
+  const size_t slots = static_cast<size_t>(grid) * kWarps + segs;
   w.counters = 0;
   w.ml = kCounterRegionBytes;
   w.o = w.ml + align256(slots * nqp * 2 * sizeof(float));
@@ -727,10 +726,9 @@ inline WorkspaceLayout workspace_layout(int num_seqs, int num_kv_heads, int nqp,
 
 inline int fast_grid(int sm_count) { return sm_count * kCtasPerSm; }
 
-inline size_t fast_smem_bytes(int nqp, int num_seqs) {
-  return 1024 + static_cast<size_t>(kStages) * kStageBytes + nqp * kQRowBytes +
-         nqp * kHeadDim * 4 + kConsumerWarps * nqp * 2 * 4 + nqp * 2 * 4 + 2 * kStages * 8 +
-         (num_seqs + 1) * 4;
+inline size_t fast_smem_bytes(int num_seqs) {
+  return 1024 + static_cast<size_t>(kWarps) * kStagesPerWarp * (kStageBytes + 8) +
+         (static_cast<size_t>(num_seqs) + 1) * 4;
 }
 
 // Tensor map over one pool viewed as [num_blocks * num_kv_heads * 16 rows, 128 elements]
@@ -780,18 +778,18 @@ int pool_map(const void* pool, int64_t rows, CUtensorMap* out) {
   return INFERD_OK;
 }
 
-template <bool kBf16, int NT>
+template <bool kBf16, int NT, int STAGES = kStagesPerWarp>
 int launch_fast_t(const CUtensorMap& km, const CUtensorMap& vm, const FastParams& fp, int grid,
                   size_t smem, cudaStream_t s) {
   static bool configured[64] = {false};
   const int dev = current_device();
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(paged_attn_tc_kernel<kBf16, NT>,
+    cudaError_t e = cudaFuncSetAttribute(paged_attn_tc_kernel<kBf16, NT, STAGES>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return cuda_status(e);
     configured[dev] = true;
   }
-  paged_attn_tc_kernel<kBf16, NT><<<grid, (kConsumerWarps + 1) * 32, smem, s>>>(km, vm, fp);
+  paged_attn_tc_kernel<kBf16, NT, STAGES><<<grid, kWarps * 32, smem, s>>>(km, vm, fp);
   return launch_status();
 }
 
@@ -815,7 +813,8 @@ using namespace inferd;
 
 extern "C" size_t inferd_paged_attention_counter_bytes(int32_t num_seqs, int32_t num_kv_heads) {
   if (num_seqs <= 0 || num_kv_heads <= 0) return 0;
-  return align256(static_cast<size_t>(num_seqs) * num_kv_heads * sizeof(int32_t));
+  const size_t seqs = num_seqs < kMaxSeqsFast ? num_seqs : kMaxSeqsFast;
+  return align256(seqs * num_kv_heads * sizeof(int32_t));
 }
 
 extern "C" size_t inferd_paged_attention_workspace_bytes(int32_t num_seqs, int32_t q_len,
@@ -944,8 +943,9 @@ extern "C" int inferd_paged_attention(void* out, const void* query, const void* 
     const int64_t pages_ub = static_cast<int64_t>(nb) * num_kv_heads *
                              ((static_cast<int64_t>(max_context_len) + kPage - 1) / kPage);
     int g = grid;
-    if (pages_ub < g) g = pages_ub > 0 ? static_cast<int>(pages_ub) : 1;
-    const size_t smem = fast_smem_bytes(nqp, nb);
+    const int64_t ctas_ub = (pages_ub + kWarps - 1) / kWarps;  // one warp per page at most
+    if (ctas_ub < g) g = ctas_ub > 0 ? static_cast<int>(ctas_ub) : 1;
+    const size_t smem = fast_smem_bytes(nb);
     st = dtype == INFERD_BF16 ? launch_fast<true>(km, vm, fp, nqp / 8, g, smem, s)
                               : launch_fast<false>(km, vm, fp, nqp / 8, g, smem, s);
     if (st != INFERD_OK) return st;

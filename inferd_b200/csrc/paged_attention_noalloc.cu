@@ -7,7 +7,7 @@
 // a caller-provided workspace for its split partials and ticket counters; this entry
 // point instead uses a fixed scratch area that lives in the library itself.
 //
-// The scratch is one file-scope __device__ array of kNoAllocScratchBytes (16 MiB).
+// The scratch is one file-scope __device__ array of kNoAllocScratchBytes (32 MiB).
 // Every GPU that loads the library holds it until the process exits.  All calls on a
 // device share it and it keeps the previous call's contents, so:
 //   * each call clears the ticket counters at its head before launching;
@@ -21,7 +21,7 @@
 namespace inferd {
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = size_t{16} << 20;  // 16 MiB
+constexpr size_t kNoAllocScratchBytes = size_t{32} << 20;  // 32 MiB
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];

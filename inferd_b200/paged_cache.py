@@ -155,6 +155,25 @@ class PagedKVCache:
         self.allocator.free(table.blocks)
         del self.sequences[seq_id]
 
+    def truncate_sequence(self, seq_id: int, length: int) -> list[int]:
+        """Drop the tokens at positions >= length and free the blocks no longer needed.
+
+        This is the rollback of rejected speculative drafts. The reference crops its
+        contiguous cache with copies (core/spec_decode.py:48-57). Here no K/V byte moves:
+        the length drops, and whole blocks past the new end go back to the allocator in
+        table order. Returns the freed block ids.
+        """
+        table = self._table(seq_id)
+        if length < 0 or length > table.length:
+            raise ValueError(f"cannot truncate a sequence of length {table.length} to {length}")
+        keep = (length + self.block_size - 1) // self.block_size
+        freed = table.blocks[keep:]
+        if freed:
+            del table.blocks[keep:]
+            self.allocator.free(freed)
+        table.length = length
+        return freed
+
     def _reserve(self, table: SequencePageTable, n_tokens: int) -> list[int]:
         """Extend a page table to hold n_tokens more tokens (core/paged_cache.py:170-176)."""
         needed_capacity = table.length + n_tokens

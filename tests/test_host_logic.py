@@ -177,3 +177,22 @@ def test_decode_metadata_packing():
 def test_sequence_page_table_properties():
     t = SequencePageTable(seq_id=0, block_size=4, blocks=[3, 1], length=5)
     assert t.block_count == 2 and t.capacity_tokens == 8 and t.free_slots == 3
+
+
+def test_truncate_sequence_rolls_back_without_copies():
+    cache = RecordingCache(num_layers=1, num_blocks=8, block_size=4, num_kv_heads=1, head_dim=1,
+                           dtype=torch.float32)
+    cache.create_sequence(0)
+    cache.append_tokens(0, [torch.zeros(10, 1, 1)], [torch.zeros(10, 1, 1)])
+    assert cache.sequences[0].blocks == [0, 1, 2]
+    n_writes = len(cache.writes)
+    assert cache.truncate_sequence(0, 5) == [2]
+    assert cache.sequence_length(0) == 5 and cache.sequences[0].blocks == [0, 1]
+    assert len(cache.writes) == n_writes          # no K/V movement
+    assert cache.truncate_sequence(0, 5) == []
+    with pytest.raises(ValueError):
+        cache.truncate_sequence(0, 6)
+    cache.append_tokens(0, [torch.zeros(4, 1, 1)], [torch.zeros(4, 1, 1)])
+    assert cache.sequences[0].blocks == [0, 1, 2]  # the freed block is reused first
+    assert cache.writes[-1][1] == [5, 6, 7, 8]
+    cache.assert_consistent()
