@@ -163,6 +163,31 @@ INFERD_API int inferd_dense_attention(void* out, const void* query, const void* 
                            int32_t num_kv_heads, int32_t head_dim, float scale, int32_t dtype,
                            void* stream);
 
+/*
+ * Load-time FP8 weight quantisation, per output channel: s[n] = max_k |W[n, k]| / 448 in
+ * fp32 (1 for an all-zero row) and w_e4m3[n, k] = e4m3(W[n, k] / s[n]), IEEE division,
+ * round-to-nearest-even, saturating.  Replaces torchao 0.17.0 Float8WeightOnlyConfig as
+ * configured in bench/model_loader.py:46-58 (applied at :82-88).  w_dtype: f32/f16/bf16.
+ */
+INFERD_API int inferd_fp8_quantize_per_channel(const void* w, int32_t w_dtype, void* w_e4m3,
+                                               float* w_scale, int64_t n, int64_t k,
+                                               void* stream);
+
+/*
+ * y[m, n] = s[n] * sum_k x[m, k] * w_e4m3[n, k]: x bf16 [M, K], w_e4m3 [N, K] (16-byte
+ * aligned), w_scale fp32 [N], y bf16 [M, N], all row-major; K % 16 == 0.  The FP8
+ * weight-only linear the reference runs through torchao (bench/model_loader.py:46-58;
+ * caller core/model_runner.py:27-45).  tcgen05 kind::f8f6f4 tensor cores with the
+ * activations split exactly into two e4m3 planes under a power-of-two row scale.
+ * workspace >= inferd_fp8_linear_workspace_bytes(m, n, k, device), 256-byte aligned.
+ */
+INFERD_API int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3,
+                                 const float* w_scale, int64_t m, int64_t n, int64_t k,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+INFERD_API size_t inferd_fp8_linear_workspace_bytes(int64_t m, int64_t n, int64_t k,
+                                                    int32_t device);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,106 @@
+"""GPU parity of the FP8 weight-only linear (tcgen05) and its load-time quantiser.
+
+Quantisation (scales and e4m3 codes) must be bit-exact with the oracle, which is pinned to
+torch's float8_e4m3fn cast.  The linear must be within 1e-2 relative of the oracle's
+dequant-then-matmul: max |y - y_ref| <= 1e-2 * max |y_ref| and
+||y - y_ref||_F <= 1e-2 * ||y_ref||_F.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from inferd_b200.fp8_linear import Fp8Linear, fp8_linear, quantize_fp8_per_channel, quantize_model_fp8
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-2
+
+
+def assert_linear_close(y: np.ndarray, ref: np.ndarray, what: str) -> None:
+    err = np.abs(y - ref)
+    scale = float(np.abs(ref).max())
+    assert float(err.max()) <= RTOL * scale, f"{what}: max err {err.max()} vs max |ref| {scale}"
+    fro = float(np.linalg.norm(y - ref) / max(np.linalg.norm(ref), 1e-30))
+    assert fro <= RTOL, f"{what}: relative Frobenius error {fro}"
+
+
+def test_quantize_matches_golden_and_oracle(cuda_device, golden):
+    w = torch.from_numpy(golden["fp8_w"]).to(torch.bfloat16).to(cuda_device)
+    q, s = quantize_fp8_per_channel(w)
+    assert np.array_equal(s.cpu().numpy(), golden["fp8_scale"])
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy(), golden["fp8_q"])
+    g = torch.Generator().manual_seed(3)
+    for dtype in (torch.bfloat16, torch.float16, torch.float32):
+        w = (torch.randn(300, 1000, generator=g) * 0.02).to(dtype)
+        w[7] = 0
+        q, s = quantize_fp8_per_channel(w.to(cuda_device))
+        q_ref, s_ref = oracle.quantize_per_channel(w.float().numpy())
+        assert np.array_equal(s.cpu().numpy(), s_ref)
+        assert np.array_equal(q.view(torch.uint8).cpu().numpy(), q_ref)
+
+
+@pytest.mark.parametrize("m", [1, 3, 8, 16, 32, 100, 128, 256, 300])
+def test_fp8_linear_matches_dequant_matmul(cuda_device, m):
+    g = torch.Generator().manual_seed(10 + m)
+    n, k = 1000, 640   # partial last weight tile (1000 = 7 * 128 + 104)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    q, s = quantize_fp8_per_channel(w.to(cuda_device))
+    y = fp8_linear(x.to(cuda_device), q, s)
+    torch.cuda.synchronize()
+    ref = oracle.fp8_linear(x.float().numpy(), q.view(torch.uint8).cpu().numpy(), s.cpu().numpy())
+    assert y.shape == (m, n) and y.dtype == torch.bfloat16
+    assert_linear_close(y.float().cpu().numpy(), ref, f"m={m}")
+
+
+@pytest.mark.parametrize("m", [1, 8, 256])
+def test_fp8_linear_config4_shape(cuda_device, m):
+    # config-4 weight: N = 17408, K = 5120, N(0, 0.02) quantised per channel
+    g = torch.Generator().manual_seed(4)
+    n, k = 17408, 5120
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    q, s = quantize_fp8_per_channel(w.to(cuda_device))
+    y = fp8_linear(x.to(cuda_device), q, s)
+    torch.cuda.synchronize()
+    rows = slice(0, n) if m <= 8 else slice(0, 2048)  # keep the float64 oracle to seconds
+    ref = oracle.fp8_linear(x.float().numpy(), q.view(torch.uint8).cpu().numpy()[rows],
+                            s.cpu().numpy()[rows])
+    assert_linear_close(y.float().cpu().numpy()[:, rows], ref, f"config 4, m={m}")
+
+
+def test_fp8_linear_leading_dims_bias_and_outliers(cuda_device):
+    g = torch.Generator().manual_seed(5)
+    w = (torch.randn(256, 512, generator=g) * 0.05).to(torch.bfloat16)
+    x = torch.randn(2, 3, 512, generator=g)
+    x[0, 1, 17] = 900.0     # activation outlier: the per-row power-of-two scale absorbs it
+    x[1, 2] = 0.0           # an all-zero row
+    x = x.to(torch.bfloat16)
+    bias = torch.randn(256, generator=g).to(torch.bfloat16)
+    q, s = quantize_fp8_per_channel(w.to(cuda_device))
+    y = fp8_linear(x.to(cuda_device), q, s, bias.to(cuda_device))
+    ref = oracle.fp8_linear(x.reshape(6, 512).float().numpy(), q.view(torch.uint8).cpu().numpy(),
+                            s.cpu().numpy()) + bias.float().numpy()
+    assert y.shape == (2, 3, 256)
+    assert_linear_close(y.reshape(6, 256).float().cpu().numpy(), ref, "leading dims")
+    assert torch.all(y[1, 2] == bias.to(cuda_device))
+
+
+def test_quantize_model_keeps_lm_head(cuda_device):
+    model = torch.nn.Sequential()
+    model.add_module("proj", torch.nn.Linear(128, 256, bias=False))
+    model.add_module("lm_head", torch.nn.Linear(256, 64, bias=False))
+    model = model.to(cuda_device).to(torch.bfloat16)
+    x = torch.randn(4, 128, device=cuda_device, dtype=torch.bfloat16)
+    with torch.no_grad():
+        ref = model(x).float()
+        quantize_model_fp8(model)
+        assert isinstance(model.proj, Fp8Linear)
+        assert isinstance(model.lm_head, torch.nn.Linear)
+        out = model(x).float()
+    rel = float((out - ref).norm() / ref.norm())
+    assert rel < 5e-2  # weight quantisation error, not a kernel tolerance
