@@ -105,7 +105,7 @@ INFERD_API int inferd_gather_paged_kv(void* key_out, void* value_out,
  * max_context_len keys".  max_context_len is a host-side upper bound used for grid sizing.
  * A sequence with no visible keys gets an all-zero output row (softmax over nothing).
  * workspace: >= inferd_paged_attention_workspace_bytes(...) bytes, 256-byte aligned.  It
- * starts with a fixed 2 MiB ticket-counter region (partials are stored after it, whatever
+ * starts with a fixed 512 KiB ticket-counter region (partials are stored after it, whatever
  * the call's shape); the first inferd_paged_attention_counter_bytes(num_seqs,
  * num_kv_heads) bytes of that region are used by a call, must be zero before it, and are
  * left zero by every completed call -- zero the region once when the workspace is
@@ -174,16 +174,29 @@ INFERD_API int inferd_fp8_quantize_per_channel(const void* w, int32_t w_dtype, v
                                                void* stream);
 
 /*
- * y[m, n] = s[n] * sum_k x[m, k] * w_e4m3[n, k]: x bf16 [M, K], w_e4m3 [N, K] (16-byte
- * aligned), w_scale fp32 [N], y bf16 [M, N], all row-major; K % 16 == 0.  The FP8
- * weight-only linear the reference runs through torchao (bench/model_loader.py:46-58;
- * caller core/model_runner.py:27-45).  tcgen05 kind::f8f6f4 tensor cores with the
- * activations split exactly into two e4m3 planes under a power-of-two row scale.
+ * Load-time repacking of row-major e4m3 weights [N, K] into the tile layout the linear
+ * streams fastest: every 128-row x 128-byte tile is one contiguous 16 KiB block (already
+ * in the MMA's 128-byte-swizzled form), the tiles of a 128-row band consecutive along K,
+ * zero-filled past N and K.  w_packed needs inferd_fp8_packed_weight_bytes(n, k) bytes,
+ * 16-byte aligned.  No counterpart in the reference (its torchao weights stay row-major).
+ */
+INFERD_API size_t inferd_fp8_packed_weight_bytes(int64_t n, int64_t k);
+INFERD_API int inferd_fp8_pack_weights(const void* w_e4m3, void* w_packed, int64_t n, int64_t k,
+                                       void* stream);
+
+/*
+ * y[m, n] = s[n] * sum_k x[m, k] * w[n, k]: x bf16 [M, K], w_scale fp32 [N], y bf16 [M, N],
+ * row-major; K % 16 == 0.  w_layout 0: w_e4m3 row-major [N, K]; 1: packed by
+ * inferd_fp8_pack_weights.  w must be 16-byte aligned.  The FP8 weight-only linear the
+ * reference runs through torchao (bench/model_loader.py:46-58; caller
+ * core/model_runner.py:27-45).  tcgen05 kind::f8f6f4 tensor cores with the activations
+ * split exactly into two e4m3 planes under a power-of-two row scale.
  * workspace >= inferd_fp8_linear_workspace_bytes(m, n, k, device), 256-byte aligned.
  */
 INFERD_API int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3,
                                  const float* w_scale, int64_t m, int64_t n, int64_t k,
-                                 void* workspace, size_t workspace_bytes, void* stream);
+                                 int32_t w_layout, void* workspace, size_t workspace_bytes,
+                                 void* stream);
 
 INFERD_API size_t inferd_fp8_linear_workspace_bytes(int64_t m, int64_t n, int64_t k,
                                                     int32_t device);

@@ -66,7 +66,10 @@ _SIGNATURES = {
     "inferd_fp8_quantize_per_channel": (ctypes.c_int, [
         _c_void_p, _i32, _c_void_p, _c_void_p, _i64, _i64, _c_void_p]),
     "inferd_fp8_linear": (ctypes.c_int, [
-        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _sz, _c_void_p]),
+        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p, _sz,
+        _c_void_p]),
+    "inferd_fp8_packed_weight_bytes": (_sz, [_i64, _i64]),
+    "inferd_fp8_pack_weights": (ctypes.c_int, [_c_void_p, _c_void_p, _i64, _i64, _c_void_p]),
     "inferd_fp8_linear_workspace_bytes": (_sz, [_i64, _i64, _i64, _i32]),
 }
 

@@ -14,6 +14,13 @@
 // multiplied with the same weight tile into one fp32 TMEM accumulator.  The weights are
 // read by TMA straight from HBM in their stored e4m3 form; nothing converts them.
 //
+// Weight layouts.  Row-major [N, K] e4m3 is read by TMA 128 bytes per row per stage.
+// The packed layout produced once at load time stores every 128-row x 128-byte tile as
+// one contiguous 16 KiB block, already in the 128-byte-swizzled shared-memory form the
+// MMA reads, tiles of one 128-row band consecutive along K -- so each CTA streams one
+// contiguous region with 16 KiB bulk copies (the row-major form's 128-byte pieces at a
+// 5 KiB stride use HBM pages poorly).  Tiles past N or K are zero-filled.
+//
 // Kernel layout (swap-AB): the MMA's M = 128 is the weight rows n, its N is the token
 // count m (16..256), so small decode batches do not pad to 128.  One CTA owns 128 weight
 // rows: warp 0 streams weight and activation tiles with TMA into a shared-memory ring,
@@ -21,6 +28,7 @@
 // all four warps run the epilogue (tcgen05.ld, scale by s_w[n] * 2^e[m], bf16 store).
 #include <cuda_fp8.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -64,6 +72,14 @@ __device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Programmatic dependent launch: the GEMM may start while the activation split still
+// runs; griddepcontrol.wait blocks until the split grid has finished and its writes are
+// visible, launch_dependents lets the dependent grid be scheduled early.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // mbarrier arrives when every tcgen05.mma issued so far by this thread has completed
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -105,6 +121,7 @@ __host__ __device__ constexpr uint32_t f8_idesc(int n) {
 }
 
 struct Fp8Params {
+  const uint8_t* w_packed;  // packed weight tiles (nullptr: row-major through wmap)
   __nv_bfloat16* y;      // [M, N]
   const float* w_scale;  // [N]
   const float* x_scale;  // [M] (powers of two)
@@ -136,8 +153,16 @@ __global__ void __launch_bounds__(kThreadsFp8, 1)
   const uint32_t x_bytes = static_cast<uint32_t>(T) * kTileK;
   const uint32_t stage_bytes = w_bytes + 2 * x_bytes;  // multiple of 1024
   const int k_steps = (p.k + kTileK - 1) / kTileK;
-  uint32_t ncols = 32;
-  while (ncols < static_cast<uint32_t>(T)) ncols <<= 1;
+  // Accumulator plan.  With T <= 128 the h and l tiles (adjacent in shared memory) form
+  // one B operand of N = 2T rows, so one MMA covers both planes; consecutive MMAs rotate
+  // over `chains` independent accumulators so they do not wait on each other.  With
+  // T = 256 (N would exceed 256) h and l go to two accumulators of 256 columns.
+  const bool merged = T <= 128;
+  const int n_mma = merged ? 2 * T : T;
+  int chains = merged ? 512 / n_mma : 1;
+  if (chains > 4) chains = 4;
+  uint32_t ncols = 32;  // tcgen05.alloc takes a power of two >= 32 (<= 512 here)
+  while (ncols < (merged ? static_cast<uint32_t>(chains * n_mma) : 512u)) ncols <<= 1;
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -160,16 +185,35 @@ __global__ void __launch_bounds__(kThreadsFp8, 1)
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer
-    prefetch_tensormap(&wmap);
+    if (p.w_packed == nullptr) prefetch_tensormap(&wmap);
     prefetch_tensormap(&hmap);
     prefetch_tensormap(&lmap);
     const uint64_t pol_w = l2_policy_evict_first();
     uint64_t pol_x;
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_x));
-    for (int ks = 0; ks < k_steps; ++ks) {
+    const uint8_t* wband = p.w_packed + static_cast<int64_t>(blockIdx.x) * k_steps * w_bytes;
+    auto load_w = [&](uint8_t* st, int ks, uint64_t* bar) {
+      if (p.w_packed != nullptr) bulk_load(st, wband + static_cast<int64_t>(ks) * w_bytes, w_bytes, bar, pol_w);
+      else tma_load_2d(st, &wmap, ks * kTileK, n0, bar, pol_w);
+    };
+    // The weight tiles of the first ring do not depend on the activation split: issue
+    // them before waiting for it.
+    const int first = k_steps < S ? k_steps : S;
+    for (int ks = 0; ks < first; ++ks) {
+      uint8_t* st = smem + ks * stage_bytes;
+      mbar_arrive_expect_tx(&full[ks], stage_bytes);
+      load_w(st, ks, &full[ks]);
+    }
+    grid_dependency_wait();
+    for (int ks = 0; ks < first; ++ks) {
+      uint8_t* st = smem + ks * stage_bytes;
+      tma_load_2d(st + w_bytes, &hmap, ks * kTileK, p.tok0, &full[ks], pol_x);
+      tma_load_2d(st + w_bytes + x_bytes, &lmap, ks * kTileK, p.tok0, &full[ks], pol_x);
+    }
+    for (int ks = first; ks < k_steps; ++ks) {
       const int s = ks % S;
       const uint32_t round = ks / S;
-      if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1u)) {
+      if (!mbar_wait(&empty[s], (round - 1) & 1u)) {
         report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
         *vabort = 1;
         break;
@@ -177,13 +221,14 @@ __global__ void __launch_bounds__(kThreadsFp8, 1)
       if (*vabort) break;
       uint8_t* st = smem + s * stage_bytes;
       mbar_arrive_expect_tx(&full[s], stage_bytes);
-      tma_load_2d(st, &wmap, ks * kTileK, n0, &full[s], pol_w);
+      load_w(st, ks, &full[s]);
       tma_load_2d(st + w_bytes, &hmap, ks * kTileK, p.tok0, &full[s], pol_x);
       tma_load_2d(st + w_bytes + x_bytes, &lmap, ks * kTileK, p.tok0, &full[s], pol_x);
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer (one thread)
-    const uint32_t idesc = f8_idesc(T);
+    const uint32_t idesc = f8_idesc(n_mma);
+    int issued = 0;  // MMAs issued so far (selects the accumulator chain)
     for (int ks = 0; ks < k_steps; ++ks) {
       const int s = ks % S;
       if (*vabort || !mbar_wait(&full[s], (ks / S) & 1u)) {
@@ -197,8 +242,15 @@ __global__ void __launch_bounds__(kThreadsFp8, 1)
 #pragma unroll
       for (int kk = 0; kk < kTileK / kMmaK; ++kk) {
         const uint64_t ad = sw128_desc(a0 + kk * kMmaK);
-        mma_f8(tmem, ad, sw128_desc(h0 + kk * kMmaK), idesc, (ks | kk) != 0);
-        mma_f8(tmem, ad, sw128_desc(l0 + kk * kMmaK), idesc, 1u);
+        if (merged) {
+          const int c = issued % chains;
+          mma_f8(tmem + static_cast<uint32_t>(c * n_mma), ad, sw128_desc(h0 + kk * kMmaK), idesc,
+                 issued >= chains);
+        } else {
+          mma_f8(tmem, ad, sw128_desc(h0 + kk * kMmaK), idesc, issued > 0);
+          mma_f8(tmem + 256u, ad, sw128_desc(l0 + kk * kMmaK), idesc, issued > 0);
+        }
+        ++issued;
       }
       mma_commit(&empty[s]);  // stage s free once these MMAs have read it
     }
@@ -207,21 +259,37 @@ __global__ void __launch_bounds__(kThreadsFp8, 1)
   __syncwarp();
 
   // ---------------- epilogue: all four warps, TMEM lanes 32*warp .. 32*warp+31
+  grid_dependency_wait();  // x_scale comes from the split grid
   bool ok = mbar_wait(&acc_full, 0);
   if (!ok) report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
   tc_fence_after();
   const int n = n0 + warp * 32 + lane;
   const float sw = (ok && n < p.n) ? __ldg(p.w_scale + n) : 0.f;
+  // with fewer MMAs than chains (tiny K) the unused chains were never written
+  const int live_chains = merged ? (k_steps * (kTileK / kMmaK) < chains ? k_steps * (kTileK / kMmaK) : chains) : 1;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
   for (int c0 = 0; c0 < T; c0 += 16) {
-    uint32_t r[16];
-    tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, r);
-    tmem_ld_wait();
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+    // sum the h and l partials of every chain: columns c*n_mma + m (h) and + T + m (l),
+    // or 0 + m (h) and 256 + m (l) when the planes have their own accumulators
+    const int parts = merged ? 2 * live_chains : 2;
+    for (int q = 0; q < parts; ++q) {
+      const uint32_t col = merged ? static_cast<uint32_t>((q >> 1) * n_mma + (q & 1) * T + c0)
+                                  : static_cast<uint32_t>((q & 1) * 256 + c0);
+      uint32_t r[16];
+      tmem_ld16(lane_base + col, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[j] += __uint_as_float(r[j]);
+    }
     if (ok && n < p.n) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int m = p.tok0 + c0 + j;
         if (m < p.m) {
-          const float v = __uint_as_float(r[j]) * sw * __ldg(p.x_scale + m);
+          const float v = acc[j] * sw * __ldg(p.x_scale + m);
           p.y[static_cast<int64_t>(m) * p.n + n] = __float2bfloat16_rn(v);
         }
       }
@@ -253,19 +321,54 @@ __device__ __forceinline__ float from_e4m3(uint8_t c) {
   return __half2float(__half(hr));
 }
 
-__global__ void __launch_bounds__(256) split_activations_kernel(const __nv_bfloat16* __restrict__ x, int k,
-                                                                uint8_t* __restrict__ h, uint8_t* __restrict__ l,
-                                                                float* __restrict__ x_scale) {
-  __shared__ float red[8];
+// One CTA per token row.  Each thread holds up to kSplitRegs groups of 8 bf16 in registers
+// (16-byte loads), so the row is read from global memory once when K <= 256 * 8 * 4.
+constexpr int kSplitThreads = 256;
+constexpr int kSplitRegs = 4;
+
+__device__ __forceinline__ uint32_t split_pair(float a, float b, uint32_t& lo_out) {
+  // returns h codes of (a, b) in the low 16 bits; l codes in lo_out
+  const uint8_t ha = to_e4m3(a), hb = to_e4m3(b);
+  const uint8_t la = to_e4m3(a - from_e4m3(ha)), lb = to_e4m3(b - from_e4m3(hb));
+  lo_out = static_cast<uint32_t>(la) | (static_cast<uint32_t>(lb) << 8);
+  return static_cast<uint32_t>(ha) | (static_cast<uint32_t>(hb) << 8);
+}
+
+__global__ void __launch_bounds__(kSplitThreads) split_activations_kernel(const __nv_bfloat16* __restrict__ x, int k,
+                                                                         uint8_t* __restrict__ h, uint8_t* __restrict__ l,
+                                                                         float* __restrict__ x_scale) {
+  __shared__ float red[kSplitThreads / 32];
+  grid_launch_dependents();
   const int m = blockIdx.x;
   const __nv_bfloat16* row = x + static_cast<int64_t>(m) * k;
+  const int groups = k / 8;  // k % 16 == 0
+  uint4 keep[kSplitRegs];
   float amax = 0.f;
-  for (int i = threadIdx.x; i < k; i += blockDim.x) amax = fmaxf(amax, fabsf(__bfloat162float(row[i])));
+#pragma unroll
+  for (int r = 0; r < kSplitRegs; ++r) {
+    const int gidx = threadIdx.x + r * kSplitThreads;
+    keep[r] = make_uint4(0, 0, 0, 0);
+    if (gidx < groups) keep[r] = __ldg(reinterpret_cast<const uint4*>(row) + gidx);
+  }
+  auto group_max = [](const uint4& v) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float a = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      a = fmaxf(a, fabsf(__uint_as_float(w[j] << 16)));
+      a = fmaxf(a, fabsf(__uint_as_float(w[j] & 0xffff0000u)));
+    }
+    return a;
+  };
+#pragma unroll
+  for (int r = 0; r < kSplitRegs; ++r) amax = fmaxf(amax, group_max(keep[r]));
+  for (int gidx = threadIdx.x + kSplitRegs * kSplitThreads; gidx < groups; gidx += kSplitThreads)
+    amax = fmaxf(amax, group_max(*reinterpret_cast<const uint4*>(row + gidx * 8)));
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   amax = 0.f;
-  for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) amax = fmaxf(amax, red[w]);
+  for (int w = 0; w < kSplitThreads / 32; ++w) amax = fmaxf(amax, red[w]);
   // smallest power of two 2^e with amax * 2^-e <= 448: amax = f 2^ex, f in [0.5, 1),
   // 448 = 0.875 * 2^9
   int e = 0;
@@ -275,13 +378,31 @@ __global__ void __launch_bounds__(256) split_activations_kernel(const __nv_bfloa
     e = ex - 9 + (f > 0.875f ? 1 : 0);
   }
   const float inv = ldexpf(1.f, -e);
-  for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    const float v = __bfloat162float(row[i]) * inv;  // exact: power-of-two scaling
-    const uint8_t hc = to_e4m3(v);
-    const uint8_t lc = to_e4m3(v - from_e4m3(hc));
-    h[static_cast<int64_t>(m) * k + i] = hc;
-    l[static_cast<int64_t>(m) * k + i] = lc;
+  auto emit = [&](const uint4& v, int gidx) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t hw[2], lw[2];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t l0, l1;
+      // exact: power-of-two scaling of bf16 values
+      const uint32_t h0 = split_pair(__uint_as_float(w[2 * half] << 16) * inv,
+                                     __uint_as_float(w[2 * half] & 0xffff0000u) * inv, l0);
+      const uint32_t h1 = split_pair(__uint_as_float(w[2 * half + 1] << 16) * inv,
+                                     __uint_as_float(w[2 * half + 1] & 0xffff0000u) * inv, l1);
+      hw[half] = h0 | (h1 << 16);
+      lw[half] = l0 | (l1 << 16);
+    }
+    const int64_t off = static_cast<int64_t>(m) * k + gidx * 8;
+    *reinterpret_cast<uint2*>(h + off) = make_uint2(hw[0], hw[1]);
+    *reinterpret_cast<uint2*>(l + off) = make_uint2(lw[0], lw[1]);
+  };
+#pragma unroll
+  for (int r = 0; r < kSplitRegs; ++r) {
+    const int gidx = threadIdx.x + r * kSplitThreads;
+    if (gidx < groups) emit(keep[r], gidx);
   }
+  for (int gidx = threadIdx.x + kSplitRegs * kSplitThreads; gidx < groups; gidx += kSplitThreads)
+    emit(*reinterpret_cast<const uint4*>(row + gidx * 8), gidx);
   if (threadIdx.x == 0) x_scale[m] = ldexpf(1.f, e);
 }
 
@@ -306,6 +427,36 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
   if (threadIdx.x == 0) scale[n] = s;
 }
 
+// ---------------------------------------------------------------- weight packing
+// packed[(nt * KT + kt) * 16384 + r * 128 + ((c16 ^ (r & 7)) * 16) + b] =
+//     q[nt * 128 + r, kt * 128 + c16 * 16 + b]   (zero outside [N, K])
+__global__ void __launch_bounds__(256) pack_weights_kernel(const uint8_t* __restrict__ q, int64_t n, int64_t k,
+                                                           int64_t kt_count, uint4* __restrict__ packed,
+                                                           int64_t chunks) {
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < chunks; i += step) {
+    const int64_t tile = i >> 10;               // 1024 chunks of 16 B per tile
+    const int within = static_cast<int>(i & 1023);
+    const int r = within >> 3, cpos = within & 7;
+    const int c16 = cpos ^ (r & 7);             // logical 16-byte chunk stored at cpos
+    const int64_t nt = tile / kt_count, kt = tile - nt * kt_count;
+    const int64_t row = nt * kTileN + r;
+    const int64_t col = kt * kTileK + c16 * 16;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < n && col < k) {
+      const uint8_t* src = q + row * k + col;
+      if (col + 16 <= k && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        v = *reinterpret_cast<const uint4*>(src);
+      } else {
+        __align__(16) uint8_t tmp[16];
+        for (int b = 0; b < 16; ++b) tmp[b] = (col + b < k) ? src[b] : 0;
+        v = *reinterpret_cast<const uint4*>(tmp);
+      }
+    }
+    packed[i] = v;
+  }
+}
+
 // ---------------------------------------------------------------- host side
 inline int encode_u8_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                          uint32_t box_rows) {
@@ -319,6 +470,49 @@ inline int encode_u8_map(CUtensorMap* map, const void* base, uint64_t rows, uint
                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? INFERD_OK : INFERD_ERR_CUDA;
+}
+
+// Small cache of encoded tensor maps keyed by (base, rows, cols, box rows, device):
+// encoding costs microseconds of host time per map.
+struct U8MapCache {
+  std::mutex mu;
+  struct Entry {
+    const void* base;
+    uint64_t rows, cols;
+    uint32_t box_rows;
+    int dev;
+    CUtensorMap map;
+  } e[32];
+  int n = 0, next = 0;
+};
+U8MapCache g_u8maps;
+
+inline int cached_u8_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                         uint32_t box_rows) {
+  const int dev = current_device();
+  {
+    std::lock_guard<std::mutex> lock(g_u8maps.mu);
+    for (int i = 0; i < g_u8maps.n; ++i) {
+      const U8MapCache::Entry& c = g_u8maps.e[i];
+      if (c.base == base && c.rows == rows && c.cols == cols && c.box_rows == box_rows && c.dev == dev) {
+        *map = c.map;
+        return INFERD_OK;
+      }
+    }
+  }
+  const int st = encode_u8_map(map, base, rows, cols, box_rows);
+  if (st != INFERD_OK) return st;
+  std::lock_guard<std::mutex> lock(g_u8maps.mu);
+  U8MapCache::Entry& c = g_u8maps.e[g_u8maps.next];
+  c.base = base;
+  c.rows = rows;
+  c.cols = cols;
+  c.box_rows = box_rows;
+  c.dev = dev;
+  c.map = *map;
+  g_u8maps.next = (g_u8maps.next + 1) % 32;
+  if (g_u8maps.n < 32) ++g_u8maps.n;
+  return INFERD_OK;
 }
 
 inline size_t align256_fp8(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
@@ -369,14 +563,37 @@ extern "C" int inferd_fp8_quantize_per_channel(const void* w, int32_t w_dtype, v
   return launch_status();
 }
 
+extern "C" size_t inferd_fp8_packed_weight_bytes(int64_t n, int64_t k) {
+  if (n <= 0 || k <= 0) return 0;
+  const int64_t nt = (n + kTileN - 1) / kTileN, kt = (k + kTileK - 1) / kTileK;
+  return static_cast<size_t>(nt * kt) * kTileN * kTileK;
+}
+
+extern "C" int inferd_fp8_pack_weights(const void* w_e4m3, void* w_packed, int64_t n, int64_t k, void* stream) {
+  if (n <= 0 || k <= 0) return INFERD_ERR_INVALID_ARGUMENT;
+  if (!w_e4m3 || !w_packed || (reinterpret_cast<uintptr_t>(w_packed) & 15) != 0)
+    return INFERD_ERR_INVALID_ARGUMENT;
+  const int64_t kt = (k + kTileK - 1) / kTileK;
+  const int64_t chunks = static_cast<int64_t>(inferd_fp8_packed_weight_bytes(n, k)) / 16;
+  int64_t blocks = (chunks + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(current_sm_count()) * 32;
+  if (blocks > cap) blocks = cap;
+  pack_weights_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(w_e4m3), n, k, kt, static_cast<uint4*>(w_packed), chunks);
+  return launch_status();
+}
+
 extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, const float* w_scale, int64_t m,
-                                 int64_t n, int64_t k, void* workspace, size_t workspace_bytes, void* stream) {
+                                 int64_t n, int64_t k, int32_t w_layout, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (w_layout != 0 && w_layout != 1) return INFERD_ERR_INVALID_ARGUMENT;
   if (m < 0 || n <= 0 || k <= 0) return INFERD_ERR_INVALID_ARGUMENT;
   if (m == 0) return INFERD_OK;
   if (!y || !x || !w_e4m3 || !w_scale) return INFERD_ERR_INVALID_ARGUMENT;
   if (k % 16 != 0) return INFERD_ERR_UNSUPPORTED;  // TMA rows must be 16-byte multiples
   if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return INFERD_ERR_UNSUPPORTED;
-  if ((reinterpret_cast<uintptr_t>(w_e4m3) & 15) != 0) return INFERD_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(w_e4m3) & 15) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
+    return INFERD_ERR_INVALID_ARGUMENT;  // 16-byte aligned weights and activations
   const Fp8Workspace wl = fp8_workspace(m, k);
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0 || workspace_bytes < wl.total)
     return INFERD_ERR_WORKSPACE;
@@ -385,11 +602,6 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
   uint8_t* h = ws + wl.h;
   uint8_t* l = ws + wl.l;
   float* xs = reinterpret_cast<float*>(ws + wl.scale);
-
-  split_activations_kernel<<<static_cast<unsigned>(m), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
-                                                                   static_cast<int>(k), h, l, xs);
-  int st = launch_status();
-  if (st != INFERD_OK) return st;
 
   static bool configured[64] = {false};
   const int dev = current_device();
@@ -400,36 +612,64 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
     configured[dev] = true;
   }
 
+  // encode every tensor map before the first launch so no host work separates the two
+  // kernels
+  const int n_tok_tiles = static_cast<int>((m + kMaxTokTile - 1) / kMaxTokTile);
   CUtensorMap wmap;
-  st = encode_u8_map(&wmap, w_e4m3, static_cast<uint64_t>(n), static_cast<uint64_t>(k), kTileN);
+  int st = INFERD_OK;
+  if (w_layout == 0) {
+    st = cached_u8_map(&wmap, w_e4m3, static_cast<uint64_t>(n), static_cast<uint64_t>(k), kTileN);
+    if (st != INFERD_OK) return st;
+  } else {
+    memset(&wmap, 0, sizeof(wmap));  // unused: packed tiles are bulk-copied
+  }
+  CUtensorMap hmaps[2], lmaps[2];  // full tiles share one map; a last partial tile its own
+  int tiles[2];
+  for (int i = 0; i < 2; ++i) {
+    const int64_t rem = i == 0 ? (m < kMaxTokTile ? m : kMaxTokTile) : m - static_cast<int64_t>(n_tok_tiles - 1) * kMaxTokTile;
+    tiles[i] = static_cast<int>((rem + 15) / 16 * 16);
+    st = cached_u8_map(&hmaps[i], h, static_cast<uint64_t>(m), static_cast<uint64_t>(k), static_cast<uint32_t>(tiles[i]));
+    if (st != INFERD_OK) return st;
+    st = cached_u8_map(&lmaps[i], l, static_cast<uint64_t>(m), static_cast<uint64_t>(k), static_cast<uint32_t>(tiles[i]));
+    if (st != INFERD_OK) return st;
+  }
+
+  split_activations_kernel<<<static_cast<unsigned>(m), kSplitThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                                   static_cast<int>(k), h, l, xs);
+  st = launch_status();
   if (st != INFERD_OK) return st;
+
   const unsigned grid = static_cast<unsigned>((n + kTileN - 1) / kTileN);
-  for (int64_t t0 = 0; t0 < m; t0 += kMaxTokTile) {
-    const int64_t rem = m - t0;
-    const int tile = static_cast<int>(((rem < kMaxTokTile ? rem : kMaxTokTile) + 15) / 16 * 16);
-    CUtensorMap hmap, lmap;
-    st = encode_u8_map(&hmap, h, static_cast<uint64_t>(m), static_cast<uint64_t>(k), static_cast<uint32_t>(tile));
-    if (st != INFERD_OK) return st;
-    st = encode_u8_map(&lmap, l, static_cast<uint64_t>(m), static_cast<uint64_t>(k), static_cast<uint32_t>(tile));
-    if (st != INFERD_OK) return st;
+  for (int t = 0; t < n_tok_tiles; ++t) {
+    const int which = (t == n_tok_tiles - 1) ? 1 : 0;
+    const int tile = tiles[which];
     const int stage_bytes = kTileN * kTileK + 2 * tile * kTileK;
     int stages = kSmemBudget / stage_bytes;
     if (stages > 8) stages = 8;
     if (stages < 2) return INFERD_ERR_UNSUPPORTED;
     Fp8Params p;
+    p.w_packed = w_layout == 1 ? static_cast<const uint8_t*>(w_e4m3) : nullptr;
     p.y = static_cast<__nv_bfloat16*>(y);
     p.w_scale = w_scale;
     p.x_scale = xs;
     p.m = static_cast<int32_t>(m);
     p.n = static_cast<int32_t>(n);
     p.k = static_cast<int32_t>(k);
-    p.tok0 = static_cast<int32_t>(t0);
+    p.tok0 = t * kMaxTokTile;
     p.tok_tile = tile;
     p.stages = stages;
     p.error_word = nullptr;
-    const size_t smem = 1024 + static_cast<size_t>(stages) * stage_bytes;
-    fp8_linear_kernel<<<grid, kThreadsFp8, smem, s>>>(wmap, hmap, lmap, p);
-    st = launch_status();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreadsFp8);
+    cfg.dynamicSmemBytes = 1024 + static_cast<size_t>(stages) * stage_bytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    st = cuda_status(cudaLaunchKernelEx(&cfg, fp8_linear_kernel, wmap, hmaps[which], lmaps[which], p));
     if (st != INFERD_OK) return st;
   }
   return INFERD_OK;

@@ -41,6 +41,24 @@ def quantize_fp8_per_channel(weight: torch.Tensor) -> tuple[torch.Tensor, torch.
     return q.view(torch.float8_e4m3fn), s
 
 
+def pack_fp8_weight(w_e4m3: torch.Tensor) -> torch.Tensor:
+    """Row-major e4m3 [N, K] -> the packed tile layout fp8_linear streams fastest (uint8).
+
+    Every 128-row x 128-byte tile becomes one contiguous 16 KiB block in the MMA's
+    128-byte-swizzled shared-memory form; done once at load time.
+    """
+    if w_e4m3.ndim != 2:
+        raise ValueError("weight must be [N, K]")
+    dev = _lib.require_cuda(w_e4m3)
+    q = w_e4m3.contiguous().view(torch.uint8)
+    n, k = q.shape
+    lib = _lib.load()
+    packed = torch.empty(lib.inferd_fp8_packed_weight_bytes(n, k), dtype=torch.uint8, device=dev)
+    _lib.check(lib.inferd_fp8_pack_weights(q.data_ptr(), packed.data_ptr(), n, k, _lib.stream_of(dev)),
+               "fp8_pack_weights")
+    return packed
+
+
 _WS: dict[int, torch.Tensor] = {}
 
 
@@ -54,24 +72,33 @@ def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
 
 
 def fp8_linear(x: torch.Tensor, w_e4m3: torch.Tensor, w_scale: torch.Tensor,
-               bias: torch.Tensor | None = None, *, out: torch.Tensor | None = None) -> torch.Tensor:
+               bias: torch.Tensor | None = None, *, out: torch.Tensor | None = None,
+               packed_shape: tuple[int, int] | None = None) -> torch.Tensor:
     """y = x @ (w_e4m3 * w_scale[:, None])^T (+ bias), bf16 in and out.
 
-    x [..., K] bf16, w_e4m3 [N, K] (float8_e4m3fn or uint8 codes), w_scale [N] fp32.
+    x [..., K] bf16, w_scale [N] fp32.  w_e4m3 is either the row-major codes [N, K]
+    (float8_e4m3fn or uint8) or, with packed_shape=(N, K), the buffer from pack_fp8_weight.
     """
     if x.dtype != torch.bfloat16:
         raise ValueError("fp8_linear takes bf16 activations")
-    if w_e4m3.ndim != 2 or w_scale.ndim != 1 or w_scale.shape[0] != w_e4m3.shape[0]:
-        raise ValueError("w_e4m3 must be [N, K] and w_scale [N]")
-    n, k = w_e4m3.shape
+    if packed_shape is not None:
+        n, k = packed_shape
+        layout = 1
+    else:
+        if w_e4m3.ndim != 2:
+            raise ValueError("w_e4m3 must be [N, K]")
+        n, k = w_e4m3.shape
+        layout = 0
+    if w_scale.ndim != 1 or w_scale.shape[0] != n:
+        raise ValueError("w_scale must be [N]")
     if x.shape[-1] != k:
         raise ValueError(f"x has {x.shape[-1]} features, weight expects {k}")
     if w_scale.dtype != torch.float32:
         raise ValueError("w_scale must be float32")
     dev = _lib.require_cuda(x, w_e4m3, w_scale)
     x2 = x.reshape(-1, k)
-    if not x2.is_contiguous():
-        x2 = x2.contiguous()
+    if not x2.is_contiguous() or x2.data_ptr() % 16:
+        x2 = x2.contiguous() if x2.data_ptr() % 16 == 0 else x2.clone()
     m = x2.shape[0]
     if out is None:
         y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
@@ -83,7 +110,7 @@ def fp8_linear(x: torch.Tensor, w_e4m3: torch.Tensor, w_scale: torch.Tensor,
         ws = _workspace(dev, ws_bytes)
         w = w_e4m3 if w_e4m3.is_contiguous() else w_e4m3.contiguous()
         st = lib.inferd_fp8_linear(y.data_ptr(), x2.data_ptr(), w.data_ptr(), w_scale.data_ptr(),
-                                   m, n, k, ws.data_ptr(), ws.numel(), _lib.stream_of(dev))
+                                   m, n, k, layout, ws.data_ptr(), ws.numel(), _lib.stream_of(dev))
         _lib.check(st, "fp8_linear")
     if bias is not None:
         y = y + bias.to(y.dtype)
@@ -91,13 +118,14 @@ def fp8_linear(x: torch.Tensor, w_e4m3: torch.Tensor, w_scale: torch.Tensor,
 
 
 class Fp8Linear(nn.Module):
-    """nn.Linear replacement holding e4m3 weights and per-channel fp32 scales."""
+    """nn.Linear replacement holding e4m3 weights (packed tile layout) and per-channel
+    fp32 scales."""
 
     def __init__(self, w_e4m3: torch.Tensor, w_scale: torch.Tensor,
                  bias: torch.Tensor | None = None) -> None:
         super().__init__()
         self.out_features, self.in_features = w_e4m3.shape
-        self.register_buffer("weight_e4m3", w_e4m3)
+        self.register_buffer("weight_packed", pack_fp8_weight(w_e4m3))
         self.register_buffer("weight_scale", w_scale)
         if bias is not None:
             self.register_buffer("bias", bias.to(torch.bfloat16))
@@ -110,7 +138,8 @@ class Fp8Linear(nn.Module):
         return cls(q, s, None if linear.bias is None else linear.bias.detach())
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return fp8_linear(x.to(torch.bfloat16), self.weight_e4m3, self.weight_scale, self.bias)
+        return fp8_linear(x.to(torch.bfloat16), self.weight_packed, self.weight_scale, self.bias,
+                          packed_shape=(self.out_features, self.in_features))
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, e4m3 weight-only"

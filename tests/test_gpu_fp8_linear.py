@@ -13,7 +13,13 @@ import pytest
 import torch
 
 import oracle
-from inferd_b200.fp8_linear import Fp8Linear, fp8_linear, quantize_fp8_per_channel, quantize_model_fp8
+from inferd_b200.fp8_linear import (
+    Fp8Linear,
+    fp8_linear,
+    pack_fp8_weight,
+    quantize_fp8_per_channel,
+    quantize_model_fp8,
+)
 
 pytestmark = pytest.mark.gpu
 
@@ -57,6 +63,34 @@ def test_fp8_linear_matches_dequant_matmul(cuda_device, m):
     assert_linear_close(y.float().cpu().numpy(), ref, f"m={m}")
 
 
+def _pack_reference(q: np.ndarray) -> np.ndarray:
+    """numpy statement of the packed tile layout (zero padding, 16-byte chunk swizzle)."""
+    n, k = q.shape
+    nt, kt = -(-n // 128), -(-k // 128)
+    padded = np.zeros((nt * 128, kt * 128), np.uint8)
+    padded[:n, :k] = q
+    tiles = padded.reshape(nt, 128, kt, 8, 16).transpose(0, 2, 1, 3, 4)  # [nt, kt, r, c16, b]
+    out = np.empty_like(tiles)
+    r = np.arange(128)[:, None]
+    c = np.arange(8)[None, :]
+    out[:, :, r, c ^ (r & 7), :] = tiles[:, :, r, c, :]
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("n,k", [(256, 512), (1000, 640), (130, 144)])
+def test_pack_layout_and_packed_linear(cuda_device, n, k):
+    g = torch.Generator().manual_seed(n + k)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    q, s = quantize_fp8_per_channel(w.to(cuda_device))
+    packed = pack_fp8_weight(q)
+    assert np.array_equal(packed.cpu().numpy(), _pack_reference(q.view(torch.uint8).cpu().numpy()))
+    x = torch.randn(37, k, generator=g).to(torch.bfloat16).to(cuda_device)
+    y_row = fp8_linear(x, q, s)
+    y_packed = fp8_linear(x, packed, s, packed_shape=(n, k))
+    torch.cuda.synchronize()
+    assert torch.equal(y_row, y_packed)  # same MMAs in the same order
+
+
 @pytest.mark.parametrize("m", [1, 8, 256])
 def test_fp8_linear_config4_shape(cuda_device, m):
     # config-4 weight: N = 17408, K = 5120, N(0, 0.02) quantised per channel
@@ -65,7 +99,7 @@ def test_fp8_linear_config4_shape(cuda_device, m):
     w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
     x = torch.randn(m, k, generator=g).to(torch.bfloat16)
     q, s = quantize_fp8_per_channel(w.to(cuda_device))
-    y = fp8_linear(x.to(cuda_device), q, s)
+    y = fp8_linear(x.to(cuda_device), pack_fp8_weight(q), s, packed_shape=(n, k))
     torch.cuda.synchronize()
     rows = slice(0, n) if m <= 8 else slice(0, 2048)  # keep the float64 oracle to seconds
     ref = oracle.fp8_linear(x.float().numpy(), q.view(torch.uint8).cpu().numpy()[rows],
