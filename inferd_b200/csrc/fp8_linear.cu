@@ -40,7 +40,6 @@ namespace {
 constexpr int kTileN = 128;     // weight rows per CTA (MMA M)
 constexpr int kTileK = 128;     // K bytes per stage = one 128-byte swizzle row
 constexpr int kMmaK = 32;       // K per tcgen05.mma of kind::f8f6f4
-constexpr int kThreadsFp8 = 128;
 constexpr int kMaxTokTile = 256;  // MMA N upper bound
 constexpr int kSmemBudget = 200 * 1024;
 
@@ -122,46 +121,81 @@ __host__ __device__ constexpr uint32_t f8_idesc(int n) {
 
 struct Fp8Params {
   const uint8_t* w_packed;  // packed weight tiles (nullptr: row-major through wmap)
-  __nv_bfloat16* y;      // [M, N]
-  const float* w_scale;  // [N]
-  const float* x_scale;  // [M] (powers of two)
+  __nv_bfloat16* y;         // [M, N]
+  const float* w_scale;     // [N]
+  const float* x_scale;     // [M] (powers of two)
   int32_t m, n, k;
-  int32_t tok0;          // first token of this launch's token tile
-  int32_t tok_tile;      // MMA N (multiple of 16)
+  int32_t tok0;             // first token of this launch's token tile
+  int32_t tok_tile;         // tokens per MMA (multiple of 16)
   int32_t stages;
+  int32_t* counters;        // [weight tiles] tickets, 0 between launches
+  float* part;              // [slot][tok_tile][128] partial accumulators
   int32_t* error_word;
 };
 
-// One CTA = 128 weight rows x tok_tile tokens, full K.
-__global__ void __launch_bounds__(kThreadsFp8, 1)
+constexpr int kFp8Warps = 6;  // 0: TMA producer, 1: MMA issuer, 2..5: epilogue
+constexpr int kFp8Threads = kFp8Warps * 32;
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 lane;\n\t.reg .pred p;\n\t"
+      "elect.sync lane|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// CTA whose balanced range [c*W/G, (c+1)*W/G) of the work axis contains unit g.
+__device__ __forceinline__ int fp8_cta_of(int64_t g, int64_t W, int G) {
+  int64_t c = ((g + 1) * G + W - 1) / W - 1;
+  if (c < 0) c = 0;
+  if (c > G - 1) c = G - 1;
+  return static_cast<int>(c);
+}
+
+// Stream-K over the work axis (weight tile t, K step ks) -> g = t * KS + ks: CTA c of G
+// runs [c*W/G, (c+1)*W/G).  Every run of one tile inside that range is a segment with
+// its own TMEM accumulator pass; a segment that is a whole tile is stored directly,
+// otherwise it becomes a partial that the CTA finishing the tile last merges.
+__global__ void __launch_bounds__(kFp8Threads, 1)
     fp8_linear_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap hmap,
                       const __grid_constant__ CUtensorMap lmap, const Fp8Params p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[8];
   __shared__ __align__(8) uint64_t empty[8];
   __shared__ __align__(8) uint64_t acc_full;
+  __shared__ __align__(8) uint64_t acc_empty;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
+  __shared__ int last_flag;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * kTileN;
   const int T = p.tok_tile;
   const int S = p.stages;
   const uint32_t w_bytes = kTileN * kTileK;  // 16 KiB
   const uint32_t x_bytes = static_cast<uint32_t>(T) * kTileK;
   const uint32_t stage_bytes = w_bytes + 2 * x_bytes;  // multiple of 1024
-  const int k_steps = (p.k + kTileK - 1) / kTileK;
+  const int KS = (p.k + kTileK - 1) / kTileK;
+  const int NT = (p.n + kTileN - 1) / kTileN;
+  const int64_t W = static_cast<int64_t>(NT) * KS;
+  const int G = gridDim.x;
+  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * W / G;
+  const int64_t g1 = static_cast<int64_t>(blockIdx.x + 1) * W / G;
+  const int n_units = static_cast<int>(g1 - g0);
+
   // Accumulator plan.  With T <= 128 the h and l tiles (adjacent in shared memory) form
   // one B operand of N = 2T rows, so one MMA covers both planes; consecutive MMAs rotate
   // over `chains` independent accumulators so they do not wait on each other.  With
   // T = 256 (N would exceed 256) h and l go to two accumulators of 256 columns.
   const bool merged = T <= 128;
   const int n_mma = merged ? 2 * T : T;
-  int chains = merged ? 512 / n_mma : 1;
+  int chains = merged ? 256 / n_mma : 1;
   if (chains > 4) chains = 4;
-  uint32_t ncols = 32;  // tcgen05.alloc takes a power of two >= 32 (<= 512 here)
+  if (chains < 1) chains = 1;
+  uint32_t ncols = 32;  // tcgen05.alloc takes a power of two >= 32
   while (ncols < (merged ? static_cast<uint32_t>(chains * n_mma) : 512u)) ncols <<= 1;
 
   if (tid == 0) {
@@ -170,6 +204,7 @@ __global__ void __launch_bounds__(kThreadsFp8, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(&acc_full, 1);
+    mbar_init(&acc_empty, 4);  // one arrival per epilogue warp
     abort_flag = 0;
     fence_mbar_init();
   }
@@ -183,129 +218,229 @@ __global__ void __launch_bounds__(kThreadsFp8, 1)
   const uint32_t tmem = tmem_base;
   volatile int* vabort = &abort_flag;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer
-    if (p.w_packed == nullptr) prefetch_tensormap(&wmap);
-    prefetch_tensormap(&hmap);
-    prefetch_tensormap(&lmap);
-    const uint64_t pol_w = l2_policy_evict_first();
-    uint64_t pol_x;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_x));
-    const uint8_t* wband = p.w_packed + static_cast<int64_t>(blockIdx.x) * k_steps * w_bytes;
-    auto load_w = [&](uint8_t* st, int ks, uint64_t* bar) {
-      if (p.w_packed != nullptr) bulk_load(st, wband + static_cast<int64_t>(ks) * w_bytes, w_bytes, bar, pol_w);
-      else tma_load_2d(st, &wmap, ks * kTileK, n0, bar, pol_w);
-    };
-    // The weight tiles of the first ring do not depend on the activation split: issue
-    // them before waiting for it.
-    const int first = k_steps < S ? k_steps : S;
-    for (int ks = 0; ks < first; ++ks) {
-      uint8_t* st = smem + ks * stage_bytes;
-      mbar_arrive_expect_tx(&full[ks], stage_bytes);
-      load_w(st, ks, &full[ks]);
-    }
-    grid_dependency_wait();
-    for (int ks = 0; ks < first; ++ks) {
-      uint8_t* st = smem + ks * stage_bytes;
-      tma_load_2d(st + w_bytes, &hmap, ks * kTileK, p.tok0, &full[ks], pol_x);
-      tma_load_2d(st + w_bytes + x_bytes, &lmap, ks * kTileK, p.tok0, &full[ks], pol_x);
-    }
-    for (int ks = first; ks < k_steps; ++ks) {
-      const int s = ks % S;
-      const uint32_t round = ks / S;
-      if (!mbar_wait(&empty[s], (round - 1) & 1u)) {
-        report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
-        *vabort = 1;
-        break;
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      if (p.w_packed == nullptr) prefetch_tensormap(&wmap);
+      prefetch_tensormap(&hmap);
+      prefetch_tensormap(&lmap);
+      const uint64_t pol_w = l2_policy_evict_first();
+      uint64_t pol_x;
+      asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_x));
+      auto load_w = [&](uint8_t* st, int64_t g, uint64_t* bar) {
+        const int t = static_cast<int>(g / KS), ks = static_cast<int>(g - static_cast<int64_t>(t) * KS);
+        if (p.w_packed != nullptr) bulk_load(st, p.w_packed + g * w_bytes, w_bytes, bar, pol_w);
+        else tma_load_2d(st, &wmap, ks * kTileK, t * kTileN, bar, pol_w);
+      };
+      auto load_x = [&](uint8_t* st, int64_t g, uint64_t* bar) {
+        const int ks = static_cast<int>(g % KS);
+        tma_load_2d(st + w_bytes, &hmap, ks * kTileK, p.tok0, bar, pol_x);
+        tma_load_2d(st + w_bytes + x_bytes, &lmap, ks * kTileK, p.tok0, bar, pol_x);
+      };
+      // The weight tiles of the first ring do not depend on the activation split: issue
+      // them before waiting for it.
+      const int first = n_units < S ? n_units : S;
+      for (int j = 0; j < first; ++j) {
+        mbar_arrive_expect_tx(&full[j], stage_bytes);
+        load_w(smem + j * stage_bytes, g0 + j, &full[j]);
       }
-      if (*vabort) break;
-      uint8_t* st = smem + s * stage_bytes;
-      mbar_arrive_expect_tx(&full[s], stage_bytes);
-      load_w(st, ks, &full[s]);
-      tma_load_2d(st + w_bytes, &hmap, ks * kTileK, p.tok0, &full[s], pol_x);
-      tma_load_2d(st + w_bytes + x_bytes, &lmap, ks * kTileK, p.tok0, &full[s], pol_x);
+      grid_dependency_wait();
+      for (int j = 0; j < first; ++j) load_x(smem + j * stage_bytes, g0 + j, &full[j]);
+      for (int j = first; j < n_units; ++j) {
+        const int s = j % S;
+        if (*vabort) break;
+        if (!mbar_wait(&empty[s], ((j / S) - 1) & 1u)) {
+          report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+          *vabort = 1;
+          break;
+        }
+        uint8_t* st = smem + s * stage_bytes;
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        load_w(st, g0 + j, &full[s]);
+        load_x(st, g0 + j, &full[s]);
+      }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer (one thread)
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: the whole warp walks the loop, one elected lane issues
     const uint32_t idesc = f8_idesc(n_mma);
-    int issued = 0;  // MMAs issued so far (selects the accumulator chain)
-    for (int ks = 0; ks < k_steps; ++ks) {
-      const int s = ks % S;
-      if (*vabort || !mbar_wait(&full[s], (ks / S) & 1u)) {
+    int seg = 0;        // segments started
+    int in_seg = 0;     // MMAs issued in the current segment
+    for (int j = 0; j < n_units; ++j) {
+      const int64_t g = g0 + j;
+      const int ks = static_cast<int>(g % KS);
+      const bool seg_begin = (j == 0) || (ks == 0);
+      const bool seg_end = (j == n_units - 1) || (ks == KS - 1);
+      // Waits are done by lane 0 and broadcast, so every branch below is warp-uniform
+      // (elect.sync needs the whole warp).
+      if (seg_begin) {
+        // the previous segment's accumulator must have been read out
+        if (seg > 0) {
+          int w_ok = 1;
+          if (lane == 0 && !*vabort) {
+            w_ok = mbar_wait(&acc_empty, (seg - 1) & 1u) ? 1 : 0;
+            if (!w_ok) {
+              report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+              *vabort = 1;
+            }
+          }
+          __shfl_sync(0xffffffffu, w_ok, 0);
+        }
+        in_seg = 0;
+        tc_fence_after();
+      }
+      const int s = j % S;
+      int ok = 0;
+      if (lane == 0 && !*vabort) {
+        ok = mbar_wait(&full[s], (j / S) & 1u) ? 1 : 0;
+        if (!ok) {
+          report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+          *vabort = 1;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (ok && elect_one()) {
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + s * stage_bytes);
+        const uint32_t h0 = a0 + w_bytes, l0 = h0 + x_bytes;
+        int cnt = in_seg;
+#pragma unroll
+        for (int kk = 0; kk < kTileK / kMmaK; ++kk) {
+          const uint64_t ad = sw128_desc(a0 + kk * kMmaK);
+          if (merged) {
+            const int c = cnt % chains;
+            mma_f8(tmem + static_cast<uint32_t>(c * n_mma), ad, sw128_desc(h0 + kk * kMmaK), idesc,
+                   cnt >= chains);
+          } else {
+            mma_f8(tmem, ad, sw128_desc(h0 + kk * kMmaK), idesc, cnt > 0);
+            mma_f8(tmem + 256u, ad, sw128_desc(l0 + kk * kMmaK), idesc, cnt > 0);
+          }
+          ++cnt;
+        }
+        mma_commit(&empty[s]);  // stage s free once these MMAs have read it
+      }
+      __syncwarp();
+      in_seg += kTileK / kMmaK;
+      if (seg_end) {
+        if (elect_one()) mma_commit(&acc_full);  // segment accumulator complete
+        __syncwarp();
+        ++seg;
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..5: TMEM lane quarter q = warp % 4
+    const int q = warp & 3;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const int ep = tid - 64;  // 0..127 among the epilogue threads
+    grid_dependency_wait();   // x_scale comes from the split grid
+    int seg = 0;
+    int64_t g = g0;
+    while (g < g1) {
+      const int t = static_cast<int>(g / KS);
+      const int64_t t_begin = static_cast<int64_t>(t) * KS, t_end = t_begin + KS;
+      const int64_t s_end = g1 < t_end ? g1 : t_end;
+      const bool whole = (g == t_begin) && (s_end == t_end);
+      const int live = merged ? (static_cast<int>(s_end - g) * (kTileK / kMmaK) < chains
+                                     ? static_cast<int>(s_end - g) * (kTileK / kMmaK)
+                                     : chains)
+                              : 1;
+      bool ok = !*vabort && mbar_wait(&acc_full, seg & 1u);
+      if (!ok && !*vabort) {
         report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
         *vabort = 1;
-        break;
       }
       tc_fence_after();
-      const uint32_t a0 = smem_u32(smem + s * stage_bytes);
-      const uint32_t h0 = a0 + w_bytes, l0 = h0 + x_bytes;
+      const int row = q * 32 + lane;
+      const int n_idx = t * kTileN + row;
+      const float sw = (n_idx < p.n) ? __ldg(p.w_scale + n_idx) : 0.f;
+      const int64_t slot = static_cast<int64_t>(blockIdx.x) + t;
+      float* prow = p.part + slot * static_cast<int64_t>(T) * kTileN + row;
+      for (int c0 = 0; c0 < T; c0 += 16) {
+        float acc[16];
 #pragma unroll
-      for (int kk = 0; kk < kTileK / kMmaK; ++kk) {
-        const uint64_t ad = sw128_desc(a0 + kk * kMmaK);
-        if (merged) {
-          const int c = issued % chains;
-          mma_f8(tmem + static_cast<uint32_t>(c * n_mma), ad, sw128_desc(h0 + kk * kMmaK), idesc,
-                 issued >= chains);
+        for (int jj = 0; jj < 16; ++jj) acc[jj] = 0.f;
+        const int parts = merged ? 2 * live : 2;
+        for (int qq = 0; qq < parts; ++qq) {
+          const uint32_t col = merged ? static_cast<uint32_t>((qq >> 1) * n_mma + (qq & 1) * T + c0)
+                                      : static_cast<uint32_t>((qq & 1) * 256 + c0);
+          uint32_t r[16];
+          tmem_ld16(lane_base + col, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) acc[jj] += __uint_as_float(r[jj]);
+        }
+        if (whole) {
+          if (n_idx < p.n) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int m = p.tok0 + c0 + jj;
+              if (m < p.m)
+                p.y[static_cast<int64_t>(m) * p.n + n_idx] =
+                    __float2bfloat16_rn(acc[jj] * sw * __ldg(p.x_scale + m));
+            }
+          }
         } else {
-          mma_f8(tmem, ad, sw128_desc(h0 + kk * kMmaK), idesc, issued > 0);
-          mma_f8(tmem + 256u, ad, sw128_desc(l0 + kk * kMmaK), idesc, issued > 0);
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) prow[static_cast<int64_t>(c0 + jj) * kTileN] = acc[jj];
         }
-        ++issued;
       }
-      mma_commit(&empty[s]);  // stage s free once these MMAs have read it
+      // accumulator read out: the MMA warp may start the next segment
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty);
+      if (!whole) {
+        __threadfence();
+        named_barrier_sync(1, 128);
+        const int c_first = fp8_cta_of(t_begin, W, G), c_last = fp8_cta_of(t_end - 1, W, G);
+        if (ep == 0) {
+          const int prev = atomicAdd(p.counters + t, 1);
+          last_flag = (prev == c_last - c_first) ? 1 : 0;
+        }
+        named_barrier_sync(1, 128);
+        if (last_flag) {
+          __threadfence();
+          // merge the tile's partials: pieces from CTAs c_first..c_last, slots cc + t;
+          // 16 independent loads per piece keep the merge off the load-latency chain
+          for (int c0 = 0; c0 < T; c0 += 16) {
+            float sum[16];
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) sum[jj] = 0.f;
+            for (int cc = c_first; cc <= c_last; ++cc) {
+              const float* src = p.part + (static_cast<int64_t>(cc) + t) * T * kTileN +
+                                 static_cast<int64_t>(c0) * kTileN + row;
+              float v[16];
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) v[jj] = __ldcg(src + jj * kTileN);
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) sum[jj] += v[jj];
+            }
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int m = p.tok0 + c0 + jj;
+              if (m < p.m && n_idx < p.n)
+                p.y[static_cast<int64_t>(m) * p.n + n_idx] =
+                    __float2bfloat16_rn(sum[jj] * sw * __ldg(p.x_scale + m));
+            }
+          }
+          if (ep == 0) p.counters[t] = 0;
+        }
+        named_barrier_sync(1, 128);
+      }
+      ++seg;
+      g = s_end;
     }
-    mma_commit(&acc_full);  // accumulator complete
   }
-  __syncwarp();
 
-  // ---------------- epilogue: all four warps, TMEM lanes 32*warp .. 32*warp+31
-  grid_dependency_wait();  // x_scale comes from the split grid
-  bool ok = mbar_wait(&acc_full, 0);
-  if (!ok) report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
-  tc_fence_after();
-  const int n = n0 + warp * 32 + lane;
-  const float sw = (ok && n < p.n) ? __ldg(p.w_scale + n) : 0.f;
-  // with fewer MMAs than chains (tiny K) the unused chains were never written
-  const int live_chains = merged ? (k_steps * (kTileK / kMmaK) < chains ? k_steps * (kTileK / kMmaK) : chains) : 1;
-  const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  for (int c0 = 0; c0 < T; c0 += 16) {
-    float acc[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-    // sum the h and l partials of every chain: columns c*n_mma + m (h) and + T + m (l),
-    // or 0 + m (h) and 256 + m (l) when the planes have their own accumulators
-    const int parts = merged ? 2 * live_chains : 2;
-    for (int q = 0; q < parts; ++q) {
-      const uint32_t col = merged ? static_cast<uint32_t>((q >> 1) * n_mma + (q & 1) * T + c0)
-                                  : static_cast<uint32_t>((q & 1) * 256 + c0);
-      uint32_t r[16];
-      tmem_ld16(lane_base + col, r);
-      tmem_ld_wait();
-#pragma unroll
-      for (int j = 0; j < 16; ++j) acc[j] += __uint_as_float(r[j]);
-    }
-    if (ok && n < p.n) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int m = p.tok0 + c0 + j;
-        if (m < p.m) {
-          const float v = acc[j] * sw * __ldg(p.x_scale + m);
-          p.y[static_cast<int64_t>(m) * p.n + n] = __float2bfloat16_rn(v);
-        }
-      }
-    }
-  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, ncols);
   }
-  // never leave with a TMA write in flight: the producer stopped early only on abort,
-  // in which case every issued stage was either consumed or is drained here
+  // never leave with a TMA write in flight (only possible after an abort)
   if (*vabort && tid == 0) {
-    for (int s = 0; s < S && s < k_steps; ++s) {
-      const int rounds = (k_steps - s + S - 1) / S;
+    for (int s = 0; s < S && s < n_units; ++s) {
+      const int rounds = (n_units - s + S - 1) / S;
       mbar_wait(&full[s], (rounds - 1) & 1u);
     }
   }
@@ -517,15 +652,49 @@ inline int cached_u8_map(CUtensorMap* map, const void* base, uint64_t rows, uint
 
 inline size_t align256_fp8(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
-struct Fp8Workspace {
-  size_t h, l, scale, total;
+// Workspace: [tile tickets: fixed region][h plane][l plane][x scales][partials].  The
+// ticket region has one size for every call, so calls of any shape can share a
+// workspace; completed calls leave the tickets at zero.
+constexpr int kMaxTilesFp8 = 4096;  // N <= 524288
+constexpr size_t kFp8CounterBytes = kMaxTilesFp8 * sizeof(int32_t);
+
+struct Fp8Plan {
+  int tile;      // tokens per launch tile (multiple of 16)
+  int stages;    // ring depth
+  int grid;      // CTAs (stream-K)
+  size_t smem;   // dynamic shared memory per CTA
 };
-inline Fp8Workspace fp8_workspace(int64_t m, int64_t k) {
+
+inline Fp8Plan fp8_plan(int64_t rem_tokens, int64_t n, int64_t k, int sms) {
+  Fp8Plan pl;
+  const int64_t t = rem_tokens < kMaxTokTile ? rem_tokens : kMaxTokTile;
+  pl.tile = static_cast<int>((t + 15) / 16 * 16);
+  const int per_sm = pl.tile <= 128 ? 2 : 1;           // TMEM and smem allow two CTAs up to 128 tokens
+  const int budget = per_sm == 2 ? 104 * 1024 : kSmemBudget;
+  const int stage_bytes = kTileN * kTileK + 2 * pl.tile * kTileK;
+  pl.stages = budget / stage_bytes;
+  if (pl.stages > 8) pl.stages = 8;
+  const int64_t work = ((n + kTileN - 1) / kTileN) * ((k + kTileK - 1) / kTileK);
+  int64_t g = static_cast<int64_t>(sms) * per_sm;
+  if (g > work) g = work;
+  pl.grid = static_cast<int>(g);
+  pl.smem = 1024 + static_cast<size_t>(pl.stages) * stage_bytes;
+  return pl;
+}
+
+struct Fp8Workspace {
+  size_t counters, h, l, scale, part, total;
+};
+inline Fp8Workspace fp8_workspace(int64_t m, int64_t n, int64_t k, int sms) {
   Fp8Workspace w;
-  w.h = 0;
-  w.l = align256_fp8(static_cast<size_t>(m * k));
+  w.counters = 0;
+  w.h = kFp8CounterBytes;
+  w.l = w.h + align256_fp8(static_cast<size_t>(m * k));
   w.scale = w.l + align256_fp8(static_cast<size_t>(m * k));
-  w.total = w.scale + align256_fp8(static_cast<size_t>(m) * 4);
+  w.part = w.scale + align256_fp8(static_cast<size_t>(m) * 4);
+  const Fp8Plan pl = fp8_plan(m, n, k, sms);  // the first launch tile is the largest
+  const int64_t tiles = (n + kTileN - 1) / kTileN;
+  w.total = w.part + align256_fp8(static_cast<size_t>(pl.grid + tiles) * pl.tile * kTileN * 4);
   return w;
 }
 
@@ -534,11 +703,18 @@ inline Fp8Workspace fp8_workspace(int64_t m, int64_t k) {
 
 using namespace inferd;
 
+inline int sm_count_of(int32_t device) {
+  int sms = 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms <= 0) {
+    cudaGetLastError();
+    sms = 148;
+  }
+  return sms;
+}
+
 extern "C" size_t inferd_fp8_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int32_t device) {
-  (void)n;
-  (void)device;
-  if (m <= 0 || k <= 0) return 0;
-  return fp8_workspace(m, k).total;
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  return fp8_workspace(m, n, k, sm_count_of(device)).total;
 }
 
 extern "C" int inferd_fp8_quantize_per_channel(const void* w, int32_t w_dtype, void* w_e4m3, float* w_scale,
@@ -594,7 +770,9 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
   if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return INFERD_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(w_e4m3) & 15) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
     return INFERD_ERR_INVALID_ARGUMENT;  // 16-byte aligned weights and activations
-  const Fp8Workspace wl = fp8_workspace(m, k);
+  if ((n + kTileN - 1) / kTileN > kMaxTilesFp8) return INFERD_ERR_UNSUPPORTED;
+  const int sms = current_sm_count();
+  const Fp8Workspace wl = fp8_workspace(m, n, k, sms);
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0 || workspace_bytes < wl.total)
     return INFERD_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -602,12 +780,23 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
   uint8_t* h = ws + wl.h;
   uint8_t* l = ws + wl.l;
   float* xs = reinterpret_cast<float*>(ws + wl.scale);
+  int32_t* counters = reinterpret_cast<int32_t*>(ws + wl.counters);
+  float* part = reinterpret_cast<float*>(ws + wl.part);
 
   static bool configured[64] = {false};
   const int dev = current_device();
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    const cudaError_t e =
+    cudaError_t e =
         cudaFuncSetAttribute(fp8_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 1024);
+    if (e != cudaSuccess) return cuda_status(e);
+    // all of the unified L1/shared array as shared memory, so two 100 KB CTAs fit per SM;
+    // the split kernel asks for the same carveout, so the SMs are not reconfigured
+    // between the two launches of every call
+    e = cudaFuncSetAttribute(fp8_linear_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return cuda_status(e);
+    e = cudaFuncSetAttribute(split_activations_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return cuda_status(e);
     configured[dev] = true;
   }
@@ -639,14 +828,12 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
   st = launch_status();
   if (st != INFERD_OK) return st;
 
-  const unsigned grid = static_cast<unsigned>((n + kTileN - 1) / kTileN);
   for (int t = 0; t < n_tok_tiles; ++t) {
     const int which = (t == n_tok_tiles - 1) ? 1 : 0;
+    const Fp8Plan pl = fp8_plan(m - static_cast<int64_t>(t) * kMaxTokTile, n, k, sms);
     const int tile = tiles[which];
-    const int stage_bytes = kTileN * kTileK + 2 * tile * kTileK;
-    int stages = kSmemBudget / stage_bytes;
-    if (stages > 8) stages = 8;
-    if (stages < 2) return INFERD_ERR_UNSUPPORTED;
+    const int stages = pl.stages;
+    if (stages < 2 || pl.tile != tile) return INFERD_ERR_UNSUPPORTED;
     Fp8Params p;
     p.w_packed = w_layout == 1 ? static_cast<const uint8_t*>(w_e4m3) : nullptr;
     p.y = static_cast<__nv_bfloat16*>(y);
@@ -658,11 +845,13 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
     p.tok0 = t * kMaxTokTile;
     p.tok_tile = tile;
     p.stages = stages;
+    p.counters = counters;
+    p.part = part;
     p.error_word = nullptr;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreadsFp8);
-    cfg.dynamicSmemBytes = 1024 + static_cast<size_t>(stages) * stage_bytes;
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(kFp8Threads);
+    cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -787,6 +787,10 @@ int launch_fast_t(const CUtensorMap& km, const CUtensorMap& vm, const FastParams
     cudaError_t e = cudaFuncSetAttribute(paged_attn_tc_kernel<kBf16, NT, STAGES>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return cuda_status(e);
+    // all of the unified L1/shared array as shared memory, so two CTAs fit per SM
+    e = cudaFuncSetAttribute(paged_attn_tc_kernel<kBf16, NT, STAGES>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return cuda_status(e);
     configured[dev] = true;
   }
   paged_attn_tc_kernel<kBf16, NT, STAGES><<<grid, kWarps * 32, smem, s>>>(km, vm, fp);

@@ -66,7 +66,8 @@ def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     ws = _WS.get(idx)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        # zeroed: the tile tickets at its head must start at zero (calls leave them zero)
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
         _WS[idx] = ws
     return ws
 
