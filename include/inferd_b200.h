@@ -177,7 +177,7 @@ INFERD_API int inferd_fp8_quantize_per_channel(const void* w, int32_t w_dtype, v
  * Load-time repacking of row-major e4m3 weights [N, K] into the tile layout the linear
  * streams fastest: every 128-row x 128-byte tile is one contiguous 16 KiB block (already
  * in the MMA's 128-byte-swizzled form), the tiles of a 128-row band consecutive along K,
- * zero-filled past N and K.  w_packed needs inferd_fp8_packed_weight_bytes(n, k) bytes,
+ * zero-filled past N and K; the band count is rounded up to even (whole 256-row pairs).  w_packed needs inferd_fp8_packed_weight_bytes(n, k) bytes,
  * 16-byte aligned.  No counterpart in the reference (its torchao weights stay row-major).
  */
 INFERD_API size_t inferd_fp8_packed_weight_bytes(int64_t n, int64_t k);

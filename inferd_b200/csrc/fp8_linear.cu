@@ -17,15 +17,18 @@
 // Weight layouts.  Row-major [N, K] e4m3 is read by TMA 128 bytes per row per stage.
 // The packed layout produced once at load time stores every 128-row x 128-byte tile as
 // one contiguous 16 KiB block, already in the 128-byte-swizzled shared-memory form the
-// MMA reads, tiles of one 128-row band consecutive along K -- so each CTA streams one
-// contiguous region with 16 KiB bulk copies (the row-major form's 128-byte pieces at a
-// 5 KiB stride use HBM pages poorly).  Tiles past N or K are zero-filled.
+// MMA reads, tiles of one 128-row band consecutive along K, bands padded to an even
+// count -- so each CTA streams one contiguous region, copied verbatim by TMA as 128-byte
+// rows.  Tiles past N or K are zero-filled.
 //
-// Kernel layout (swap-AB): the MMA's M = 128 is the weight rows n, its N is the token
-// count m (16..256), so small decode batches do not pad to 128.  One CTA owns 128 weight
-// rows: warp 0 streams weight and activation tiles with TMA into a shared-memory ring,
-// one thread of warp 1 issues tcgen05.mma and releases stages with tcgen05.commit, and
-// all four warps run the epilogue (tcgen05.ld, scale by s_w[n] * 2^e[m], bf16 store).
+// Kernel layout (swap-AB, CTA pairs): the MMA's M is the weight rows and its N the token
+// count m (16..256), so small decode batches do not pad to 128.  Two CTAs on two SMs form
+// a cluster that issues tcgen05.mma.cta_group::2 with M = 256: each CTA holds its own
+// 128-row weight tile and half of the activation tile, which halves the activation bytes
+// every SM stages per weight byte.  Per CTA, warp 0 streams tiles with TMA into a
+// shared-memory ring, one thread of the leader CTA's warp 1 issues the MMAs and releases
+// stages of both CTAs with tcgen05.commit, and four epilogue warps drain double-buffered
+// TMEM accumulators (tcgen05.ld, scale by s_w[n] * 2^e[m]) into y with TMA stores.
 #include <cuda_fp8.h>
 
 #include <cstring>
@@ -41,19 +44,26 @@ constexpr int kTileN = 128;     // weight rows per CTA (MMA M)
 constexpr int kTileK = 128;     // K bytes per stage = one 128-byte swizzle row
 constexpr int kMmaK = 32;       // K per tcgen05.mma of kind::f8f6f4
 constexpr int kMaxTokTile = 256;  // MMA N upper bound
-constexpr int kSmemBudget = 200 * 1024;
+constexpr int kSmemBudget = 224 * 1024;   // one CTA per SM
+constexpr int kSmemBudget2 = 108 * 1024;  // two CTAs per SM
+// epilogue shared memory after the ring: per epilogue warp four 16-token x 32-row bf16
+// blocks (two per 32-token step, double-buffered), then the launch tile's token scales
+constexpr int kEpiBlockElems = 16 * 32;
+constexpr int kEpiStageBytes = 4 * 4 * kEpiBlockElems * 2 + kMaxTokTile * 4;
 
-// ---------------------------------------------------------------- tcgen05 wrappers
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+// ---------------------------------------------------------------- tcgen05 / cluster wrappers
+// Every tcgen05 instruction of the GEMM uses .cta_group::2: the two CTAs of a cluster
+// form one 256-row MMA (each CTA holds its 128 weight rows as A and half of the B rows).
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
                "r"(ncols)
                : "memory");
 }
-__device__ __forceinline__ void tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -61,13 +71,13 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-// D[tmem] (+)= A[smem] * B[smem]^T, e4m3 x e4m3 -> f32
-__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                       uint32_t accumulate) {
+// D[tmem] (+)= A[smem] * B[smem]^T over the CTA pair, e4m3 x e4m3 -> f32
+__device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -78,15 +88,17 @@ __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepco
 __device__ __forceinline__ void grid_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
-
-// mbarrier arrives when every tcgen05.mma issued so far by this thread has completed
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
+// The mbarrier at the same shared-memory offset in both CTAs of the pair receives one
+// arrival once every tcgen05.mma issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
 }
-// 32 lanes x 32 bit, 16 consecutive columns per thread
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+// 32 lanes x 32 bit, 16 consecutive columns per thread, into r[0..15]
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
       "%12, %13, %14, %15}, [%16];"
@@ -96,8 +108,65 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr)
       : "memory");
 }
+// 32 lanes x 32 bit, 32 consecutive columns per thread
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// all threads of both CTAs; orders shared-memory writes (barrier inits) cluster-wide
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of this CTA's variable at `smem_addr` as seen in CTA `rank`
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+// 2-D tiled TMA load into this CTA's shared memory; the bytes are counted on the mbarrier
+// at bar_cluster_addr, which may be the peer CTA's (.cta_group::2)
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int32_t c0, int32_t c1,
+                                                 uint32_t bar_cluster_addr, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar_cluster_addr), "l"(policy)
+      : "memory");
+}
+// 2-D tiled TMA store from this CTA's shared memory (bulk async-group completion); rows
+// and columns outside the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most one committed store group still reads shared memory
+__device__ __forceinline__ void bulk_wait_read_le1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// make this thread's generic-proxy shared-memory writes visible to the TMA (async proxy)
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor of a K-major tile whose rows are 128 bytes with the
@@ -114,26 +183,28 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor: kind::f8f6f4, A = B = e4m3, D = f32, both K-major, M = 128.
-__host__ __device__ constexpr uint32_t f8_idesc(int n) {
-  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kTileN >> 4) << 24);
+// Instruction descriptor: kind::f8f6f4, A = B = e4m3, D = f32, both K-major, M = 256 (the
+// CTA pair), N = n.
+__host__ __device__ constexpr uint32_t f8_idesc_pair(int n) {
+  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(256 >> 4) << 24);
 }
 
 struct Fp8Params {
-  const uint8_t* w_packed;  // packed weight tiles (nullptr: row-major through wmap)
   __nv_bfloat16* y;         // [M, N]
   const float* w_scale;     // [N]
   const float* x_scale;     // [M] (powers of two)
   int32_t m, n, k;
+  int32_t w_packed;         // 1: wmap views the packed tiles as [tiles * 128 rows, 128 B]
   int32_t tok0;             // first token of this launch's token tile
-  int32_t tok_tile;         // tokens per MMA (multiple of 16)
+  int32_t tok_tile;         // tokens per launch tile T (multiple of 16)
   int32_t stages;
   int32_t* counters;        // [weight tiles] tickets, 0 between launches
-  float* part;              // [slot][tok_tile][128] partial accumulators
+  float* part;              // [slot][2][T][128] partial accumulators
   int32_t* error_word;
+  int32_t y_tma;            // 1: ymap describes y (bf16 [M, N], 16-byte row pitch)
 };
 
-constexpr int kFp8Warps = 6;  // 0: TMA producer, 1: MMA issuer, 2..5: epilogue
+constexpr int kFp8Warps = 6;  // 0: TMA producer, 1: MMA issuer (leader CTA), 2..5: epilogue
 constexpr int kFp8Threads = kFp8Warps * 32;
 
 __device__ __forceinline__ bool elect_one() {
@@ -146,26 +217,52 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
-// CTA whose balanced range [c*W/G, (c+1)*W/G) of the work axis contains unit g.
-__device__ __forceinline__ int fp8_cta_of(int64_t g, int64_t W, int G) {
-  int64_t c = ((g + 1) * G + W - 1) / W - 1;
+// Cluster whose balanced range [c*W/C, (c+1)*W/C) of the work axis contains unit g.
+__device__ __forceinline__ int fp8_cluster_of(int64_t g, int64_t W, int C) {
+  int64_t c = ((g + 1) * C + W - 1) / W - 1;
   if (c < 0) c = 0;
-  if (c > G - 1) c = G - 1;
+  if (c > C - 1) c = C - 1;
   return static_cast<int>(c);
 }
 
-// Stream-K over the work axis (weight tile t, K step ks) -> g = t * KS + ks: CTA c of G
-// runs [c*W/G, (c+1)*W/G).  Every run of one tile inside that range is a segment with
-// its own TMEM accumulator pass; a segment that is a whole tile is stored directly,
-// otherwise it becomes a partial that the CTA finishing the tile last merges.
-__global__ void __launch_bounds__(kFp8Threads, 1)
+// B rows each CTA of the pair holds for a launch tile of T tokens.  With T <= 128 the MMA's
+// B operand is [h tile; l tile] (N = 2T): CTA 0 holds the h plane, CTA 1 the l plane, and
+// the accumulator's column halves are added in the epilogue.  With T > 128 (N would exceed
+// 256) the h and l MMAs (N = T each) accumulate into the same T columns and each CTA holds
+// T/2 tokens of both planes.  Either way a CTA stages T * 128 activation bytes per K step.
+__host__ __device__ constexpr int fp8_acc_cols(int T) { return T <= 128 ? 2 * T : T; }
+// tcgen05.alloc takes a power of two >= 32; two accumulators (double buffering)
+__host__ __device__ constexpr uint32_t fp8_tmem_cols(int T) {
+  uint32_t c = 32;
+  while (c < static_cast<uint32_t>(2 * fp8_acc_cols(T))) c <<= 1;
+  return c;
+}
+
+// One cluster of two CTAs (on two SMs) computes weight-tile pairs: tile pair tp is weight
+// rows [256 tp, 256 tp + 256), CTA r of the pair owns tile t = 2 tp + r.  Stream-K over the
+// work axis (tile pair, K step) -> g = tp * KS + ks: cluster c of C runs [c*W/C, (c+1)*W/C).
+// Every run of one tile pair inside that range is a segment with its own accumulator;
+// segments alternate between two TMEM accumulators, so the MMA warp starts the next
+// segment while the epilogue drains the previous one.  A segment covering a whole tile is
+// stored directly.  Otherwise the pieces of a tile are merged by the CTA that finishes it
+// last: straight from its TMEM when the sibling pieces are already stored (the usual case
+// at the end of a range), or from the stored partials.
+//
+// Pipeline.  Each CTA's producer streams its own weight tile and its half of the
+// activation tile into its ring; both CTAs' loads count on the leader CTA's full barrier.
+// The leader's MMA warp issues the pair MMAs and commits to the empty barriers of both
+// CTAs (and to both CTAs' accumulator barriers at the end of a segment); each CTA's four
+// epilogue warps read their own TMEM lanes, arrive on the leader's acc_empty barrier and
+// write y through shared memory with TMA stores.
+__global__ void __launch_bounds__(kFp8Threads, 2)
     fp8_linear_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap hmap,
-                      const __grid_constant__ CUtensorMap lmap, const Fp8Params p) {
+                      const __grid_constant__ CUtensorMap lmap, const __grid_constant__ CUtensorMap ymap,
+                      const Fp8Params p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[8];
   __shared__ __align__(8) uint64_t empty[8];
-  __shared__ __align__(8) uint64_t acc_full;
-  __shared__ __align__(8) uint64_t acc_empty;
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   __shared__ int last_flag;
@@ -173,79 +270,83 @@ __global__ void __launch_bounds__(kFp8Threads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
   const int T = p.tok_tile;
   const int S = p.stages;
-  const uint32_t w_bytes = kTileN * kTileK;  // 16 KiB
-  const uint32_t x_bytes = static_cast<uint32_t>(T) * kTileK;
-  const uint32_t stage_bytes = w_bytes + 2 * x_bytes;  // multiple of 1024
+  const bool merged = T <= 128;
+  const uint32_t w_bytes = kTileN * kTileK;                    // 16 KiB
+  const uint32_t x_bytes = static_cast<uint32_t>(T) * kTileK;  // this CTA's activation rows
+  const uint32_t stage_bytes = w_bytes + x_bytes;              // multiple of 1024
   const int KS = (p.k + kTileK - 1) / kTileK;
   const int NT = (p.n + kTileN - 1) / kTileN;
-  const int64_t W = static_cast<int64_t>(NT) * KS;
-  const int G = gridDim.x;
-  const int64_t g0 = static_cast<int64_t>(blockIdx.x) * W / G;
-  const int64_t g1 = static_cast<int64_t>(blockIdx.x + 1) * W / G;
+  const int NP = (NT + 1) / 2;
+  const int64_t W = static_cast<int64_t>(NP) * KS;
+  const int C = gridDim.x / 2;
+  const int cl = blockIdx.x / 2;
+  const int64_t g0 = static_cast<int64_t>(cl) * W / C;
+  const int64_t g1 = static_cast<int64_t>(cl + 1) * W / C;
   const int n_units = static_cast<int>(g1 - g0);
-
-  // Accumulator plan.  With T <= 128 the h and l tiles (adjacent in shared memory) form
-  // one B operand of N = 2T rows, so one MMA covers both planes; consecutive MMAs rotate
-  // over `chains` independent accumulators so they do not wait on each other.  With
-  // T = 256 (N would exceed 256) h and l go to two accumulators of 256 columns.
-  const bool merged = T <= 128;
-  const int n_mma = merged ? 2 * T : T;
-  int chains = merged ? 256 / n_mma : 1;
-  if (chains > 4) chains = 4;
-  if (chains < 1) chains = 1;
-  uint32_t ncols = 32;  // tcgen05.alloc takes a power of two >= 32
-  while (ncols < (merged ? static_cast<uint32_t>(chains * n_mma) : 512u)) ncols <<= 1;
+  const uint32_t acc_cols = static_cast<uint32_t>(fp8_acc_cols(T));
+  const uint32_t ncols = fp8_tmem_cols(T);
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(&acc_full, 1);
-    mbar_init(&acc_empty, 4);  // one arrival per epilogue warp
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);  // one arrival per epilogue warp of both CTAs
+    }
     abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_base, ncols);
-    tmem_relinquish();
+    tmem_alloc_pair(&tmem_base, ncols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // barrier inits and the TMEM address are visible to both CTAs
   tc_fence_after();
   const uint32_t tmem = tmem_base;
   volatile int* vabort = &abort_flag;
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer
-      if (p.w_packed == nullptr) prefetch_tensormap(&wmap);
+      // ---------------- TMA producer (both CTAs)
+      prefetch_tensormap(&wmap);
       prefetch_tensormap(&hmap);
       prefetch_tensormap(&lmap);
       const uint64_t pol_w = l2_policy_evict_first();
       uint64_t pol_x;
       asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_x));
-      auto load_w = [&](uint8_t* st, int64_t g, uint64_t* bar) {
-        const int t = static_cast<int>(g / KS), ks = static_cast<int>(g - static_cast<int64_t>(t) * KS);
-        if (p.w_packed != nullptr) bulk_load(st, p.w_packed + g * w_bytes, w_bytes, bar, pol_w);
-        else tma_load_2d(st, &wmap, ks * kTileK, t * kTileN, bar, pol_w);
+      const int x_row = merged ? p.tok0 : p.tok0 + static_cast<int>(rank) * (T / 2);
+      auto load_w = [&](uint8_t* st, int64_t g, uint32_t bar) {
+        const int tp = static_cast<int>(g / KS), ks = static_cast<int>(g - static_cast<int64_t>(tp) * KS);
+        const int t = 2 * tp + static_cast<int>(rank);
+        if (p.w_packed) tma_load_2d_pair(st, &wmap, 0, (t * KS + ks) * kTileN, bar, pol_w);
+        else tma_load_2d_pair(st, &wmap, ks * kTileK, t * kTileN, bar, pol_w);
       };
-      auto load_x = [&](uint8_t* st, int64_t g, uint64_t* bar) {
+      auto load_x = [&](uint8_t* st, int64_t g, uint32_t bar) {
         const int ks = static_cast<int>(g % KS);
-        tma_load_2d(st + w_bytes, &hmap, ks * kTileK, p.tok0, bar, pol_x);
-        tma_load_2d(st + w_bytes + x_bytes, &lmap, ks * kTileK, p.tok0, bar, pol_x);
+        if (merged) {
+          tma_load_2d_pair(st + w_bytes, leader ? &hmap : &lmap, ks * kTileK, x_row, bar, pol_x);
+        } else {
+          tma_load_2d_pair(st + w_bytes, &hmap, ks * kTileK, x_row, bar, pol_x);
+          tma_load_2d_pair(st + w_bytes + x_bytes / 2, &lmap, ks * kTileK, x_row, bar, pol_x);
+        }
       };
+      auto full_of = [&](int s) { return cluster_addr(smem_u32(&full[s]), 0); };
       // The weight tiles of the first ring do not depend on the activation split: issue
       // them before waiting for it.
       const int first = n_units < S ? n_units : S;
       for (int j = 0; j < first; ++j) {
-        mbar_arrive_expect_tx(&full[j], stage_bytes);
-        load_w(smem + j * stage_bytes, g0 + j, &full[j]);
+        if (leader) mbar_arrive_expect_tx(&full[j], 2 * stage_bytes);
+        load_w(smem + j * stage_bytes, g0 + j, full_of(j));
       }
       grid_dependency_wait();
-      for (int j = 0; j < first; ++j) load_x(smem + j * stage_bytes, g0 + j, &full[j]);
+      for (int j = 0; j < first; ++j) load_x(smem + j * stage_bytes, g0 + j, full_of(j));
       for (int j = first; j < n_units; ++j) {
         const int s = j % S;
         if (*vabort) break;
@@ -255,143 +356,201 @@ __global__ void __launch_bounds__(kFp8Threads, 1)
           break;
         }
         uint8_t* st = smem + s * stage_bytes;
-        mbar_arrive_expect_tx(&full[s], stage_bytes);
-        load_w(st, g0 + j, &full[s]);
-        load_x(st, g0 + j, &full[s]);
+        if (leader) mbar_arrive_expect_tx(&full[s], 2 * stage_bytes);
+        load_w(st, g0 + j, full_of(s));
+        load_x(st, g0 + j, full_of(s));
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------- MMA issuer: the whole warp walks the loop, one elected lane issues
-    const uint32_t idesc = f8_idesc(n_mma);
-    int seg = 0;        // segments started
-    int in_seg = 0;     // MMAs issued in the current segment
-    for (int j = 0; j < n_units; ++j) {
-      const int64_t g = g0 + j;
-      const int ks = static_cast<int>(g % KS);
-      const bool seg_begin = (j == 0) || (ks == 0);
-      const bool seg_end = (j == n_units - 1) || (ks == KS - 1);
-      // Waits are done by lane 0 and broadcast, so every branch below is warp-uniform
-      // (elect.sync needs the whole warp).
-      if (seg_begin) {
-        // the previous segment's accumulator must have been read out
-        if (seg > 0) {
-          int w_ok = 1;
-          if (lane == 0 && !*vabort) {
-            w_ok = mbar_wait(&acc_empty, (seg - 1) & 1u) ? 1 : 0;
-            if (!w_ok) {
-              report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
-              *vabort = 1;
+    if (leader) {
+      // ---------------- MMA issuer: the whole warp walks the loop, one elected lane issues
+      const uint32_t idesc = f8_idesc_pair(merged ? 2 * T : T);
+      int seg = 0;        // segments started
+      int in_seg = 0;     // K steps issued in the current segment
+      uint32_t acc = tmem;
+      for (int j = 0; j < n_units; ++j) {
+        const int64_t g = g0 + j;
+        const int ks = static_cast<int>(g % KS);
+        const bool seg_begin = (j == 0) || (ks == 0);
+        const bool seg_end = (j == n_units - 1) || (ks == KS - 1);
+        // Waits are done by lane 0 and broadcast, so every branch below is warp-uniform
+        // (elect.sync needs the whole warp).
+        if (seg_begin) {
+          const int buf = seg & 1;
+          // this buffer's previous segment (two back) must have been read out by both CTAs
+          if (seg >= 2) {
+            int w_ok = 1;
+            if (lane == 0 && !*vabort) {
+              w_ok = mbar_wait(&acc_empty[buf], ((seg >> 1) - 1) & 1u) ? 1 : 0;
+              if (!w_ok) {
+                report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+                *vabort = 1;
+              }
             }
+            __shfl_sync(0xffffffffu, w_ok, 0);
           }
-          __shfl_sync(0xffffffffu, w_ok, 0);
+          acc = tmem + static_cast<uint32_t>(buf) * acc_cols;
+          in_seg = 0;
+          tc_fence_after();
         }
-        in_seg = 0;
-        tc_fence_after();
-      }
-      const int s = j % S;
-      int ok = 0;
-      if (lane == 0 && !*vabort) {
-        ok = mbar_wait(&full[s], (j / S) & 1u) ? 1 : 0;
-        if (!ok) {
-          report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
-          *vabort = 1;
+        const int s = j % S;
+        int ok = 0;
+        if (lane == 0 && !*vabort) {
+          ok = mbar_wait(&full[s], (j / S) & 1u) ? 1 : 0;
+          if (!ok) {
+            report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+            *vabort = 1;
+          }
         }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (ok && elect_one()) {
-        tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + s * stage_bytes);
-        const uint32_t h0 = a0 + w_bytes, l0 = h0 + x_bytes;
-        int cnt = in_seg;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (ok && elect_one()) {
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + s * stage_bytes);
+          const uint32_t b0 = a0 + w_bytes;
 #pragma unroll
-        for (int kk = 0; kk < kTileK / kMmaK; ++kk) {
-          const uint64_t ad = sw128_desc(a0 + kk * kMmaK);
-          if (merged) {
-            const int c = cnt % chains;
-            mma_f8(tmem + static_cast<uint32_t>(c * n_mma), ad, sw128_desc(h0 + kk * kMmaK), idesc,
-                   cnt >= chains);
-          } else {
-            mma_f8(tmem, ad, sw128_desc(h0 + kk * kMmaK), idesc, cnt > 0);
-            mma_f8(tmem + 256u, ad, sw128_desc(l0 + kk * kMmaK), idesc, cnt > 0);
+          for (int kk = 0; kk < kTileK / kMmaK; ++kk) {
+            const uint64_t ad = sw128_desc(a0 + kk * kMmaK);
+            const uint32_t accumulate = (in_seg | kk) != 0 ? 1u : 0u;
+            mma_f8_pair(acc, ad, sw128_desc(b0 + kk * kMmaK), idesc, accumulate);
+            if (!merged) mma_f8_pair(acc, ad, sw128_desc(b0 + x_bytes / 2 + kk * kMmaK), idesc, 1u);
           }
-          ++cnt;
+          mma_commit_pair(&empty[s]);  // stage s free in both CTAs once these MMAs have read it
         }
-        mma_commit(&empty[s]);  // stage s free once these MMAs have read it
-      }
-      __syncwarp();
-      in_seg += kTileK / kMmaK;
-      if (seg_end) {
-        if (elect_one()) mma_commit(&acc_full);  // segment accumulator complete
         __syncwarp();
-        ++seg;
+        ++in_seg;
+        if (seg_end) {
+          if (elect_one()) mma_commit_pair(&acc_full[seg & 1]);  // segment accumulator complete
+          __syncwarp();
+          ++seg;
+        }
       }
     }
   } else {
-    // ---------------- epilogue warps 2..5: TMEM lane quarter q = warp % 4
+    // ---------------- epilogue warps 2..5 (both CTAs): TMEM lane quarter q = warp % 4
     const int q = warp & 3;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const int ep = tid - 64;  // 0..127 among the epilogue threads
-    grid_dependency_wait();   // x_scale comes from the split grid
+    const int row = q * 32 + lane;
+    // per-warp output staging for the TMA stores, and the launch tile's token scales
+    __nv_bfloat16* ystage = reinterpret_cast<__nv_bfloat16*>(smem + S * stage_bytes) + (warp - 2) * 4 * kEpiBlockElems;
+    float* xsm = reinterpret_cast<float*>(smem + S * stage_bytes + 4 * 4 * kEpiBlockElems * 2);
+    int ychunk = 0;  // store groups committed by this warp
+    if (lane == 0 && p.y_tma) prefetch_tensormap(&ymap);
+    grid_dependency_wait();  // x_scale comes from the split grid
+    for (int i = ep; i < T; i += 128) xsm[i] = p.tok0 + i < p.m ? __ldg(p.x_scale + p.tok0 + i) : 0.f;
+    named_barrier_sync(1, 128);
     int seg = 0;
     int64_t g = g0;
     while (g < g1) {
-      const int t = static_cast<int>(g / KS);
-      const int64_t t_begin = static_cast<int64_t>(t) * KS, t_end = t_begin + KS;
+      const int tp = static_cast<int>(g / KS);
+      const int t = 2 * tp + static_cast<int>(rank);
+      const int64_t t_begin = static_cast<int64_t>(tp) * KS, t_end = t_begin + KS;
       const int64_t s_end = g1 < t_end ? g1 : t_end;
       const bool whole = (g == t_begin) && (s_end == t_end);
-      const int live = merged ? (static_cast<int>(s_end - g) * (kTileK / kMmaK) < chains
-                                     ? static_cast<int>(s_end - g) * (kTileK / kMmaK)
-                                     : chains)
-                              : 1;
-      bool ok = !*vabort && mbar_wait(&acc_full, seg & 1u);
+      const int buf = seg & 1;
+      bool ok = !*vabort && mbar_wait(&acc_full[buf], (seg >> 1) & 1u);
       if (!ok && !*vabort) {
         report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
         *vabort = 1;
       }
       tc_fence_after();
-      const int row = q * 32 + lane;
+      const uint32_t acc = lane_base + static_cast<uint32_t>(buf) * acc_cols;
       const int n_idx = t * kTileN + row;
       const float sw = (n_idx < p.n) ? __ldg(p.w_scale + n_idx) : 0.f;
-      const int64_t slot = static_cast<int64_t>(blockIdx.x) + t;
-      float* prow = p.part + slot * static_cast<int64_t>(T) * kTileN + row;
-      for (int c0 = 0; c0 < T; c0 += 16) {
-        float acc[16];
+      const int c_first = whole ? cl : fp8_cluster_of(t_begin, W, C);
+      const int c_last = whole ? cl : fp8_cluster_of(t_end - 1, W, C);
+      // A partial segment whose sibling pieces are all stored already is merged straight
+      // from TMEM, without storing and re-reading its own piece.
+      bool merge_now = whole;
+      if (!whole) {
+        if (ep == 0) last_flag = atomicAdd(p.counters + t, 0) == c_last - c_first ? 1 : 0;
+        named_barrier_sync(1, 128);
+        merge_now = last_flag != 0;
+        if (merge_now) __threadfence();
+      }
+      if (merge_now) {
+        // y = s_w * 2^e * (own accumulator + the stored sibling pieces), 32 tokens per step
+        for (int c0 = 0; c0 < T; c0 += 32) {
+          const bool wide = T - c0 >= 32;
+          uint32_t vr[32];  // accumulator values (fp32 bits)
+          {
+            uint32_t rl[32];
+            if (wide) {
+              tmem_ld32(acc + static_cast<uint32_t>(c0), vr);
+              if (merged) tmem_ld32(acc + static_cast<uint32_t>(T + c0), rl);
+            } else {
+              tmem_ld16(acc + static_cast<uint32_t>(c0), vr);
+              if (merged) tmem_ld16(acc + static_cast<uint32_t>(T + c0), rl);
+            }
+            tmem_ld_wait();
+            if (merged) {
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) acc[jj] = 0.f;
-        const int parts = merged ? 2 * live : 2;
-        for (int qq = 0; qq < parts; ++qq) {
-          const uint32_t col = merged ? static_cast<uint32_t>((qq >> 1) * n_mma + (qq & 1) * T + c0)
-                                      : static_cast<uint32_t>((qq & 1) * 256 + c0);
-          uint32_t r[16];
-          tmem_ld16(lane_base + col, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) acc[jj] += __uint_as_float(r[jj]);
-        }
-        if (whole) {
-          if (n_idx < p.n) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const int m = p.tok0 + c0 + jj;
-              if (m < p.m)
-                p.y[static_cast<int64_t>(m) * p.n + n_idx] =
-                    __float2bfloat16_rn(acc[jj] * sw * __ldg(p.x_scale + m));
+              for (int jj = 0; jj < 32; ++jj) vr[jj] = __float_as_uint(__uint_as_float(vr[jj]) + __uint_as_float(rl[jj]));
             }
           }
-        } else {
+          float* v = reinterpret_cast<float*>(vr);
+          if (!whole) {
+            for (int cc = c_first; cc <= c_last; ++cc) {
+              if (cc == cl) continue;
+              const float* src = p.part + (2 * (static_cast<int64_t>(cc) + tp) + rank) * T * kTileN +
+                                 static_cast<int64_t>(c0) * kTileN + row;
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) prow[static_cast<int64_t>(c0 + jj) * kTileN] = acc[jj];
+              for (int jj = 0; jj < 32; ++jj)
+                if (jj < 16 || wide) v[jj] += __ldcg(src + jj * kTileN);
+            }
+          }
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) v[jj] *= sw * xsm[c0 + (jj < 16 || wide ? jj : 0)];
+          const int n0 = t * kTileN + q * 32, m0 = p.tok0 + c0;
+          if (p.y_tma) {
+            if (n0 < p.n && m0 < p.m) {
+              // blocks [16 tokens][32 rows] of y in shared memory, then TMA stores
+              __nv_bfloat16* blk = ystage + (ychunk & 1) * 2 * kEpiBlockElems;
+              if (lane == 0) bulk_wait_read_le1();  // the group that last read these blocks is done
+              __syncwarp();
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj)
+                if (jj < 16 || wide) blk[jj * 32 + lane] = __float2bfloat16_rn(v[jj]);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&ymap, blk, n0, m0);
+                if (wide && m0 + 16 < p.m) tma_store_2d(&ymap, blk + kEpiBlockElems, n0, m0 + 16);
+                bulk_commit_group();
+              }
+              ++ychunk;
+            }
+          } else if (n_idx < p.n) {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) {
+              const int m = m0 + jj;
+              if ((jj < 16 || wide) && m < p.m) p.y[static_cast<int64_t>(m) * p.n + n_idx] = __float2bfloat16_rn(v[jj]);
+            }
+          }
+        }
+        if (!whole && ep == 0) p.counters[t] = 0;
+      } else {
+        const int64_t slot = 2 * (static_cast<int64_t>(cl) + tp) + rank;
+        float* prow = p.part + slot * static_cast<int64_t>(T) * kTileN + row;
+        for (int c0 = 0; c0 < T; c0 += 16) {
+          uint32_t rh[16], rl[16];
+          tmem_ld16(acc + static_cast<uint32_t>(c0), rh);
+          if (merged) tmem_ld16(acc + static_cast<uint32_t>(T + c0), rl);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj)
+            prow[static_cast<int64_t>(c0 + jj) * kTileN] =
+                merged ? __uint_as_float(rh[jj]) + __uint_as_float(rl[jj]) : __uint_as_float(rh[jj]);
         }
       }
-      // accumulator read out: the MMA warp may start the next segment
+      // accumulator read out: the leader's MMA warp may reuse this buffer
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty);
-      if (!whole) {
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(smem_u32(&acc_empty[buf]), 0));
+      if (!merge_now) {
         __threadfence();
         named_barrier_sync(1, 128);
-        const int c_first = fp8_cta_of(t_begin, W, G), c_last = fp8_cta_of(t_end - 1, W, G);
         if (ep == 0) {
           const int prev = atomicAdd(p.counters + t, 1);
           last_flag = (prev == c_last - c_first) ? 1 : 0;
@@ -399,50 +558,53 @@ __global__ void __launch_bounds__(kFp8Threads, 1)
         named_barrier_sync(1, 128);
         if (last_flag) {
           __threadfence();
-          // merge the tile's partials: pieces from CTAs c_first..c_last, slots cc + t;
-          // 16 independent loads per piece keep the merge off the load-latency chain
+          // the siblings finished meanwhile: merge every piece, this one included
           for (int c0 = 0; c0 < T; c0 += 16) {
             float sum[16];
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) sum[jj] = 0.f;
             for (int cc = c_first; cc <= c_last; ++cc) {
-              const float* src = p.part + (static_cast<int64_t>(cc) + t) * T * kTileN +
+              const float* src = p.part + (2 * (static_cast<int64_t>(cc) + tp) + rank) * T * kTileN +
                                  static_cast<int64_t>(c0) * kTileN + row;
-              float v[16];
+              float o[16];
 #pragma unroll
-              for (int jj = 0; jj < 16; ++jj) v[jj] = __ldcg(src + jj * kTileN);
+              for (int jj = 0; jj < 16; ++jj) o[jj] = __ldcg(src + jj * kTileN);
 #pragma unroll
-              for (int jj = 0; jj < 16; ++jj) sum[jj] += v[jj];
+              for (int jj = 0; jj < 16; ++jj) sum[jj] += o[jj];
             }
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
               const int m = p.tok0 + c0 + jj;
               if (m < p.m && n_idx < p.n)
-                p.y[static_cast<int64_t>(m) * p.n + n_idx] =
-                    __float2bfloat16_rn(sum[jj] * sw * __ldg(p.x_scale + m));
+                p.y[static_cast<int64_t>(m) * p.n + n_idx] = __float2bfloat16_rn(sum[jj] * sw * xsm[c0 + jj]);
             }
           }
           if (ep == 0) p.counters[t] = 0;
         }
-        named_barrier_sync(1, 128);
       }
+      named_barrier_sync(1, 128);  // last_flag is rewritten by the next segment
       ++seg;
       g = s_end;
     }
+    if (lane == 0 && ychunk > 0) bulk_wait_all();  // y written before the CTA retires
+    __syncwarp();
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, ncols);
-  }
-  // never leave with a TMA write in flight (only possible after an abort)
-  if (*vabort && tid == 0) {
+  // never leave with a TMA write in flight (only possible after an abort): both CTAs'
+  // bytes count on the leader's full barriers
+  if (leader && tid == 0 && *vabort) {
     for (int s = 0; s < S && s < n_units; ++s) {
       const int rounds = (n_units - s + S - 1) / S;
       mbar_wait(&full[s], (rounds - 1) & 1u);
     }
+  }
+  // neither CTA leaves while the pair's MMAs or loads may still touch its shared memory
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, ncols);
   }
 }
 
@@ -593,61 +755,71 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const uint8_t* __rest
 }
 
 // ---------------------------------------------------------------- host side
-inline int encode_u8_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                         uint32_t box_rows) {
+// 2-D tensor map over a row-major [rows, cols] array of 1-byte (u8) or 2-byte (bf16)
+// elements with a (box_cols x box_rows) box; 128-byte swizzle optional.
+struct MapKey {
+  const void* base;
+  uint64_t rows, cols;
+  uint32_t box_cols, box_rows;
+  int elem_bytes;
+  bool swizzle;
+  int dev;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && box_cols == o.box_cols &&
+           box_rows == o.box_rows && elem_bytes == o.elem_bytes && swizzle == o.swizzle && dev == o.dev;
+  }
+};
+
+inline int encode_map(CUtensorMap* map, const MapKey& k) {
   EncodeTiledFn enc = encode_tiled_fn();
   if (enc == nullptr) return INFERD_ERR_CUDA;
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileK), box_rows};
+  cuuint64_t dims[2] = {k.cols, k.rows};
+  cuuint64_t strides[1] = {k.cols * static_cast<uint64_t>(k.elem_bytes)};
+  cuuint32_t box[2] = {k.box_cols, k.box_rows};
   cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
-                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  const CUresult r = enc(map, k.elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                         const_cast<void*>(k.base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         k.swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? INFERD_OK : INFERD_ERR_CUDA;
 }
 
-// Small cache of encoded tensor maps keyed by (base, rows, cols, box rows, device):
-// encoding costs microseconds of host time per map.
-struct U8MapCache {
+// Small cache of encoded tensor maps: encoding costs microseconds of host time per map.
+struct MapCache {
   std::mutex mu;
   struct Entry {
-    const void* base;
-    uint64_t rows, cols;
-    uint32_t box_rows;
-    int dev;
+    MapKey key;
     CUtensorMap map;
-  } e[32];
+  } e[48];
   int n = 0, next = 0;
 };
-U8MapCache g_u8maps;
+MapCache g_maps;
 
-inline int cached_u8_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                         uint32_t box_rows) {
-  const int dev = current_device();
+inline int cached_map(CUtensorMap* map, const MapKey& key) {
   {
-    std::lock_guard<std::mutex> lock(g_u8maps.mu);
-    for (int i = 0; i < g_u8maps.n; ++i) {
-      const U8MapCache::Entry& c = g_u8maps.e[i];
-      if (c.base == base && c.rows == rows && c.cols == cols && c.box_rows == box_rows && c.dev == dev) {
-        *map = c.map;
+    std::lock_guard<std::mutex> lock(g_maps.mu);
+    for (int i = 0; i < g_maps.n; ++i) {
+      if (g_maps.e[i].key == key) {
+        *map = g_maps.e[i].map;
         return INFERD_OK;
       }
     }
   }
-  const int st = encode_u8_map(map, base, rows, cols, box_rows);
+  const int st = encode_map(map, key);
   if (st != INFERD_OK) return st;
-  std::lock_guard<std::mutex> lock(g_u8maps.mu);
-  U8MapCache::Entry& c = g_u8maps.e[g_u8maps.next];
-  c.base = base;
-  c.rows = rows;
-  c.cols = cols;
-  c.box_rows = box_rows;
-  c.dev = dev;
-  c.map = *map;
-  g_u8maps.next = (g_u8maps.next + 1) % 32;
-  if (g_u8maps.n < 32) ++g_u8maps.n;
+  std::lock_guard<std::mutex> lock(g_maps.mu);
+  g_maps.e[g_maps.next].key = key;
+  g_maps.e[g_maps.next].map = *map;
+  g_maps.next = (g_maps.next + 1) % 48;
+  if (g_maps.n < 48) ++g_maps.n;
   return INFERD_OK;
+}
+
+// e4m3 planes and weights: 128-byte rows per box row
+inline int cached_u8_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                         bool swizzle = true) {
+  return cached_map(map, MapKey{base, rows, cols, static_cast<uint32_t>(kTileK), box_rows, 1, swizzle,
+                                current_device()});
 }
 
 inline size_t align256_fp8(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
@@ -661,24 +833,35 @@ constexpr size_t kFp8CounterBytes = kMaxTilesFp8 * sizeof(int32_t);
 struct Fp8Plan {
   int tile;      // tokens per launch tile (multiple of 16)
   int stages;    // ring depth
-  int grid;      // CTAs (stream-K)
+  int per_sm;    // co-resident CTAs per SM
+  int clusters;  // CTA pairs; the grid is 2 * clusters
   size_t smem;   // dynamic shared memory per CTA
 };
+
+// Weight-tile pairs of an [n, k] weight.
+inline int64_t fp8_pairs(int64_t n) { return ((n + kTileN - 1) / kTileN + 1) / 2; }
 
 inline Fp8Plan fp8_plan(int64_t rem_tokens, int64_t n, int64_t k, int sms) {
   Fp8Plan pl;
   const int64_t t = rem_tokens < kMaxTokTile ? rem_tokens : kMaxTokTile;
   pl.tile = static_cast<int>((t + 15) / 16 * 16);
-  const int per_sm = pl.tile <= 128 ? 2 : 1;           // TMEM and smem allow two CTAs up to 128 tokens
-  const int budget = per_sm == 2 ? 104 * 1024 : kSmemBudget;
-  const int stage_bytes = kTileN * kTileK + 2 * pl.tile * kTileK;
-  pl.stages = budget / stage_bytes;
+  // two CTAs per SM while both double-buffered accumulators fit TMEM's 512 columns
+  pl.per_sm = 2 * fp8_tmem_cols(pl.tile) <= 512 ? 2 : 1;
+  const int budget = pl.per_sm == 2 ? kSmemBudget2 : kSmemBudget;
+  const int stage_bytes = kTileN * kTileK + pl.tile * kTileK;
+  pl.stages = (budget - kEpiStageBytes) / stage_bytes;
   if (pl.stages > 8) pl.stages = 8;
-  const int64_t work = ((n + kTileN - 1) / kTileN) * ((k + kTileK - 1) / kTileK);
-  int64_t g = static_cast<int64_t>(sms) * per_sm;
-  if (g > work) g = work;
-  pl.grid = static_cast<int>(g);
-  pl.smem = 1024 + static_cast<size_t>(pl.stages) * stage_bytes;
+  const int64_t pairs = fp8_pairs(n);
+  const int64_t work = pairs * ((k + kTileK - 1) / kTileK);
+  int64_t c = static_cast<int64_t>(sms / 2) * pl.per_sm;
+  // at least four K steps per cluster, so small problems are not cut into many pieces
+  const int64_t cap = work / 4 > 0 ? work / 4 : 1;
+  if (c > cap) c = cap;
+  // whole tile pairs per cluster (no partials to merge) when that still keeps three
+  // quarters of the clusters busy
+  if (pairs <= c && 4 * pairs >= 3 * c) c = pairs;
+  pl.clusters = static_cast<int>(c);
+  pl.smem = 1024 + static_cast<size_t>(pl.stages) * stage_bytes + kEpiStageBytes;
   return pl;
 }
 
@@ -693,9 +876,45 @@ inline Fp8Workspace fp8_workspace(int64_t m, int64_t n, int64_t k, int sms) {
   w.scale = w.l + align256_fp8(static_cast<size_t>(m * k));
   w.part = w.scale + align256_fp8(static_cast<size_t>(m) * 4);
   const Fp8Plan pl = fp8_plan(m, n, k, sms);  // the first launch tile is the largest
-  const int64_t tiles = (n + kTileN - 1) / kTileN;
-  w.total = w.part + align256_fp8(static_cast<size_t>(pl.grid + tiles) * pl.tile * kTileN * 4);
+  w.total = w.part + align256_fp8(static_cast<size_t>(2 * (pl.clusters + fp8_pairs(n))) * pl.tile * kTileN * 4);
   return w;
+}
+
+// Clusters of two CTAs with `smem` dynamic shared memory that can be resident at once on
+// the current device (0 when the query fails); cached per (device, smem).
+inline int max_active_clusters(size_t smem) {
+  static std::mutex mu;
+  static struct Entry {
+    int dev;
+    size_t smem;
+    int n;
+  } cache[32];
+  static int count = 0;
+  const int dev = current_device();
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < count; ++i)
+      if (cache[i].dev == dev && cache[i].smem == smem) return cache[i].n;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(kFp8Threads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, fp8_linear_kernel, &cfg) != cudaSuccess || n < 0) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (count < 32) cache[count++] = Entry{dev, smem, n};
+  return n;
 }
 
 }  // namespace
@@ -741,7 +960,7 @@ extern "C" int inferd_fp8_quantize_per_channel(const void* w, int32_t w_dtype, v
 
 extern "C" size_t inferd_fp8_packed_weight_bytes(int64_t n, int64_t k) {
   if (n <= 0 || k <= 0) return 0;
-  const int64_t nt = (n + kTileN - 1) / kTileN, kt = (k + kTileK - 1) / kTileK;
+  const int64_t nt = 2 * fp8_pairs(n), kt = (k + kTileK - 1) / kTileK;  // whole tile pairs
   return static_cast<size_t>(nt * kt) * kTileN * kTileK;
 }
 
@@ -789,7 +1008,7 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
     cudaError_t e =
         cudaFuncSetAttribute(fp8_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 1024);
     if (e != cudaSuccess) return cuda_status(e);
-    // all of the unified L1/shared array as shared memory, so two 100 KB CTAs fit per SM;
+    // all of the unified L1/shared array as shared memory, so two ~110 KB CTAs fit per SM;
     // the split kernel asks for the same carveout, so the SMs are not reconfigured
     // between the two launches of every call
     e = cudaFuncSetAttribute(fp8_linear_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -808,23 +1027,38 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
   int st = INFERD_OK;
   if (w_layout == 0) {
     st = cached_u8_map(&wmap, w_e4m3, static_cast<uint64_t>(n), static_cast<uint64_t>(k), kTileN);
+  } else {
+    // packed tiles are already in shared-memory form: copy them verbatim as 128-byte rows
+    const uint64_t rows = static_cast<uint64_t>(inferd_fp8_packed_weight_bytes(n, k)) / kTileK;
+    st = cached_u8_map(&wmap, w_e4m3, rows, kTileK, kTileN, false);
+  }
+  if (st != INFERD_OK) return st;
+  // y through TMA stores when its rows are 16-byte multiples at a 16-byte aligned base
+  CUtensorMap ymap;
+  const bool y_tma = (n * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+  if (y_tma) {
+    st = cached_map(&ymap, MapKey{y, static_cast<uint64_t>(m), static_cast<uint64_t>(n), 32, 16, 2, false,
+                                  current_device()});
     if (st != INFERD_OK) return st;
   } else {
-    memset(&wmap, 0, sizeof(wmap));  // unused: packed tiles are bulk-copied
+    memset(&ymap, 0, sizeof(ymap));
   }
   CUtensorMap hmaps[2], lmaps[2];  // full tiles share one map; a last partial tile its own
   int tiles[2];
   for (int i = 0; i < 2; ++i) {
-    const int64_t rem = i == 0 ? (m < kMaxTokTile ? m : kMaxTokTile) : m - static_cast<int64_t>(n_tok_tiles - 1) * kMaxTokTile;
+    const int64_t rem =
+        i == 0 ? (m < kMaxTokTile ? m : kMaxTokTile) : m - static_cast<int64_t>(n_tok_tiles - 1) * kMaxTokTile;
     tiles[i] = static_cast<int>((rem + 15) / 16 * 16);
-    st = cached_u8_map(&hmaps[i], h, static_cast<uint64_t>(m), static_cast<uint64_t>(k), static_cast<uint32_t>(tiles[i]));
+    // rows each CTA of the pair loads per plane: the whole tile, or half of it above 128
+    const uint32_t box = static_cast<uint32_t>(tiles[i] <= 128 ? tiles[i] : tiles[i] / 2);
+    st = cached_u8_map(&hmaps[i], h, static_cast<uint64_t>(m), static_cast<uint64_t>(k), box);
     if (st != INFERD_OK) return st;
-    st = cached_u8_map(&lmaps[i], l, static_cast<uint64_t>(m), static_cast<uint64_t>(k), static_cast<uint32_t>(tiles[i]));
+    st = cached_u8_map(&lmaps[i], l, static_cast<uint64_t>(m), static_cast<uint64_t>(k), box);
     if (st != INFERD_OK) return st;
   }
 
   split_activations_kernel<<<static_cast<unsigned>(m), kSplitThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
-                                                                   static_cast<int>(k), h, l, xs);
+                                                                             static_cast<int>(k), h, l, xs);
   st = launch_status();
   if (st != INFERD_OK) return st;
 
@@ -832,33 +1066,40 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
     const int which = (t == n_tok_tiles - 1) ? 1 : 0;
     const Fp8Plan pl = fp8_plan(m - static_cast<int64_t>(t) * kMaxTokTile, n, k, sms);
     const int tile = tiles[which];
-    const int stages = pl.stages;
-    if (stages < 2 || pl.tile != tile) return INFERD_ERR_UNSUPPORTED;
+    if (pl.stages < 2 || pl.tile != tile) return INFERD_ERR_UNSUPPORTED;
+    int clusters = pl.clusters;
+    const int resident = max_active_clusters(pl.smem);
+    if (resident > 0 && clusters > resident) clusters = resident;  // one wave
     Fp8Params p;
-    p.w_packed = w_layout == 1 ? static_cast<const uint8_t*>(w_e4m3) : nullptr;
     p.y = static_cast<__nv_bfloat16*>(y);
     p.w_scale = w_scale;
     p.x_scale = xs;
     p.m = static_cast<int32_t>(m);
     p.n = static_cast<int32_t>(n);
     p.k = static_cast<int32_t>(k);
+    p.w_packed = w_layout == 1 ? 1 : 0;
     p.tok0 = t * kMaxTokTile;
     p.tok_tile = tile;
-    p.stages = stages;
+    p.stages = pl.stages;
     p.counters = counters;
     p.part = part;
     p.error_word = nullptr;
+    p.y_tma = y_tma ? 1 : 0;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(pl.grid);
+    cfg.gridDim = dim3(2 * clusters);
     cfg.blockDim = dim3(kFp8Threads);
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    st = cuda_status(cudaLaunchKernelEx(&cfg, fp8_linear_kernel, wmap, hmaps[which], lmaps[which], p));
+    cfg.numAttrs = 2;
+    st = cuda_status(cudaLaunchKernelEx(&cfg, fp8_linear_kernel, wmap, hmaps[which], lmaps[which], ymap, p));
     if (st != INFERD_OK) return st;
   }
   return INFERD_OK;

@@ -64,9 +64,10 @@ def test_fp8_linear_matches_dequant_matmul(cuda_device, m):
 
 
 def _pack_reference(q: np.ndarray) -> np.ndarray:
-    """numpy statement of the packed tile layout (zero padding, 16-byte chunk swizzle)."""
+    """numpy statement of the packed tile layout (zero padding to whole 256-row tile pairs,
+    16-byte chunk swizzle)."""
     n, k = q.shape
-    nt, kt = -(-n // 128), -(-k // 128)
+    nt, kt = 2 * -(-n // 256), -(-k // 128)
     padded = np.zeros((nt * 128, kt * 128), np.uint8)
     padded[:n, :k] = q
     tiles = padded.reshape(nt, 128, kt, 8, 16).transpose(0, 2, 1, 3, 4)  # [nt, kt, r, c16, b]
