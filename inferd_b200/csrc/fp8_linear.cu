@@ -880,43 +880,6 @@ inline Fp8Workspace fp8_workspace(int64_t m, int64_t n, int64_t k, int sms) {
   return w;
 }
 
-// Clusters of two CTAs with `smem` dynamic shared memory that can be resident at once on
-// the current device (0 when the query fails); cached per (device, smem).
-inline int max_active_clusters(size_t smem) {
-  static std::mutex mu;
-  static struct Entry {
-    int dev;
-    size_t smem;
-    int n;
-  } cache[32];
-  static int count = 0;
-  const int dev = current_device();
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    for (int i = 0; i < count; ++i)
-      if (cache[i].dev == dev && cache[i].smem == smem) return cache[i].n;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2);
-  cfg.blockDim = dim3(kFp8Threads);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, fp8_linear_kernel, &cfg) != cudaSuccess || n < 0) {
-    cudaGetLastError();
-    n = 0;
-  }
-  std::lock_guard<std::mutex> lock(mu);
-  if (count < 32) cache[count++] = Entry{dev, smem, n};
-  return n;
-}
-
 }  // namespace
 }  // namespace inferd
 
@@ -1067,9 +1030,10 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
     const Fp8Plan pl = fp8_plan(m - static_cast<int64_t>(t) * kMaxTokTile, n, k, sms);
     const int tile = tiles[which];
     if (pl.stages < 2 || pl.tile != tile) return INFERD_ERR_UNSUPPORTED;
-    int clusters = pl.clusters;
-    const int resident = max_active_clusters(pl.smem);
-    if (resident > 0 && clusters > resident) clusters = resident;  // one wave
+    // The cluster-occupancy query reports one cluster per SM pair for the two-per-SM
+    // configurations, yet launching two per pair measures faster; stream-K needs no
+    // co-residency, so the grid is not clamped to it.
+    const int clusters = pl.clusters;
     Fp8Params p;
     p.y = static_cast<__nv_bfloat16*>(y);
     p.w_scale = w_scale;
