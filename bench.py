@@ -151,8 +151,11 @@ class DeviceWorkload:
     def __init__(self, workload: str, rank: int, world: int, device: torch.device) -> None:
         w = WORKLOADS[workload]
         self.q_len = w["q_len"]
+        from inferd_b200.sharded import shard_range
+
         all_lens = context_lengths(workload, world)
-        self.base = all_lens[rank * w["seqs"]:(rank + 1) * w["seqs"]].astype(np.int64)
+        lo, hi = shard_range(all_lens.size, world, rank)  # w["seqs"] per rank
+        self.base = all_lens[lo:hi].astype(np.int64)
         self.b = self.base.size
         # context after the append = base + q_len (the appended tokens sit at base .. )
         self.ctx = self.base + self.q_len
@@ -194,6 +197,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
 
     from inferd_b200 import _lib
     from inferd_b200.paged_attn import paged_attention_batched
+    from inferd_b200.sharded import gather_outputs
 
     lib = _lib.load()
     wl = DeviceWorkload(args.workload, rank, world, device)
@@ -222,7 +226,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         if ev is not None:
             ev[1].record(stream)
         if gathered is not None:
-            dist.all_gather_into_tensor(gathered, wl.out)
+            gather_outputs(wl.out, out=gathered)
 
     for _ in range(args.warmup):
         step()
@@ -329,6 +333,7 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
 
     from inferd_b200.paged_attn import paged_attention_batched
     from inferd_b200.paged_cache import PagedKVCache
+    from inferd_b200.sharded import gather_outputs
 
     ql = dwl.q_len
     cache = PagedKVCache(num_layers=1, num_blocks=dwl.num_blocks, block_size=BS,
@@ -366,7 +371,7 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
         out = paged_attention_batched(q, cache.key_cache[0], cache.value_cache[0], bt, cl,
                                       max_context_len=mx)
         if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
+            gather_outputs(out, out=gathered)
             res = gathered
         else:
             res = out
