@@ -103,6 +103,38 @@ class SequencePageTable:
         return [self.blocks[p // bs] * bs + p % bs for p in range(start, start + n)]
 
 
+class _PinnedStaging:
+    """Two reusable pinned host buffers for the small per-step uploads (slots, block tables).
+
+    Pinning a fresh buffer per call is a host allocation of its own; these grow on demand
+    and alternate, and a buffer is rewritten only after the copy that last read it has
+    finished (its event)."""
+
+    def __init__(self, dtype: torch.dtype) -> None:
+        self.dtype = dtype
+        self._bufs: list[torch.Tensor | None] = [None, None]
+        self._events: list[torch.cuda.Event | None] = [None, None]
+        self._next = 0
+
+    def upload(self, arr: np.ndarray, device: torch.device) -> torch.Tensor:
+        i = self._next
+        self._next ^= 1
+        n = int(arr.size)
+        buf = self._bufs[i]
+        if buf is None or buf.numel() < n:
+            buf = torch.empty(max(n, 2 * (0 if buf is None else buf.numel()), 1024),
+                              dtype=self.dtype, pin_memory=True)
+            self._bufs[i] = buf
+        elif self._events[i] is not None:
+            self._events[i].synchronize()
+        buf[:n].numpy()[...] = arr.reshape(-1)
+        out = buf[:n].to(device, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(device))
+        self._events[i] = ev
+        return out
+
+
 class PagedKVCache:
     """Per-layer K/V block pools plus per-sequence page tables (core/paged_cache.py:95-252)."""
 
@@ -133,6 +165,10 @@ class PagedKVCache:
         self.device = torch.device(device)
         self.allocator = BlockAllocator(num_blocks)
         self.sequences: dict[int, SequencePageTable] = {}
+        self._stage_i32 = _PinnedStaging(torch.int32)
+        self._stage_i64 = _PinnedStaging(torch.int64)
+        # decode_metadata's last host table: (seq ids, column capacity, rows, row signatures)
+        self._meta_cache: tuple | None = None
 
         shape = (num_blocks, num_kv_heads, block_size, head_dim)
         self.key_cache = [
@@ -259,10 +295,10 @@ class PagedKVCache:
             raise
 
     def _slot_tensor(self, slots: list[int]) -> torch.Tensor:
-        host = torch.from_numpy(np.asarray(slots, dtype=np.int64))
+        arr = np.asarray(slots, dtype=np.int64)
         if self.device.type != "cuda":
-            return host
-        return host.pin_memory().to(self.device, non_blocking=True)
+            return torch.from_numpy(arr)
+        return self._stage_i64.upload(arr, self.device)
 
     def _write(self, layer: int, keys: torch.Tensor, values: torch.Tensor,
                slots: torch.Tensor) -> None:
@@ -317,16 +353,31 @@ class PagedKVCache:
             if pad_pages < width:
                 raise ValueError("pad_pages is narrower than the widest page table")
             width = pad_pages
-        host = np.zeros((len(tables), width), dtype=np.int32)
-        for i, t in enumerate(tables):
-            host[i, :len(t.blocks)] = t.blocks
-        packed = torch.from_numpy(np.concatenate(
-            [host.reshape(-1), np.asarray(lens, dtype=np.int32)]))
+        b = len(tables)
+        # Page tables change only at their tail (a block appended every block_size tokens,
+        # tail blocks freed on truncation), so a row is rebuilt only when its list object,
+        # length or last block differs from the previous call's.
+        sigs = [(id(t.blocks), len(t.blocks), t.blocks[-1] if t.blocks else -1) for t in tables]
+        key = tuple(seq_ids)
+        cached = self._meta_cache
+        if cached is not None and cached[0] == key and width <= cached[1]:
+            host, old = cached[2], cached[3]
+            for i, t in enumerate(tables):
+                if sigs[i] != old[i]:
+                    host[i, :] = 0
+                    host[i, :len(t.blocks)] = t.blocks
+        else:
+            cap = (width + 63) // 64 * 64  # room to grow without a rebuild
+            host = np.zeros((b, cap), dtype=np.int32)
+            for i, t in enumerate(tables):
+                host[i, :len(t.blocks)] = t.blocks
+        self._meta_cache = (key, host.shape[1], host, sigs)
+        # one upload: the [b, width] tables, then the lengths
+        flat = np.concatenate([host[:, :width].reshape(-1), np.asarray(lens, dtype=np.int32)])
         dev = self.device if device is None else torch.device(device)
-        if dev.type == "cuda":
-            packed = packed.pin_memory().to(dev, non_blocking=True)
-        bt = packed[: len(tables) * width].view(len(tables), width)
-        cl = packed[len(tables) * width:]
+        packed = self._stage_i32.upload(flat, dev) if dev.type == "cuda" else torch.from_numpy(flat)
+        bt = packed[: b * width].view(b, width)
+        cl = packed[b * width:]
         return bt, cl, max(lens + [0])
 
     def sequence_length(self, seq_id: int) -> int:

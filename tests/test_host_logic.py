@@ -8,6 +8,7 @@ kernels themselves are covered by the gpu-marked tests.
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
@@ -196,3 +197,31 @@ def test_truncate_sequence_rolls_back_without_copies():
     assert cache.sequences[0].blocks == [0, 1, 2]  # the freed block is reused first
     assert cache.writes[-1][1] == [5, 6, 7, 8]
     cache.assert_consistent()
+
+
+def test_decode_metadata_incremental_rows_match_rebuild():
+    # the host table is updated row by row between calls; it must always equal a table
+    # rebuilt from the page tables (appends, block-crossing growth, truncation, reordering)
+    cache = RecordingCache(num_layers=1, num_blocks=400, block_size=4, num_kv_heads=1, head_dim=1,
+                           dtype=torch.float32)
+    rng = np.random.default_rng(3)
+    ids = list(range(6))
+    for s in ids:
+        cache.create_sequence(s)
+        n = int(rng.integers(1, 30))
+        cache.append_tokens(s, [torch.zeros(n, 1, 1)], [torch.zeros(n, 1, 1)])
+
+    def rebuilt(order, extra=0):
+        width = max(len(cache.sequences[s].blocks) for s in order)
+        rows = [cache.sequences[s].blocks + [0] * (width - len(cache.sequences[s].blocks)) for s in order]
+        return rows, [cache.sequences[s].length + extra for s in order]
+
+    for step in range(120):
+        cache.append_tokens_batched(ids, [torch.zeros(len(ids), 1, 1)], [torch.zeros(len(ids), 1, 1)])
+        if step % 9 == 4:
+            s = int(rng.integers(0, len(ids)))
+            cache.truncate_sequence(s, max(0, cache.sequence_length(s) - int(rng.integers(1, 9))))
+        order = ids if step % 17 else ids[::-1]
+        bt, cl, mx = cache.decode_metadata(order)
+        rows, lens = rebuilt(order)
+        assert bt.tolist() == rows and cl.tolist() == lens and mx == max(lens)
