@@ -78,7 +78,8 @@ def _pack_reference(q: np.ndarray) -> np.ndarray:
     return out.reshape(-1)
 
 
-@pytest.mark.parametrize("n,k", [(256, 512), (1000, 640), (130, 144)])
+# (384, 256): three weight tiles, so the second tile pair has one tile past N (padded band)
+@pytest.mark.parametrize("n,k", [(256, 512), (1000, 640), (130, 144), (384, 256)])
 def test_pack_layout_and_packed_linear(cuda_device, n, k):
     g = torch.Generator().manual_seed(n + k)
     w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
