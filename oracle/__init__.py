@@ -11,6 +11,8 @@ checker for the CUDA kernels in inferd_b200:
 * per-output-channel e4m3 weight quantisation and dequant-then-matmul (torchao 0.17.0
   Float8WeightOnlyConfig as configured in bench/model_loader.py:46-58; torchao is not
   vendored, so the published per-channel absmax/448 recipe is restated)
+* decode-step sampling: temperature + top-p nucleus probabilities and the inverse-CDF
+  draw                                          core/spec_decode.py:14-35
 
 Parity pins: tests/golden/*.npz hold outputs of the reference itself (imported from its
 source tree by tests/golden/make_golden.py) and of torch's float8_e4m3fn cast; the
@@ -36,4 +38,12 @@ from .fp8 import (  # noqa: F401
     e4m3_encode,
     fp8_linear,
     quantize_per_channel,
+)
+from .sampling import (  # noqa: F401
+    kept_mask_fixed,
+    nucleus_probs,
+    philox4x32_10,
+    row_random64,
+    sample_fixed,
+    to_fixed,
 )

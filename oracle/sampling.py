@@ -1,0 +1,116 @@
+"""CPU restatement of the reference's decode-step sampling -- TEST INFRASTRUCTURE ONLY.
+
+nucleus_probs follows core/spec_decode.py:14-31 step by step in float32: logits / T,
+softmax, descending sort, inclusive cumsum, zero the entries whose exclusive cumulative
+mass exceeds top_p (`cumulative - sorted_probs > top_p`, :26), scatter back, renormalise.
+T <= 0 gives a one-hot row at the argmax (:18-21).  The reference sorts with torch.sort,
+whose order among equal probabilities is unspecified; this restatement uses a stable
+descending order (equal probabilities in index order), one valid instance of it.
+
+sample_from (core/spec_decode.py:34-35) is torch.multinomial; its draws cannot be
+reproduced, so the kernels are checked in two ways: the exact inverse-CDF rule below
+(given the same random bits, the same token) and the distribution of many draws.
+
+The fixed-point helpers state the kernels' exact arithmetic: probabilities are summed
+as round(p * 2^52) integers, so the kept set and the sampled token depend on no
+summation order.  philox4x32_10 is the counter-based generator of Salmon, Moraes, Dror
+and Shaw, "Parallel random numbers: as easy as 1, 2, 3" (SC 2011), which the sampling
+kernels use for their per-row random bits.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+FIXED_ONE = 1 << 52  # fixed-point scale of probability masses
+
+
+def nucleus_probs(logits, temperature: float, top_p: float) -> np.ndarray:
+    """Row-wise probs [..., V] (float32) after temperature and top-p, as the reference."""
+    x = np.asarray(logits, dtype=np.float32)
+    squeeze = x.ndim == 1
+    x = np.atleast_2d(x)
+    out = np.zeros_like(x, dtype=np.float32)
+    for r in range(x.shape[0]):
+        row = x[r]
+        if temperature <= 0:
+            out[r, int(np.argmax(row))] = 1.0
+            continue
+        y = (row / np.float32(temperature)).astype(np.float32)
+        e = np.exp(y - y.max()).astype(np.float32)
+        p = (e / e.sum(dtype=np.float32)).astype(np.float32)
+        if top_p < 1.0:
+            order = np.argsort(-p, kind="stable")
+            sp = p[order]
+            cum = np.cumsum(sp, dtype=np.float32)
+            sp = np.where(cum - sp > np.float32(top_p), np.float32(0.0), sp).astype(np.float32)
+            p = np.zeros_like(p)
+            p[order] = sp
+        out[r] = (p / p.sum(dtype=np.float32)).astype(np.float32)
+    return out[0] if squeeze else out
+
+
+def to_fixed(p) -> np.ndarray:
+    """round(p * 2^52) as uint64 (p float32 >= 0; the product is exact before rounding)."""
+    return np.rint(np.asarray(p, dtype=np.float32).astype(np.float64) * FIXED_ONE).astype(np.uint64)
+
+
+def kept_mask_fixed(p, top_p: float) -> np.ndarray:
+    """The kernels' top-p rule on one row of float32 probabilities p: keep, in descending
+    order with ties in index order, every entry whose exclusive cumulative fixed-point
+    mass is <= round(top_p * 2^52)."""
+    p = np.asarray(p, dtype=np.float32)
+    if top_p >= 1.0:
+        return np.ones(p.shape, dtype=bool)
+    q = to_fixed(p)
+    limit = int(np.rint(np.float64(np.float32(top_p)) * FIXED_ONE))
+    order = np.argsort(-p, kind="stable")
+    excl = np.concatenate([[0], np.cumsum(q[order].astype(object))[:-1]])
+    keep = np.zeros(p.shape, dtype=bool)
+    keep[order] = np.array([int(c) <= limit for c in excl], dtype=bool)
+    return keep
+
+
+def sample_fixed(weights, rand64: int) -> int:
+    """Inverse-CDF draw over float32 weights w >= 0 in index order: the first index whose
+    inclusive fixed-point prefix exceeds floor(rand64 * total / 2^64); -1 if total is 0."""
+    q = [int(v) for v in to_fixed(weights)]
+    total = sum(q)
+    if total == 0:
+        return -1
+    target = (int(rand64) * total) >> 64
+    acc = 0
+    for i, v in enumerate(q):
+        acc += v
+        if acc > target:
+            return i
+    return len(q) - 1
+
+
+_M0, _M1 = 0xD2511F53, 0xCD9E8D57
+_W0, _W1 = 0x9E3779B9, 0xBB67AE85
+_MASK = 0xFFFFFFFF
+
+
+def philox4x32_10(counter, key) -> list[int]:
+    """Philox4x32 with 10 rounds: counter (4 x uint32), key (2 x uint32) -> 4 x uint32."""
+    c = [int(v) & _MASK for v in counter]
+    k0, k1 = int(key[0]) & _MASK, int(key[1]) & _MASK
+    for r in range(10):
+        p0 = _M0 * c[0]
+        p1 = _M1 * c[2]
+        c = [((p1 >> 32) ^ c[1] ^ k0) & _MASK, p1 & _MASK,
+             ((p0 >> 32) ^ c[3] ^ k1) & _MASK, p0 & _MASK]
+        if r < 9:
+            k0 = (k0 + _W0) & _MASK
+            k1 = (k1 + _W1) & _MASK
+    return c
+
+
+def row_random64(seed: int, offset: int, row: int) -> int:
+    """The 64 random bits the sampling kernels draw for `row`: Philox4x32-10 with key =
+    seed (low, high words) and counter = (offset + row (low, high words), 0, 0); the first
+    two output words, word 0 high."""
+    n = int(offset) + int(row)
+    out = philox4x32_10([n & _MASK, (n >> 32) & _MASK, 0, 0], [seed & _MASK, (seed >> 32) & _MASK])
+    return (out[0] << 32) | out[1]

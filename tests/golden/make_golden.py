@@ -189,6 +189,37 @@ def gen_fp8(out: dict) -> None:
         torch.float8_e4m3fn).float().numpy()
 
 
+# decode-step sampling: (vocab, temperature, top_p, rows) cases for the reference's
+# nucleus_probs (core/spec_decode.py:14-31) on seeded N(0, 3^2) float32 logits
+SAMPLING_SEED = 11
+SAMPLING_CASES = [
+    (4096, 1.0, 1.0, 1), (4096, 0.7, 0.9, 1), (4096, 1.3, 0.5, 1), (4096, 0.7, 0.05, 1),
+    (4096, 0.0, 0.9, 1), (1000, 1.0, 0.95, 4), (32000, 0.7, 0.9, 1), (32000, 1.0, 0.99, 1),
+    (7, 0.5, 0.3, 3),
+]
+
+
+def gen_sampling(out: dict) -> None:
+    """Outputs of the reference's own nucleus_probs.  core/spec_decode.py imports its
+    package's CUDA-library bootstrap (inferd.env) first; that module is stubbed here, so
+    only the sampling code runs."""
+    for name in ("inferd", "inferd.env"):
+        sys.modules.setdefault(name, types.ModuleType(name))
+    from core.spec_decode import nucleus_probs  # noqa: E402  (reference module)
+
+    rng = np.random.default_rng(SAMPLING_SEED)
+    for i, (v, t, p, rows) in enumerate(SAMPLING_CASES):
+        logits = (rng.standard_normal((rows, v), dtype=np.float32) * np.float32(3.0)).astype(np.float32)
+        probs = nucleus_probs(torch.from_numpy(logits.copy()), t, p)
+        out[f"samp_{i}_logits"] = logits
+        out[f"samp_{i}_probs"] = probs.numpy().astype(np.float32)
+    # the reference's own selfcheck logits (core/spec_decode.py:182-187)
+    sc = torch.tensor([[10.0, 9.0, 1.0, -5.0]])
+    out["samp_selfcheck_logits"] = sc.numpy()
+    out["samp_selfcheck_p_1"] = nucleus_probs(sc, 1.0, 1.0).numpy()
+    out["samp_selfcheck_p_05"] = nucleus_probs(sc, 1.0, 0.5).numpy()
+
+
 def gen_cache_trace(pc) -> dict:
     """Allocator / page-table behaviour of the reference cache under a scripted trace."""
     trace: dict = {}
@@ -258,6 +289,9 @@ def main() -> int:
     gen_verify(out)
     gen_fp8(out)
     np.savez_compressed(HERE / "reference_golden.npz", **out)
+    samp: dict = {}
+    gen_sampling(samp)
+    np.savez_compressed(HERE / "sampling_golden.npz", **samp)
     trace = gen_cache_trace(pc)
     (HERE / "cache_trace.json").write_text(json.dumps(trace, indent=0))
     print(f"wrote {len(out)} arrays and {len(trace['ops'])} trace ops")
