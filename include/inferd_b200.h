@@ -201,6 +201,42 @@ INFERD_API int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3,
 INFERD_API size_t inferd_fp8_linear_workspace_bytes(int64_t m, int64_t n, int64_t k,
                                                     int32_t device);
 
+/*
+ * Decode-step sampling, one row per sequence: temperature + top-p ("nucleus")
+ * probabilities and one multinomial draw.  Replaces core/spec_decode.py:14-31
+ * nucleus_probs and :34-35 sample_from as called by the scheduler (core/scheduler.py:341-342)
+ * and the speculative accept/resample loop (core/spec_decode.py:127-160).
+ *
+ * inferd_nucleus_sample: logits [rows, logits_stride] (dtype f32/f16/bf16) ->
+ *   probs_out [rows, out_stride] fp32 (nullable): softmax(logits / T) with every entry
+ *   zeroed whose exclusive cumulative mass in descending order exceeds top_p (equal values
+ *   in index order), renormalised; T <= 0 gives a one-hot row at the argmax (the first on
+ *   ties);
+ *   tokens [rows] int64 (nullable): one draw from that distribution (the argmax when T <= 0).
+ * temperatures / top_ps: per-row device arrays, or NULL to use the scalars; top_p > 0.
+ * The draw is an inverse CDF in index order over probabilities rounded to multiples of
+ * 2^-52, with 64 random bits per row from Philox4x32-10 keyed by seed at counter
+ * offset + row; a row with no mass yields -1 and INFERD_ERR_INVALID_ARGUMENT in *error_word.
+ * vocab <= 262144.
+ */
+INFERD_API int inferd_nucleus_sample(float* probs_out, int64_t out_stride, int64_t* tokens,
+                                     const void* logits, int32_t dtype, int64_t logits_stride,
+                                     int32_t rows, int64_t vocab, const float* temperatures,
+                                     float temperature, const float* top_ps, float top_p,
+                                     uint64_t seed, uint64_t offset, int32_t* error_word,
+                                     void* stream);
+
+/*
+ * One multinomial draw per row from non-negative fp32 weights [rows, probs_stride] (need
+ * not sum to 1): core/spec_decode.py:34-35 sample_from.  Same draw rule and generator as
+ * inferd_nucleus_sample, the weights scaled by a power of two 2^(52 - k) with
+ * 2^k >= vocab * max weight before rounding to integers; negative, NaN or infinite weights
+ * count as zero and set INFERD_ERR_INVALID_ARGUMENT in *error_word.
+ */
+INFERD_API int inferd_sample_probs(int64_t* tokens, const float* probs, int64_t probs_stride,
+                                   int32_t rows, int64_t vocab, uint64_t seed, uint64_t offset,
+                                   int32_t* error_word, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,7 @@ _lock = threading.Lock()
 _c_void_p = ctypes.c_void_p
 _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
+_u64 = ctypes.c_uint64
 _f32 = ctypes.c_float
 _sz = ctypes.c_size_t
 
@@ -71,6 +72,11 @@ _SIGNATURES = {
     "inferd_fp8_packed_weight_bytes": (_sz, [_i64, _i64]),
     "inferd_fp8_pack_weights": (ctypes.c_int, [_c_void_p, _c_void_p, _i64, _i64, _c_void_p]),
     "inferd_fp8_linear_workspace_bytes": (_sz, [_i64, _i64, _i64, _i32]),
+    "inferd_nucleus_sample": (ctypes.c_int, [
+        _c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i64, _i32, _i64, _c_void_p, _f32,
+        _c_void_p, _f32, _u64, _u64, _c_void_p, _c_void_p]),
+    "inferd_sample_probs": (ctypes.c_int, [
+        _c_void_p, _c_void_p, _i64, _i32, _i64, _u64, _u64, _c_void_p, _c_void_p]),
 }
 
 

@@ -24,7 +24,7 @@ LIB_PATH = LIB_DIR / "libinferd_sm100a.so"
 INCLUDE_DIR = REPO_DIR / "include"
 
 SOURCES = ["runtime.cu", "cache_ops.cu", "paged_attention.cu", "paged_attention_noalloc.cu",
-           "fp8_linear.cu"]
+           "fp8_linear.cu", "sampling.cu"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

@@ -46,4 +46,5 @@ from .sampling import (  # noqa: F401
     row_random64,
     sample_fixed,
     to_fixed,
+    weight_scale,
 )

@@ -12,8 +12,8 @@ reproduced, so the kernels are checked in two ways: the exact inverse-CDF rule b
 (given the same random bits, the same token) and the distribution of many draws.
 
 The fixed-point helpers state the kernels' exact arithmetic: probabilities are summed
-as round(p * 2^52) integers, so the kept set and the sampled token depend on no
-summation order.  philox4x32_10 is the counter-based generator of Salmon, Moraes, Dror
+as round(p * 2^52) integers (unnormalised weights first scaled by a power of two, see
+weight_scale), so the kept set and the sampled token depend on no summation order.  philox4x32_10 is the counter-based generator of Salmon, Moraes, Dror
 and Shaw, "Parallel random numbers: as easy as 1, 2, 3" (SC 2011), which the sampling
 kernels use for their per-row random bits.
 """
@@ -71,10 +71,23 @@ def kept_mask_fixed(p, top_p: float) -> np.ndarray:
     return keep
 
 
+def weight_scale(weights) -> np.float32:
+    """The power of two 2^(52 - k), 2^k >= vocab * max weight, by which the draw from
+    unnormalised weights turns them into integers (the total stays <= 2^52)."""
+    w = np.asarray(weights, dtype=np.float32)
+    wmax = float(w.max()) if w.size else 0.0
+    ex = int(np.frexp(np.float32(wmax))[1])
+    lv = int(w.size - 1).bit_length() if w.size > 1 else 0
+    return np.float32(2.0 ** (52 - max(0, ex + lv)))
+
+
 def sample_fixed(weights, rand64: int) -> int:
-    """Inverse-CDF draw over float32 weights w >= 0 in index order: the first index whose
-    inclusive fixed-point prefix exceeds floor(rand64 * total / 2^64); -1 if total is 0."""
-    q = [int(v) for v in to_fixed(weights)]
+    """Inverse-CDF draw over float32 weights w >= 0 in index order (sample_from): weights
+    scaled by weight_scale and rounded to integers; the first index whose inclusive prefix
+    exceeds floor(rand64 * total / 2^64); -1 if the total is 0."""
+    w = np.asarray(weights, dtype=np.float32)
+    scaled = (w * weight_scale(w)).astype(np.float32)  # exact: a power of two
+    q = [int(v) for v in np.rint(scaled.astype(np.float64)).astype(np.uint64)]
     total = sum(q)
     if total == 0:
         return -1

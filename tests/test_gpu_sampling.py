@@ -1,0 +1,173 @@
+"""GPU decode-step sampling (inferd_b200.sampling) against the reference's own
+nucleus_probs outputs and the CPU oracle."""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from inferd_b200 import _lib
+from inferd_b200.sampling import nucleus_probs, sample_from, sample_nucleus
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "sampling_golden.npz"
+CASES = [
+    (4096, 1.0, 1.0, 1), (4096, 0.7, 0.9, 1), (4096, 1.3, 0.5, 1), (4096, 0.7, 0.05, 1),
+    (4096, 0.0, 0.9, 1), (1000, 1.0, 0.95, 4), (32000, 0.7, 0.9, 1), (32000, 1.0, 0.99, 1),
+    (7, 0.5, 0.3, 3),
+]
+
+
+@pytest.mark.parametrize("i", range(len(CASES)))
+def test_nucleus_probs_matches_reference_outputs(cuda_device, i):
+    golden = np.load(GOLDEN)
+    v, t, p, rows = CASES[i]
+    logits = torch.from_numpy(golden[f"samp_{i}_logits"]).to(cuda_device)
+    ref = golden[f"samp_{i}_probs"]
+    got = nucleus_probs(logits, t, p).cpu().numpy()
+    assert got.shape == ref.shape and got.dtype == np.float32
+    assert np.array_equal(got > 0, ref > 0), "kept sets differ from the reference"
+    np.testing.assert_allclose(got, ref, rtol=2e-6, atol=1e-9)
+
+
+def _boundary_ok(got: np.ndarray, logits: np.ndarray, t: float, p: float) -> None:
+    """Kept sets equal to the oracle's, except entries whose exclusive cumulative mass is
+    within 5e-4 of top_p: the reference decides those with an fp32 cumsum over up to 262k
+    sorted entries, whose rounding drifts by ~1e-5 .. 1e-4 that deep (the kernel sums
+    exactly in fixed point)."""
+    ref = oracle.nucleus_probs(logits, t, p)
+    for r in range(ref.shape[0]):
+        diff = np.nonzero((got[r] > 0) != (ref[r] > 0))[0]
+        if diff.size:
+            x = logits[r] / np.float32(t)
+            e = np.exp(x - x.max())
+            pr = e / e.sum()
+            order = np.argsort(-pr, kind="stable")
+            excl = np.concatenate([[0.0], np.cumsum(pr[order])[:-1]])
+            pos = np.empty_like(order)
+            pos[order] = np.arange(order.size)
+            assert np.all(np.abs(excl[pos[diff]] - p) < 5e-4), f"row {r}: {diff.size} entries differ"
+        keep = (got[r] > 0) & (ref[r] > 0)
+        np.testing.assert_allclose(got[r][keep], ref[r][keep], rtol=1e-4)
+
+
+@pytest.mark.parametrize("vocab", [7, 5000, 32768 + 17, 100000, 151936, 262144])
+def test_nucleus_probs_cluster_sizes(cuda_device, vocab):
+    # 1, 2, 4 and 8 CTAs per row (32768 entries per CTA at most)
+    g = torch.Generator().manual_seed(vocab)
+    logits = torch.randn(3, vocab, generator=g) * 3.0
+    got = nucleus_probs(logits.to(cuda_device), 0.8, 0.9).cpu().numpy()
+    _boundary_ok(got, logits.numpy(), 0.8, 0.9)
+    np.testing.assert_allclose(got.sum(axis=1), 1.0, rtol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_nucleus_probs_half_logits(cuda_device, dtype):
+    # bf16 logits of a 151936 vocabulary: many equal values, including at the cut
+    g = torch.Generator().manual_seed(5)
+    logits = (torch.randn(4, 151936, generator=g) * 2.0).to(dtype)
+    got = nucleus_probs(logits.to(cuda_device), 0.7, 0.95).cpu().numpy()
+    _boundary_ok(got, logits.float().numpy(), 0.7, 0.95)
+
+
+@pytest.mark.parametrize("vocab", [4096, 65536])
+def test_ties_cut_in_index_order(cuda_device, vocab):
+    # equal logits: p = 1/vocab exactly; entry j is kept iff j / vocab <= top_p, so the first
+    # floor(top_p * vocab) + 1 indices are kept -- across CTAs when vocab = 65536
+    logits = torch.zeros(2, vocab, device=cuda_device)
+    got = nucleus_probs(logits, 1.0, 0.3).cpu().numpy()
+    n_keep = int(np.floor(np.float32(0.3) * vocab)) + 1
+    expect = np.zeros(vocab, np.float32)
+    expect[:n_keep] = 1.0 / n_keep
+    for r in range(2):
+        assert np.count_nonzero(got[r]) == n_keep
+        np.testing.assert_allclose(got[r], expect, rtol=1e-6)
+
+
+def test_greedy_rows(cuda_device):
+    logits = torch.randn(4, 5000, device=cuda_device)
+    logits[1, 10] = logits[1, 20] = 50.0  # a tie at the max: the first index wins
+    got = nucleus_probs(logits, 0.0, 0.9)
+    idx = logits.argmax(dim=-1)
+    idx[1] = 10
+    assert torch.equal(got.argmax(dim=-1), idx) and torch.all(got.sum(dim=-1) == 1)
+    tok = sample_nucleus(logits, 0.0, 0.5)
+    assert tok.view(-1).tolist() == idx.tolist()
+
+
+def test_per_row_temperature_and_top_p(cuda_device):
+    g = torch.Generator().manual_seed(9)
+    logits = torch.randn(4, 3000, generator=g) * 3.0
+    temps = torch.tensor([0.5, 1.0, 0.0, 1.5])
+    tops = torch.tensor([0.9, 1.0, 0.5, 0.2])
+    got = nucleus_probs(logits.to(cuda_device), temps.to(cuda_device), tops.to(cuda_device)).cpu().numpy()
+    for r in range(4):
+        ref = oracle.nucleus_probs(logits[r].numpy(), float(temps[r]), float(tops[r]))
+        assert np.array_equal(got[r] > 0, ref > 0)
+        np.testing.assert_allclose(got[r], ref, rtol=1e-5, atol=1e-9)
+
+
+def test_sample_probs_exact_draws_through_c_abi(cuda_device):
+    # given the same 64 random bits (Philox4x32-10, seed, counter = row) the same token
+    lib = _lib.load()
+    g = torch.Generator().manual_seed(3)
+    rows, vocab = 64, 50000
+    w = torch.rand(rows, vocab, generator=g) ** 8
+    w[5, :] = 0.0
+    w[5, 123] = 2.0  # a single non-zero weight
+    wd = w.to(cuda_device)
+    tokens = torch.empty(rows, dtype=torch.int64, device=cuda_device)
+    seed = 0x1234_5678_9ABC
+    err = _lib.error_word(cuda_device)
+    st = lib.inferd_sample_probs(tokens.data_ptr(), wd.data_ptr(), vocab, rows, vocab, seed, 7,
+                                 err.data_ptr(), _lib.stream_of(cuda_device))
+    assert st == 0
+    torch.cuda.synchronize()
+    _lib.raise_device_errors(cuda_device)
+    expect = [oracle.sample_fixed(w[r].numpy(), oracle.row_random64(seed, 7, r)) for r in range(rows)]
+    assert tokens.cpu().tolist() == expect
+    assert expect[5] == 123
+
+
+def test_sample_from_distribution(cuda_device):
+    p = torch.tensor([0.05, 0.0, 0.4, 0.25, 0.3], dtype=torch.float32)
+    n = 200_000
+    tok = sample_from(p.to(cuda_device).expand(n, 5).contiguous()).view(-1).cpu()
+    assert tok.shape == (n,) and tok.min() >= 0 and tok.max() <= 4
+    freq = torch.bincount(tok, minlength=5).double() / n
+    assert freq[1] == 0.0
+    assert torch.all((freq - p.double()).abs() < 5 * torch.sqrt(p.double() * (1 - p.double()) / n) + 1e-9)
+
+
+def test_sample_nucleus_distribution_and_support(cuda_device):
+    logits = torch.tensor([3.0, 2.5, 0.0, -1.0, 2.0, 1.0, -3.0, 0.5])
+    ref = torch.from_numpy(oracle.nucleus_probs(logits.numpy(), 0.9, 0.8)).double()
+    n = 200_000
+    tok, probs = sample_nucleus(logits.to(cuda_device).expand(n, 8).contiguous(), 0.9, 0.8,
+                                return_probs=True)
+    np.testing.assert_allclose(probs[0].cpu().numpy(), ref.numpy(), rtol=1e-5)
+    freq = torch.bincount(tok.view(-1).cpu(), minlength=8).double() / n
+    assert torch.all(freq[ref == 0] == 0), "drew a token outside the nucleus"
+    assert torch.all((freq - ref).abs() < 5 * torch.sqrt(ref * (1 - ref) / n) + 1e-9)
+
+
+def test_seeded_draws_repeat_under_manual_seed(cuda_device):
+    logits = torch.randn(32, 20000, device=cuda_device)
+    torch.manual_seed(123)
+    a = sample_nucleus(logits, 1.0, 0.95)
+    torch.manual_seed(123)
+    b = sample_nucleus(logits, 1.0, 0.95)
+    assert torch.equal(a, b)
+
+
+def test_zero_row_is_an_error(cuda_device):
+    p = torch.zeros(2, 100, device=cuda_device)
+    p[0, 3] = 1.0
+    with pytest.raises(ValueError):
+        sample_from(p)
