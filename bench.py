@@ -484,6 +484,85 @@ def run_fp8(args, device: torch.device) -> list[dict]:
     return lines
 
 
+# ------------------------------------------------------------------ decode-step sampling
+SAMP_ROWS, SAMP_VOCAB, SAMP_T, SAMP_TOP_P = 64, 151936, 0.7, 0.9
+
+
+def run_sampling(args, device: torch.device) -> list[dict]:
+    """Decode-step sampling for a batch of 64 sequences over a 151,936-entry vocabulary
+    (the Qwen tokenizer's embedding width), bf16 logits ~ N(0, 3^2), temperature 0.7,
+    top_p 0.9.  Two lines: nucleus_probs (fp32 probabilities written) and the fused sampler
+    (one token per row, no probabilities).  Eight logits copies (156 MB) and eight output
+    buffers rotate so no call finds its data in L2.  The timed calls go straight to the C
+    ABI (the Python wrapper's per-call checks would otherwise be the bottleneck)."""
+    import oracle
+    from inferd_b200 import _lib
+
+    lib = _lib.load()
+    g = torch.Generator(device=device).manual_seed(7)
+    rows, vocab = SAMP_ROWS, SAMP_VOCAB
+    copies = [(torch.randn(rows, vocab, generator=g, device=device) * 3.0).to(torch.bfloat16)
+              for _ in range(8)]
+    outs = [torch.empty(rows, vocab, dtype=torch.float32, device=device) for _ in range(8)]
+    toks = torch.empty(rows, dtype=torch.int64, device=device)
+    err = _lib.error_word(device)
+    stream = torch.cuda.current_stream(device)
+    peaks = measured_peaks()
+
+    def call(i, with_probs):
+        x = copies[i % 8]
+        st = lib.inferd_nucleus_sample(
+            outs[i % 8].data_ptr() if with_probs else None, vocab,
+            None if with_probs else toks.data_ptr(), x.data_ptr(), 2, vocab, rows, vocab,
+            None, SAMP_T, None, SAMP_TOP_P, 1234, i * rows, err.data_ptr(), stream.cuda_stream)
+        _lib.check(st, "nucleus_sample")
+
+    lines = []
+    for with_probs in (True, False):
+        for i in range(args.warmup):
+            call(i, with_probs)
+        torch.cuda.synchronize(device)
+        _lib.raise_device_errors(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(20_000_000)
+        e0.record(stream)
+        for i in range(args.steps):
+            call(i, with_probs)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        _lib.raise_device_errors(device)
+        ms = e0.elapsed_time(e1) / args.steps
+        nbytes = rows * vocab * 2 + (rows * vocab * 4 if with_probs else rows * 8)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        lines.append({
+            "metric": "decode-step sampling (temperature + top-p)",
+            "variant": "nucleus_probs" if with_probs else "sample_nucleus",
+            "rows": rows, "vocab": vocab, "temperature": SAMP_T, "top_p": SAMP_TOP_P,
+            "logits_dtype": "bf16", "us_per_call": round(ms * 1000, 2),
+            "rows_per_s": round(rows / (ms * 1e-3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                         "bytes_per_call": nbytes, "peak_source": peaks["source"],
+                         "kernel": "sampling_kernel"},
+            "l2": "eight rotating logits copies (156 MB) and outputs",
+            "calls_timed": args.steps,
+        })
+    if not args.no_cpu_baseline:
+        # the oracle restates the reference's per-row softmax + sort + cumsum in numpy
+        x = copies[0][:4].float().cpu().numpy()
+        t0 = time.perf_counter()
+        done = 0
+        while time.perf_counter() - t0 < min(args.cpu_budget, 10.0) or done == 0:
+            oracle.nucleus_probs(x[done % 4], SAMP_T, SAMP_TOP_P)
+            done += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": round(done / dt, 2), "unit": "rows/s", "cores": _cpu_threads(), "kind": "port",
+               "sample": f"{done} rows of nucleus_probs in numpy (softmax, stable sort, cumsum), {dt:.1f} s"}
+        for line in lines:
+            line["cpu_baseline"] = cpu
+    return lines
+
+
 # ------------------------------------------------------------------ CPU baseline (oracle)
 class CpuWork:
     """The oracle (numpy restatement of the reference's per-sequence gather + attention)
@@ -582,7 +661,7 @@ def main(argv=None) -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["fp8"], default="decode")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["fp8", "sampling"], default="decode")
     ap.add_argument("--fp8-m", default="1,8,32,128,256", help="token counts for --workload fp8")
     ap.add_argument("--fp8-layout", choices=["packed", "rowmajor"], default="packed")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -605,6 +684,11 @@ def main(argv=None) -> int:
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.workload == "sampling":
+        if rank == 0:
+            for line in run_sampling(args, device):
+                print(json.dumps(line), flush=True)
+        return 0
     if args.workload == "fp8":
         if rank == 0:
             for line in run_fp8(args, device):

@@ -16,8 +16,8 @@
 //
 // No sort: the top-p cut is found by a radix select on the fp32 bit patterns of the
 // probabilities (monotonic for p >= 0), four passes of 8 bits with 256-bin histograms of
-// count and mass.  Masses are summed as round(p * 2^52) integers, so nothing depends on
-// the order of atomic updates.  The kept set is every entry whose exclusive cumulative
+// count and mass.  Masses are summed as integers (round(p * 2^31) in the select,
+// round(p * 2^52) for the draw), so nothing depends on the order of atomic updates.  The kept set is every entry whose exclusive cumulative
 // mass in descending order is <= top_p, ties in index order (a stable sort; the
 // reference's torch.sort leaves the order of equal values unspecified).
 //
@@ -68,25 +68,21 @@ __device__ __forceinline__ uint32_t samp_rank() {
 __device__ __forceinline__ void samp_cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ uint32_t samp_map(const void* p, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-  return r;
+// Generic address of this CTA's shared variable *p as seen in CTA `rank` of the cluster.
+// Reads through it are ordinary loads, so several can be in flight; the cluster barriers
+// (with memory clobbers) order them against the writes they read.
+template <typename T>
+__device__ __forceinline__ const T* cl_ptr(const T* p, uint32_t rank) {
+  unsigned long long r;
+  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(reinterpret_cast<unsigned long long>(p)), "r"(rank));
+  return reinterpret_cast<const T*>(r);
 }
-__device__ __forceinline__ float ld_cl_f32(const void* p, uint32_t rank) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(samp_map(p, rank)) : "memory");
-  return v;
-}
+__device__ __forceinline__ float ld_cl_f32(const float* p, uint32_t rank) { return *cl_ptr(p, rank); }
 __device__ __forceinline__ uint32_t ld_cl_u32(const void* p, uint32_t rank) {
-  uint32_t v;
-  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(samp_map(p, rank)) : "memory");
-  return v;
+  return *cl_ptr(static_cast<const uint32_t*>(p), rank);
 }
-__device__ __forceinline__ unsigned long long ld_cl_u64(const void* p, uint32_t rank) {
-  unsigned long long v;
-  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(samp_map(p, rank)) : "memory");
-  return v;
+__device__ __forceinline__ unsigned long long ld_cl_u64(const unsigned long long* p, uint32_t rank) {
+  return *cl_ptr(p, rank);
 }
 
 // ---------------------------------------------------------------- Philox4x32-10
@@ -124,11 +120,14 @@ __device__ __forceinline__ float load_src(const In* p) {
 }
 
 // ---------------------------------------------------------------- block reductions
+constexpr int kMaxSweeps = kSampMaxPerCta / kSampThreads;
+
 struct SampShared {
-  unsigned long long hist_m[256];
-  uint32_t hist_c[256];
-  unsigned long long tot_m[256];
+  uint32_t hist_m[2][256];  // select histograms: mass (multiples of 2^-31) and count,
+  uint32_t hist_c[2][256];  // double-buffered by pass
+  unsigned long long tot_m[256];  // the cluster's sums
   uint32_t tot_c[256];
+  uint32_t tie_cnt[kMaxSweeps * kSampWarps];
   float wf[kSampWarps];
   int wi[kSampWarps];
   unsigned long long wu[kSampWarps];
@@ -238,6 +237,25 @@ __device__ __forceinline__ unsigned long long block_exscan_u64(SampShared& sh, u
   return base + inc - v;
 }
 
+// One loaded entry: x / T (mode 0), weight sanity (mode 1), store, running argmax.
+__device__ __forceinline__ void take_entry(float* e, int i, float x, int64_t lo, int mode, bool greedy,
+                                           float temp, bool& bad, float& mv, int& mi) {
+  if (mode == 0 && !greedy) x = __fdiv_rn(x, temp);
+  if (mode == 1 && (!(x >= 0.f) || x == INFINITY)) {  // negative, NaN or infinite weight
+    bad = true;
+    x = 0.f;
+  }
+  e[i] = x;
+  const int gi = static_cast<int>(lo) + i;
+  if (x > mv || (x == mv && gi < mi)) {
+    mv = x;
+    mi = gi;
+  }
+}
+
+// mass of p in units of 2^-31 for the radix select (p <= 1, so it fits 32 bits)
+__device__ __forceinline__ uint32_t to_q31(float p) { return __float2uint_rn(p * 2147483648.0f); }
+
 // ---------------------------------------------------------------- the kernel
 // mode 0: probs_out (optional) = nucleus probabilities; tokens (optional) = one draw.
 // mode 1: tokens = one draw from the given non-negative weights (sample_from).
@@ -246,6 +264,7 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
   extern __shared__ __align__(16) float e[];
   __shared__ SampShared sh;
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
   const uint32_t rank = samp_rank();
   const int row = blockIdx.x / C;
   const int64_t lo = static_cast<int64_t>(rank) * p.per_cta;
@@ -260,19 +279,26 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
   float mv = -INFINITY;
   int mi = 0x7fffffff;
   bool bad = false;
-  for (int i = tid; i < n; i += kSampThreads) {
-    float x = load_src<In>(src + i);
-    if (p.mode == 0 && !greedy) x = __fdiv_rn(x, temp);
-    if (p.mode == 1 && (!(x >= 0.f) || x == INFINITY)) {  // negative, NaN or infinite weight
-      bad = true;
-      x = 0.f;
+  {
+    constexpr int kVec = 16 / static_cast<int>(sizeof(In));
+    int done = 0;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+      const int nv = n / kVec;
+      const uint4* src4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll 8
+      for (int v = tid; v < nv; v += kSampThreads) {
+        const uint4 raw = __ldg(src4 + v);
+        const In* el = reinterpret_cast<const In*>(&raw);
+#pragma unroll
+        for (int j = 0; j < kVec; ++j)
+          take_entry(e, v * kVec + j, to_f32<In>(el[j]), lo, p.mode, greedy, temp, bad, mv, mi);
+      }
+      done = nv * kVec;
     }
-    e[i] = x;
-    if (x > mv || (x == mv && static_cast<int>(lo) + i < mi)) {
-      mv = x;
-      mi = static_cast<int>(lo) + i;
-    }
+    for (int i = done + tid; i < n; i += kSampThreads)
+      take_entry(e, i, load_src<In>(src + i), lo, p.mode, greedy, temp, bad, mv, mi);
   }
+  if (bad) report_error(p.error_word, INFERD_ERR_INVALID_ARGUMENT);
   block_argmax(sh, mv, mi);
   if (tid == 0) {
     sh.x_f = mv;
@@ -301,19 +327,10 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
     return;
   }
 
-  // ---- phase 2: probabilities
-  // Fixed point: probabilities (mode 0) as multiples of 2^-52; weights (mode 1) scaled by
-  // the power of two 2^(52 - k) with 2^k >= vocab * max weight, so the total stays <= 2^52.
+  // ---- phase 2: probabilities (mode 0); weights stay as given (mode 1)
+  // Fixed point for the draw: probabilities as multiples of 2^-52; weights scaled by the
+  // power of two 2^(52 - k) with 2^k >= vocab * max weight, so totals stay <= 2^52.
   float fxs = 4503599627370496.0f;
-  if (p.mode == 1) {
-    int ex = 0;
-    frexpf(gmax, &ex);  // gmax <= 2^ex (gmax = 0 gives ex = 0)
-    const int lv = p.vocab > 1 ? 64 - __clzll(static_cast<unsigned long long>(p.vocab - 1)) : 0;
-    int k = ex + lv;
-    if (k < 0) k = 0;
-    fxs = ldexpf(1.f, 52 - k);
-  }
-  unsigned long long total = 0;  // fixed-point mass of every entry
   if (p.mode == 0) {
     float s = 0.f;
     for (int i = tid; i < n; i += kSampThreads) {
@@ -328,40 +345,36 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
 #pragma unroll
     for (int r = 0; r < C; ++r) z += ld_cl_f32(&sh.x_f, r);
     samp_cluster_sync();
-    unsigned long long q = 0;
-    for (int i = tid; i < n; i += kSampThreads) {
-      const float pv = __fdiv_rn(e[i], z);
-      e[i] = pv;
-      q += to_fixed(pv, fxs);
-    }
-    q = block_sum_u64(sh, q);
-    if (tid == 0) sh.x_u = q;
+    for (int i = tid; i < n; i += kSampThreads) e[i] = __fdiv_rn(e[i], z);
   } else {
-    unsigned long long q = 0;
-    for (int i = tid; i < n; i += kSampThreads) q += to_fixed(e[i], fxs);
-    if (bad) report_error(p.error_word, INFERD_ERR_INVALID_ARGUMENT);
-    q = block_sum_u64(sh, q);
-    if (tid == 0) sh.x_u = q;
+    int ex = 0;
+    frexpf(gmax, &ex);  // gmax <= 2^ex (gmax = 0 gives ex = 0)
+    const int lv = p.vocab > 1 ? 64 - __clzll(static_cast<unsigned long long>(p.vocab - 1)) : 0;
+    int k = ex + lv;
+    if (k < 0) k = 0;
+    fxs = ldexpf(1.f, 52 - k);
   }
-  samp_cluster_sync();
-#pragma unroll
-  for (int r = 0; r < C; ++r) total += ld_cl_u64(&sh.x_u, r);
-  samp_cluster_sync();
 
   // ---- phase 3: top-p threshold by radix select on the bits of p
-  unsigned long long kept = total;
+  // The select sums masses as multiples of 2^-31 in 32-bit counters (native shared-memory
+  // atomics; a bin's sum is at most the row's total, about 2^31).  An entry is kept when
+  // the mass of the entries before it in descending order (ties in index order) is
+  // <= round(top_p * 2^31).
   const bool cut = p.mode == 0 && top_p < 1.f;
   uint32_t tbits = 0;
   if (cut) {
-    const unsigned long long limit = static_cast<unsigned long long>(
-        __double2ull_rn(static_cast<double>(top_p) * kFixedOne));
+    const unsigned long long limit = __double2ull_rn(static_cast<double>(top_p) * 2147483648.0);
     uint32_t prefix = 0;
     unsigned long long above = 0;
     uint32_t ties = 0;
     for (int shift = 24; shift >= 0; shift -= 8) {
+      // a pass's histogram buffer is next written two passes later, after the next pass's
+      // cluster barrier, by which time every CTA has read it
+      uint32_t* hm = sh.hist_m[(shift >> 3) & 1];
+      uint32_t* hc = sh.hist_c[(shift >> 3) & 1];
       for (int b = tid; b < 256; b += kSampThreads) {
-        sh.hist_m[b] = 0;
-        sh.hist_c[b] = 0;
+        hm[b] = 0;
+        hc[b] = 0;
       }
       __syncthreads();
       const uint32_t hi_mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
@@ -369,8 +382,8 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
         const uint32_t bits = __float_as_uint(e[i]);
         if ((bits & hi_mask) == (prefix & hi_mask)) {
           const uint32_t d = (bits >> shift) & 255u;
-          atomicAdd(&sh.hist_m[d], to_fixed(e[i], fxs));
-          atomicAdd(&sh.hist_c[d], 1u);
+          atomicAdd(&hm[d], to_q31(e[i]));
+          atomicAdd(&hc[d], 1u);
         }
       }
       __syncthreads();
@@ -380,32 +393,48 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
         uint32_t c = 0;
 #pragma unroll
         for (int r = 0; r < C; ++r) {
-          m += ld_cl_u64(&sh.hist_m[b], r);
-          c += ld_cl_u32(&sh.hist_c[b], r);
+          m += ld_cl_u32(&hm[b], r);
+          c += ld_cl_u32(&hc[b], r);
         }
         sh.tot_m[b] = m;
         sh.tot_c[b] = c;
       }
-      samp_cluster_sync();  // remote reads done before the histograms are cleared again
-      if (tid == 0) {
-        // lowest non-empty bin whose mass above is still within the limit
-        unsigned long long acc = above, acc_best = above;
-        int best = -1;
-        for (int b = 255; b >= 0; --b) {
-          if (sh.tot_c[b] > 0) {
-            if (acc <= limit) {
-              best = b;
-              acc_best = acc;
-            } else {
-              break;
-            }
+      __syncthreads();
+      if (tid < 32) {
+        // Lane l owns bins 255 - 8l .. 248 - 8l (descending).  The cut bin is the lowest
+        // non-empty bin whose mass above (above + all higher bins) is within the limit.
+        unsigned long long mine = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mine += sh.tot_m[255 - 8 * lane - j];
+        unsigned long long pre = mine;  // inclusive scan in lane order
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const unsigned long long t = __shfl_up_sync(0xffffffffu, pre, o);
+          if (lane >= o) pre += t;
+        }
+        unsigned long long acc = above + pre - mine;
+        int cand = 256;
+        unsigned long long cand_acc = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int b = 255 - 8 * lane - j;
+          if (sh.tot_c[b] > 0 && acc <= limit) {
+            cand = b;
+            cand_acc = acc;
           }
           acc += sh.tot_m[b];
         }
-        if (best < 0) best = 0;  // not reached: the largest entry always qualifies
-        sh.b_prefix = prefix | (static_cast<uint32_t>(best) << shift);
-        sh.b_mass = acc_best;
-        sh.b_ties = sh.tot_c[best];
+        int best = cand;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
+        if (best == 256) best = 0;  // not reached: the largest entry always qualifies
+        const uint32_t owner = static_cast<uint32_t>((255 - best) / 8);
+        const unsigned long long best_acc = __shfl_sync(0xffffffffu, cand_acc, owner);
+        if (lane == 0) {
+          sh.b_prefix = prefix | (static_cast<uint32_t>(best) << shift);
+          sh.b_mass = best_acc;
+          sh.b_ties = sh.tot_c[best];
+        }
       }
       __syncthreads();
       prefix = sh.b_prefix;
@@ -414,68 +443,93 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
       __syncthreads();
     }
     tbits = prefix;
-    const unsigned long long tq = to_fixed(__uint_as_float(tbits), fxs);
+    const unsigned long long tq = to_q31(__uint_as_float(tbits));
     uint32_t keep_ties = ties;
     if (tq > 0) {
       const unsigned long long room = (limit - above) / tq + 1;  // above <= limit
       if (room < keep_ties) keep_ties = static_cast<uint32_t>(room);
     }
-    kept = above + static_cast<unsigned long long>(keep_ties) * tq;
 
-    // ---- phase 4: a tied group cut in the middle keeps its first entries in index order
+    // ---- phase 4: a tied group cut in the middle keeps its first entries in index order.
+    // Entry i = k * 512 + tid is the k-th sweep's; ranks come from per-(sweep, warp) ballot
+    // counts scanned once.
     if (keep_ties < ties) {
-      uint32_t local = 0;
-      for (int i = tid; i < n; i += kSampThreads) local += __float_as_uint(e[i]) == tbits ? 1u : 0u;
-      local = static_cast<uint32_t>(block_sum_u64(sh, local));
-      if (tid == 0) sh.x_u2 = local;
+      const int nk = (n + kSampThreads - 1) / kSampThreads;  // <= kMaxSweeps
+      const int w = tid >> 5;
+      for (int k = 0; k < nk; ++k) {
+        const int i = k * kSampThreads + tid;
+        const bool tie = i < n && __float_as_uint(e[i]) == tbits;
+        const uint32_t bal = __ballot_sync(0xffffffffu, tie);
+        if (lane == 0) sh.tie_cnt[k * kSampWarps + w] = static_cast<uint32_t>(__popc(bal));
+      }
+      __syncthreads();
+      // exclusive scan of the nk * 16 counts in (sweep, warp) order; thread t owns 2 slots
+      const int slots = nk * kSampWarps;
+      const uint32_t a0 = 2 * tid < slots ? sh.tie_cnt[2 * tid] : 0u;
+      const uint32_t a1 = 2 * tid + 1 < slots ? sh.tie_cnt[2 * tid + 1] : 0u;
+      unsigned long long cta_ties;
+      const unsigned long long ex = block_exscan_u64(sh, a0 + a1, cta_ties);
+      if (2 * tid < slots) sh.tie_cnt[2 * tid] = static_cast<uint32_t>(ex);
+      if (2 * tid + 1 < slots) sh.tie_cnt[2 * tid + 1] = static_cast<uint32_t>(ex + a0);
+      if (tid == 0) sh.x_u2 = cta_ties;
       samp_cluster_sync();
       unsigned long long base = 0;
       for (uint32_t r = 0; r < rank; ++r) base += ld_cl_u64(&sh.x_u2, r);
       samp_cluster_sync();
-      for (int c0 = 0; c0 < n; c0 += kSampChunk) {
-        const int i0 = c0 + tid * 8;
-        uint32_t mine = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (i0 + j < n && __float_as_uint(e[i0 + j]) == tbits) ++mine;
-        unsigned long long tot_chunk;
-        unsigned long long ex = block_exscan_u64(sh, mine, tot_chunk);
-        unsigned long long rk = base + ex;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (i0 + j < n && __float_as_uint(e[i0 + j]) == tbits) {
-            if (rk >= keep_ties) e[i0 + j] = 0.f;  // dropped: excluded below as p < t
-            ++rk;
+      if (base + cta_ties > keep_ties) {  // otherwise every tie of this CTA is kept
+        const uint32_t lt = (1u << lane) - 1u;
+        for (int k = 0; k < nk; ++k) {
+          const int i = k * kSampThreads + tid;
+          const bool tie = i < n && __float_as_uint(e[i]) == tbits;
+          const uint32_t bal = __ballot_sync(0xffffffffu, tie);
+          if (tie) {
+            const unsigned long long rk = base + sh.tie_cnt[k * kSampWarps + w] + __popc(bal & lt);
+            if (rk >= keep_ties) e[i] = 0.f;  // dropped: excluded below as p < t
           }
-        base += tot_chunk;
-        __syncthreads();
+        }
       }
+      __syncthreads();
     }
   }
+
+  // ---- kept mass in fixed point: this CTA's share, the shares before it, the row total
+  unsigned long long local = 0;
+  for (int i = tid; i < n; i += kSampThreads) {
+    const float v = e[i];
+    if (!cut || __float_as_uint(v) >= tbits) local += to_fixed(v, fxs);
+  }
+  local = block_sum_u64(sh, local);
+  if (tid == 0) sh.x_u2 = local;
+  samp_cluster_sync();
+  unsigned long long base = 0, kept = 0;
+#pragma unroll
+  for (int r = 0; r < C; ++r) {
+    const unsigned long long v = ld_cl_u64(&sh.x_u2, r);
+    if (r < static_cast<int>(rank)) base += v;
+    kept += v;
+  }
+  samp_cluster_sync();
 
   // ---- phase 5: renormalised probabilities
   if (p.mode == 0 && out) {
     const float s = static_cast<float>(static_cast<double>(kept) / kFixedOne);
-    for (int i = tid; i < n; i += kSampThreads) {
-      const float v = e[i];
-      const bool keep = !cut || __float_as_uint(v) >= tbits;
-      out[i] = (keep && v > 0.f) ? __fdiv_rn(v, s) : 0.f;
+    auto val = [&](float v) { return ((!cut || __float_as_uint(v) >= tbits) && v > 0.f) ? __fdiv_rn(v, s) : 0.f; };
+    int done = 0;
+    if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+      const int nv = n / 4;
+      float4* out4 = reinterpret_cast<float4*>(out);
+      const float4* e4 = reinterpret_cast<const float4*>(e);
+      for (int v = tid; v < nv; v += kSampThreads) {
+        const float4 x = e4[v];
+        out4[v] = make_float4(val(x.x), val(x.y), val(x.z), val(x.w));
+      }
+      done = nv * 4;
     }
+    for (int i = done + tid; i < n; i += kSampThreads) out[i] = val(e[i]);
   }
 
   // ---- phase 6: one draw, inverse CDF in index order over the kept masses
   if (p.tokens) {
-    unsigned long long local = 0;
-    for (int i = tid; i < n; i += kSampThreads) {
-      const float v = e[i];
-      if (!cut || __float_as_uint(v) >= tbits) local += to_fixed(v, fxs);
-    }
-    local = block_sum_u64(sh, local);
-    if (tid == 0) sh.x_u2 = local;
-    samp_cluster_sync();
-    unsigned long long base = 0;
-    for (uint32_t r = 0; r < rank; ++r) base += ld_cl_u64(&sh.x_u2, r);
-    samp_cluster_sync();
     if (kept == 0) {
       if (rank == 0 && tid == 0) {
         p.tokens[row] = -1;
@@ -487,6 +541,7 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
     if (target >= base && target < base + local) {
       if (tid == 0) sh.found = 0;
       __syncthreads();
+      unsigned long long acc0 = base;
       for (int c0 = 0; c0 < n; c0 += kSampChunk) {
         const int i0 = c0 + tid * 8;
         unsigned long long q[8];
@@ -501,7 +556,7 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
           mine += q[j];
         }
         unsigned long long tot_chunk;
-        const unsigned long long ex = base + block_exscan_u64(sh, mine, tot_chunk);
+        const unsigned long long ex = acc0 + block_exscan_u64(sh, mine, tot_chunk);
         if (target >= ex && target < ex + mine) {
           unsigned long long acc = ex;
 #pragma unroll
@@ -514,7 +569,7 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
             }
           }
         }
-        base += tot_chunk;
+        acc0 += tot_chunk;
         __syncthreads();
         if (sh.found) break;
       }
@@ -552,7 +607,7 @@ template <typename In>
 int dispatch_cluster(SampParams& p, cudaStream_t s) {
   int c = 1;
   while (c < 8 && (p.vocab + c - 1) / c > kSampMaxPerCta) c <<= 1;
-  const int64_t per = (p.vocab + c - 1) / c;
+  const int64_t per = ((p.vocab + c - 1) / c + 7) / 8 * 8;  // 16-byte aligned CTA slices
   if (per > kSampMaxPerCta) return INFERD_ERR_UNSUPPORTED;
   p.per_cta = static_cast<int32_t>(per);
   switch (c) {

@@ -11,9 +11,10 @@ sample_from (core/spec_decode.py:34-35) is torch.multinomial; its draws cannot b
 reproduced, so the kernels are checked in two ways: the exact inverse-CDF rule below
 (given the same random bits, the same token) and the distribution of many draws.
 
-The fixed-point helpers state the kernels' exact arithmetic: probabilities are summed
-as round(p * 2^52) integers (unnormalised weights first scaled by a power of two, see
-weight_scale), so the kept set and the sampled token depend on no summation order.  philox4x32_10 is the counter-based generator of Salmon, Moraes, Dror
+The fixed-point helpers state the kernels' exact arithmetic: the top-p select sums
+round(p * 2^31) integers and the draw round(p * 2^52) integers (unnormalised weights first
+scaled by a power of two, see weight_scale), so the kept set and the sampled token depend
+on no summation order.  philox4x32_10 is the counter-based generator of Salmon, Moraes, Dror
 and Shaw, "Parallel random numbers: as easy as 1, 2, 3" (SC 2011), which the sampling
 kernels use for their per-row random bits.
 """
@@ -55,15 +56,18 @@ def to_fixed(p) -> np.ndarray:
     return np.rint(np.asarray(p, dtype=np.float32).astype(np.float64) * FIXED_ONE).astype(np.uint64)
 
 
+SELECT_ONE = 1 << 31  # fixed-point scale of the masses in the top-p select
+
+
 def kept_mask_fixed(p, top_p: float) -> np.ndarray:
     """The kernels' top-p rule on one row of float32 probabilities p: keep, in descending
-    order with ties in index order, every entry whose exclusive cumulative fixed-point
-    mass is <= round(top_p * 2^52)."""
+    order with ties in index order, every entry whose exclusive cumulative mass, in
+    multiples of 2^-31 (each entry rounded), is <= round(top_p * 2^31)."""
     p = np.asarray(p, dtype=np.float32)
     if top_p >= 1.0:
         return np.ones(p.shape, dtype=bool)
-    q = to_fixed(p)
-    limit = int(np.rint(np.float64(np.float32(top_p)) * FIXED_ONE))
+    q = np.rint(p.astype(np.float64) * SELECT_ONE).astype(np.uint64)
+    limit = int(np.rint(np.float64(np.float32(top_p)) * SELECT_ONE))
     order = np.argsort(-p, kind="stable")
     excl = np.concatenate([[0], np.cumsum(q[order].astype(object))[:-1]])
     keep = np.zeros(p.shape, dtype=bool)
