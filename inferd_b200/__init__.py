@@ -6,6 +6,7 @@ Modules mirror the reference's (likhith-v1/inferd) call surface:
     inferd_b200.paged_cache           <- core/paged_cache.py
     inferd_b200.paged_attn_interface  <- core/paged_attn_interface.py
     inferd_b200.fp8_linear            <- bench/model_loader.py FP8 weight-only linear
+    inferd_b200.sampling              <- core/spec_decode.py nucleus_probs / sample_from
     inferd_b200.sharded               sequence shards per GPU, outputs gathered over NCCL
 
 All kernels live in libinferd_sm100a.so (C ABI: include/inferd_b200.h), built with
