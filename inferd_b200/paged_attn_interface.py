@@ -11,6 +11,9 @@ enables the routes the reference left to eager:
                     are appended to a paged cache, then one batched decode launch)
   "verify"          b == 1, 1 < q_len and q_len * group <= 32 (the speculative verify
                     window, causal over the cached prefix; longer prefills stay on eager)
+
+A model driven with a PagedRuntimeCache (inferd_b200.paged_runtime) needs only install():
+its full-attention layers then read K/V from the cache's persistent pool.
 """
 
 from __future__ import annotations
@@ -25,6 +28,9 @@ _MAX_VERIFY_ROWS = 32
 
 _real_eager = None
 _routes: frozenset[str] = frozenset({"decode"})
+# the PagedRuntimeCache (inferd_b200.paged_runtime) whose step is in progress: its
+# full-attention layers attend over its pool instead of the K/V HF passes in
+_runtime = None
 
 
 def _paged_cache_for(k: torch.Tensor, v: torch.Tensor, lengths: list[int]) -> tuple[PagedKVCache, list[int]]:
@@ -114,7 +120,11 @@ def _verify(query, key, value, scaling):
 
 
 def _wrapper(module, query, key, value, attention_mask, scaling, dropout=0.0, **kwargs):
-    """Dispatch on shape (core/paged_attn_interface.py:68-75)."""
+    """Dispatch on shape (core/paged_attn_interface.py:68-75); a layer of a persistent
+    PagedRuntimeCache step attends over that cache's pool."""
+    rt = _runtime
+    if rt is not None and rt.owns_layer(getattr(module, "layer_idx", None)):
+        return rt.attend(module.layer_idx, query, scaling), None
     b, _, q_len, _ = query.shape
     group = query.shape[1] // key.shape[1]
     take = (b == 1 and q_len == 1) \
