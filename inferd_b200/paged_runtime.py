@@ -24,6 +24,10 @@ stack_caches / split_caches), and its paged cache is a one-shot round trip
                    position_ids=cache.position_ids()).logits
     cache.release(seq_id)                        # frees its pages, moves one state row
 
+Speculative verify (core/spec_decode.py:117-170): `snap = cache.snapshot()`, one forward of
+the gamma + 1 window (causal inside it), then `cache.restore(snap)` and a forward of the
+emitted tokens -- the K/V rollback is a page-table truncation, not a cache copy.
+
 This is the "persistent paged runtime cache" the reference plans as its next step
 (core/batched_cache.py, core/scheduler.py:142-159); the page-table semantics are
 PagedKVCache's (core/paged_cache.py:95-252).
@@ -130,6 +134,33 @@ class PagedRuntimeCache(DynamicCache):
             lyr.max_batch_size = n
             lyr.dtype, lyr.device = self._conv[layer].dtype, self._conv[layer].device
             lyr.conv_kernel_size = self._conv[layer].shape[-1]
+
+    # ------------------------------------------------------------ speculative rollback
+    def snapshot(self) -> dict:
+        """Lengths and linear-attention states of the active rows before a speculative
+        verify forward (core/spec_decode.py:118-119 _snapshot_linear).  The K/V need no
+        copy: rollback only shortens the page tables."""
+        n = len(self.rows)
+        return {"rows": list(self.rows),
+                "lengths": [self.pool.sequence_length(s) for s in self.rows],
+                "conv": {k: v[:n].clone() for k, v in self._conv.items()},
+                "rec": {k: v[:n].clone() for k, v in self._rec.items()}}
+
+    def restore(self, snap: dict, lengths: list[int] | None = None) -> None:
+        """Roll the active rows back to `snap` (core/spec_decode.py:48-57 _restore_to, which
+        copies the whole cache): linear states are copied back and each row's K/V is cut to
+        `lengths` (default: the snapshot's) by truncating its page table -- the tail blocks
+        return to the allocator and no K/V byte moves."""
+        if snap["rows"] != self.rows:
+            raise ValueError("the active rows changed since the snapshot")
+        n = len(self.rows)
+        for k, v in snap["conv"].items():
+            self._conv[k][:n].copy_(v)
+        for k, v in snap["rec"].items():
+            self._rec[k][:n].copy_(v)
+        for s, length in zip(self.rows, lengths if lengths is not None else snap["lengths"]):
+            self.pool.truncate_sequence(s, length)
+        self._use_rows()
 
     def position_ids(self) -> torch.Tensor:
         """[rows, 1] positions of the next token of every active row."""

@@ -80,3 +80,50 @@ def test_batched_decode_matches_per_sequence_hf(cuda_device, dtype, tol):
             (n + steps + 15) // 16 for n in (33, 17))  # sequence 0's pages went back
     finally:
         paged_attn_interface.uninstall()
+
+
+def test_speculative_window_and_rollback(cuda_device):
+    # verify a 5-token window for every row, roll back, then feed 2 "accepted" tokens: the
+    # logits equal a clean HF run over prompt + those tokens (the rejected ones left no trace)
+    from transformers import DynamicCache
+
+    from inferd_b200 import paged_attn_interface
+    from inferd_b200.paged_runtime import PagedRuntimeCache
+
+    model = _model(torch.float32, cuda_device)
+    g = torch.Generator().manual_seed(2)
+    prompts = [torch.randint(0, 512, (n,), generator=g).tolist() for n in (14, 31)]
+    window = [torch.randint(0, 512, (5,), generator=g).tolist() for _ in prompts]
+    keep = [w[:2] for w in window]
+    paged_attn_interface.uninstall()
+    with torch.no_grad():
+        clean = []
+        for p, k in zip(prompts, keep):
+            kv = DynamicCache(config=model.config)
+            model(torch.tensor([p], device=cuda_device), past_key_values=kv, use_cache=True)
+            clean.append(model(torch.tensor([k], device=cuda_device), past_key_values=kv,
+                               use_cache=True).logits[0].float().cpu())
+    paged_attn_interface.install()
+    try:
+        cache = PagedRuntimeCache(model.config, num_blocks=32, max_seqs=2, dtype=torch.float32,
+                                  device=cuda_device)
+        with torch.no_grad():
+            for sid, p in enumerate(prompts):
+                cache.begin_prefill(sid)
+                model(torch.tensor([p], device=cuda_device), past_key_values=cache, use_cache=True)
+                cache.end_prefill()
+            free_before = cache.pool.allocator.free_count
+            snap = cache.snapshot()
+            pos = cache.position_ids() + torch.arange(5, device=cuda_device)
+            model(torch.tensor(window, device=cuda_device), past_key_values=cache, use_cache=True,
+                  position_ids=pos)
+            assert [cache.pool.sequence_length(s) for s in cache.rows] == [19, 36]
+            cache.restore(snap)
+            assert cache.pool.allocator.free_count == free_before  # the window's blocks came back
+            pos = cache.position_ids() + torch.arange(2, device=cuda_device)
+            lg = model(torch.tensor(keep, device=cuda_device), past_key_values=cache, use_cache=True,
+                       position_ids=pos).logits.float().cpu()
+        for r in range(2):
+            assert (lg[r] - clean[r]).abs().max() < 2e-3
+    finally:
+        paged_attn_interface.uninstall()
