@@ -2,6 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|long|verify]
                     [--impl ours|reference]
+    python bench.py --workload fp8|fp8-dynamic|sampling     (one line per kernel case)
 
 One step = one decode step of one attention layer for every sequence this GPU owns:
 a one-token KV append per sequence (reshape_and_cache) followed by paged attention
@@ -419,10 +420,18 @@ FP8_PEAK_NOMINAL_TFLOPS = 4500.0  # dense e4m3 per B200 (no measured FP8 figure 
 
 
 def run_fp8(args, device: torch.device) -> list[dict]:
-    """Config 4: W [17408, 5120] e4m3 from N(0, 0.02) bf16 quantised per channel, x ~ N(0,1)
-    bf16 [M, 5120].  Three weight copies (267 MB > L2) rotate between calls so every call
-    streams its weight from HBM.  One line per M."""
-    from inferd_b200.fp8_linear import fp8_linear, pack_fp8_weight, quantize_fp8_per_channel
+    """Config 4: W [17408, 5120] e4m3 from N(0, 0.02) bf16 quantised per channel ("fp8",
+    weight-only) or per tensor ("fp8-dynamic", activations quantised per tensor on every
+    call), x ~ N(0,1) bf16 [M, 5120].  Three weight copies (267 MB > L2) rotate between
+    calls so every call streams its weight from HBM.  One line per M."""
+    from functools import partial
+
+    from inferd_b200.fp8_linear import (fp8_dynamic_linear, fp8_linear, pack_fp8_weight,
+                                        quantize_fp8_dynamic, quantize_fp8_per_channel)
+
+    dynamic = args.workload == "fp8-dynamic"
+    quantize = quantize_fp8_dynamic if dynamic else quantize_fp8_per_channel
+    linear = partial(fp8_dynamic_linear, granularity="tensor") if dynamic else fp8_linear
 
     peaks = measured_peaks()
     p = REPO / "MEASURED_PEAKS.json"
@@ -431,7 +440,7 @@ def run_fp8(args, device: torch.device) -> list[dict]:
     copies = []
     for _ in range(3):
         w = torch.randn(FP8_N, FP8_K, generator=g, device=device, dtype=torch.float32).mul_(0.02)
-        q, s = quantize_fp8_per_channel(w.to(torch.bfloat16))
+        q, s = quantize(w.to(torch.bfloat16))
         copies.append((pack_fp8_weight(q), s) if args.fp8_layout == "packed" else (q, s))
         del w, q
     stream = torch.cuda.current_stream(device)
@@ -442,7 +451,7 @@ def run_fp8(args, device: torch.device) -> list[dict]:
         out = torch.empty(m, FP8_N, dtype=torch.bfloat16, device=device)
         for i in range(args.warmup):
             q, s = copies[i % 3]
-            fp8_linear(x, q, s, out=out, packed_shape=shape)
+            linear(x, q, s, out=out, packed_shape=shape)
         torch.cuda.synchronize(device)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         # keep the GPU busy while the host queues the timed calls, so the events time the
@@ -451,7 +460,7 @@ def run_fp8(args, device: torch.device) -> list[dict]:
         e0.record(stream)
         for i in range(args.steps):
             q, s = copies[i % 3]
-            fp8_linear(x, q, s, out=out, packed_shape=shape)
+            linear(x, q, s, out=out, packed_shape=shape)
         e1.record(stream)
         torch.cuda.synchronize(device)
         ms = e0.elapsed_time(e1) / args.steps
@@ -459,25 +468,29 @@ def run_fp8(args, device: torch.device) -> list[dict]:
         flops = 2.0 * m * FP8_N * FP8_K
         gbs = nbytes / (ms * 1e-3) / 1e9
         tfs = flops / (ms * 1e-3) / 1e12
+        planes = 1 if dynamic else 2  # e4m3 activation planes the tensor pipe multiplies
         lines.append({
-            "metric": "fp8 weight-only linear (config 4)", "m": m, "n": FP8_N, "k": FP8_K,
+            "metric": ("fp8-dynamic linear, per-tensor scales (config 4)" if dynamic
+                       else "fp8 weight-only linear (config 4)"), "m": m, "n": FP8_N, "k": FP8_K,
             "ms": round(ms, 5), "value": round(tfs, 1), "unit": "TFLOP/s",
             "hbm_gbs": round(gbs, 1), "pct_of_hbm_peak": round(100 * gbs / peaks["hbm_gbs"], 2),
             "pct_of_fp8_nominal_peak": round(100 * tfs / FP8_PEAK_NOMINAL_TFLOPS, 2),
             "pct_of_measured_bf16_peak": round(100 * tfs / bf16_peak, 2),
-            "tensor_flops_issued": "2x algorithmic (two e4m3 activation planes)",
+            "tensor_flops_issued": ("1x algorithmic (one e4m3 activation plane)" if dynamic
+                                    else "2x algorithmic (two e4m3 activation planes)"),
             "roofline": {
                 "bound": "tensor" if m >= 128 else "hbm",
                 "achieved": round(tfs, 1) if m >= 128 else round(gbs, 1),
                 "peak": round(2 * bf16_peak, 1) if m >= 128 else peaks["hbm_gbs"],
                 "unit": "TFLOP/s" if m >= 128 else "GB/s",
                 "frac": round(tfs / (2 * bf16_peak), 4) if m >= 128 else round(gbs / peaks["hbm_gbs"], 4),
-                "tensor_pipe_frac": round(2 * tfs / (2 * bf16_peak), 4),
+                "tensor_pipe_frac": round(planes * tfs / (2 * bf16_peak), 4),
                 "peak_source": "of measured: e4m3 dense peak = 2 x the measured cuBLAS bf16 burst"
                                if m >= 128 else "of measured: HBM copy bandwidth",
             },
             "calls_timed": args.steps,
-            "timing": "one CUDA event pair around the timed calls (split + GEMM per call)",
+            "timing": ("one CUDA event pair around the timed calls (absmax + quantise + GEMM per call)"
+                       if dynamic else "one CUDA event pair around the timed calls (split + GEMM per call)"),
             "l2": "three weight copies rotated (267 MB > 126 MB L2)",
             "weight_layout": args.fp8_layout,
         })
@@ -661,7 +674,8 @@ def main(argv=None) -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["fp8", "sampling"], default="decode")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["fp8", "fp8-dynamic", "sampling"],
+                    default="decode")
     ap.add_argument("--fp8-m", default="1,8,32,128,256", help="token counts for --workload fp8")
     ap.add_argument("--fp8-layout", choices=["packed", "rowmajor"], default="packed")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -689,7 +703,7 @@ def main(argv=None) -> int:
             for line in run_sampling(args, device):
                 print(json.dumps(line), flush=True)
         return 0
-    if args.workload == "fp8":
+    if args.workload in ("fp8", "fp8-dynamic"):
         if rank == 0:
             for line in run_fp8(args, device):
                 print(json.dumps(line), flush=True)

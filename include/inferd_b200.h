@@ -202,6 +202,34 @@ INFERD_API size_t inferd_fp8_linear_workspace_bytes(int64_t m, int64_t n, int64_
                                                     int32_t device);
 
 /*
+ * FP8 with dynamic activation scaling: the reference's "fp8-dynamic" recipe, torchao 0.17.0
+ * Float8DynamicActivationFloat8WeightConfig() (bench/model_loader.py:53-55; granularity
+ * PerTensor by default, PerRow optional).  A tensor (or row) is quantised as
+ * s = amax / 448 in fp32 (1 when amax is 0), q = e4m3(x / s): IEEE division,
+ * round-to-nearest-even, saturating at +-448 (torchao's clamp before the cast).
+ *
+ * inferd_fp8_quantize_dynamic: x [rows, k] (f32/f16/bf16) -> q e4m3 [rows, k] and
+ * scale fp32 [rows] (per tensor: every entry holds the tensor's scale).  Per tensor needs
+ * row_amax, rows floats of scratch; per row ignores it.  Used at load time for the weights
+ * (every row of scale then feeds the linear's w_scale) and by the linear for activations.
+ *
+ * inferd_fp8_dynamic_linear: y[m, n] = s_x[m] * s_w[n] * sum_k q_x[m, k] * w[n, k], the
+ * activations quantised on the fly with `granularity` (one e4m3 plane: half the tensor
+ * work of inferd_fp8_linear), fp32 accumulation in TMEM, bf16 out.  Arguments, layouts and
+ * workspace (inferd_fp8_linear_workspace_bytes) as inferd_fp8_linear.
+ */
+typedef enum { INFERD_FP8_PER_TENSOR = 0, INFERD_FP8_PER_ROW = 1 } inferd_fp8_granularity_t;
+
+INFERD_API int inferd_fp8_quantize_dynamic(const void* x, int32_t x_dtype, void* q, float* scale,
+                                           int64_t rows, int64_t k, int32_t granularity,
+                                           float* row_amax, void* stream);
+
+INFERD_API int inferd_fp8_dynamic_linear(void* y, const void* x, const void* w_e4m3,
+                                         const float* w_scale, int64_t m, int64_t n, int64_t k,
+                                         int32_t w_layout, int32_t granularity, void* workspace,
+                                         size_t workspace_bytes, void* stream);
+
+/*
  * Decode-step sampling, one row per sequence: temperature + top-p ("nucleus")
  * probabilities and one multinomial draw.  Replaces core/spec_decode.py:14-31
  * nucleus_probs and :34-35 sample_from as called by the scheduler (core/scheduler.py:341-342)

@@ -2,6 +2,11 @@
 //
 // y[m, n] = s_w[n] * sum_k x[m, k] * q[n, k]       x bf16 [M, K], q e4m3 [N, K], y bf16 [M, N]
 //
+// The same GEMM serves the reference's "fp8-dynamic" recipe (torchao's
+// Float8DynamicActivationFloat8WeightConfig, bench/model_loader.py:53-55): there x is
+// quantised on the fly to ONE e4m3 plane with s_x = amax / 448 (per tensor or per row) and
+// y = s_x[m] s_w[n] sum_k q_x[m, k] q[n, k] -- the kernel's `planes = 1` mode.
+//
 // The reference quantises every nn.Linear but lm_head at load time with torchao's
 // Float8WeightOnlyConfig (bench/model_loader.py:46-58): per output channel
 // s_w[n] = max_k |W[n, k]| / 448 and q = e4m3(W / s_w), activations stay bf16.
@@ -202,6 +207,7 @@ struct Fp8Params {
   float* part;              // [slot][2][T][128] partial accumulators
   int32_t* error_word;
   int32_t y_tma;            // 1: ymap describes y (bf16 [M, N], 16-byte row pitch)
+  int32_t planes;           // activation planes: 2 = exact h + l split, 1 = one e4m3 copy
 };
 
 constexpr int kFp8Warps = 6;  // 0: TMA producer, 1: MMA issuer (leader CTA), 2..5: epilogue
@@ -225,16 +231,21 @@ __device__ __forceinline__ int fp8_cluster_of(int64_t g, int64_t W, int C) {
   return static_cast<int>(c);
 }
 
-// B rows each CTA of the pair holds for a launch tile of T tokens.  With T <= 128 the MMA's
-// B operand is [h tile; l tile] (N = 2T): CTA 0 holds the h plane, CTA 1 the l plane, and
-// the accumulator's column halves are added in the epilogue.  With T > 128 (N would exceed
-// 256) the h and l MMAs (N = T each) accumulate into the same T columns and each CTA holds
-// T/2 tokens of both planes.  Either way a CTA stages T * 128 activation bytes per K step.
-__host__ __device__ constexpr int fp8_acc_cols(int T) { return T <= 128 ? 2 * T : T; }
+// B rows each CTA of the pair holds for a launch tile of T tokens.  Two planes (the exact
+// split): with T <= 128 the MMA's B operand is [h tile; l tile] (N = 2T): CTA 0 holds the
+// h plane, CTA 1 the l plane, and the accumulator's column halves are added in the
+// epilogue.  With T > 128 (N would exceed 256) the h and l MMAs (N = T each) accumulate
+// into the same T columns and each CTA holds T/2 tokens of both planes.  Either way a CTA
+// stages T * 128 activation bytes per K step.  One plane (dynamic activation scaling):
+// N = T, each CTA holds T/2 tokens, T/2 * 128 bytes per K step.
+__host__ __device__ constexpr int fp8_acc_cols(int T, int planes) { return planes == 2 && T <= 128 ? 2 * T : T; }
+__host__ __device__ constexpr int fp8_x_stage_bytes(int T, int planes) {
+  return planes == 2 ? T * kTileK : (T / 2) * kTileK;
+}
 // tcgen05.alloc takes a power of two >= 32; two accumulators (double buffering)
-__host__ __device__ constexpr uint32_t fp8_tmem_cols(int T) {
+__host__ __device__ constexpr uint32_t fp8_tmem_cols(int T, int planes) {
   uint32_t c = 32;
-  while (c < static_cast<uint32_t>(2 * fp8_acc_cols(T))) c <<= 1;
+  while (c < static_cast<uint32_t>(2 * fp8_acc_cols(T, planes))) c <<= 1;
   return c;
 }
 
@@ -274,9 +285,10 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
   const bool leader = rank == 0;
   const int T = p.tok_tile;
   const int S = p.stages;
-  const bool merged = T <= 128;
-  const uint32_t w_bytes = kTileN * kTileK;                    // 16 KiB
-  const uint32_t x_bytes = static_cast<uint32_t>(T) * kTileK;  // this CTA's activation rows
+  const bool two = p.planes == 2;
+  const bool merged = two && T <= 128;
+  const uint32_t w_bytes = kTileN * kTileK;                                        // 16 KiB
+  const uint32_t x_bytes = static_cast<uint32_t>(fp8_x_stage_bytes(T, p.planes));  // this CTA's activation rows
   const uint32_t stage_bytes = w_bytes + x_bytes;              // multiple of 1024
   const int KS = (p.k + kTileK - 1) / kTileK;
   const int NT = (p.n + kTileN - 1) / kTileN;
@@ -287,8 +299,8 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
   const int64_t g0 = static_cast<int64_t>(cl) * W / C;
   const int64_t g1 = static_cast<int64_t>(cl + 1) * W / C;
   const int n_units = static_cast<int>(g1 - g0);
-  const uint32_t acc_cols = static_cast<uint32_t>(fp8_acc_cols(T));
-  const uint32_t ncols = fp8_tmem_cols(T);
+  const uint32_t acc_cols = static_cast<uint32_t>(fp8_acc_cols(T, p.planes));
+  const uint32_t ncols = fp8_tmem_cols(T, p.planes);
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -332,9 +344,11 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
         const int ks = static_cast<int>(g % KS);
         if (merged) {
           tma_load_2d_pair(st + w_bytes, leader ? &hmap : &lmap, ks * kTileK, x_row, bar, pol_x);
-        } else {
+        } else if (two) {
           tma_load_2d_pair(st + w_bytes, &hmap, ks * kTileK, x_row, bar, pol_x);
           tma_load_2d_pair(st + w_bytes + x_bytes / 2, &lmap, ks * kTileK, x_row, bar, pol_x);
+        } else {
+          tma_load_2d_pair(st + w_bytes, &hmap, ks * kTileK, x_row, bar, pol_x);
         }
       };
       auto full_of = [&](int s) { return cluster_addr(smem_u32(&full[s]), 0); };
@@ -413,7 +427,7 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
             const uint64_t ad = sw128_desc(a0 + kk * kMmaK);
             const uint32_t accumulate = (in_seg | kk) != 0 ? 1u : 0u;
             mma_f8_pair(acc, ad, sw128_desc(b0 + kk * kMmaK), idesc, accumulate);
-            if (!merged) mma_f8_pair(acc, ad, sw128_desc(b0 + x_bytes / 2 + kk * kMmaK), idesc, 1u);
+            if (two && !merged) mma_f8_pair(acc, ad, sw128_desc(b0 + x_bytes / 2 + kk * kMmaK), idesc, 1u);
           }
           mma_commit_pair(&empty[s]);  // stage s free in both CTAs once these MMAs have read it
         }
@@ -724,6 +738,112 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict_
   if (threadIdx.x == 0) scale[n] = s;
 }
 
+// ---------------------------------------------------------------- dynamic (absmax) scaling
+// torchao's Float8DynamicActivationFloat8WeightConfig scales a tensor by s = amax / 448,
+// over the whole tensor (PerTensor, its default) or per row (PerRow), and stores
+// q = e4m3(clamp(x / s, -448, 448)); the same rule quantises the activations of every
+// forward and, once, the weights.  amax is exact (a maximum of magnitudes), s an fp32
+// division, x / s an IEEE division rounded to fp32, the cast round-to-nearest-even with
+// saturation (the clamp).  An all-zero tensor (row) gets s = 1 and zero codes.
+
+// 16-byte vector loads over a row of T when its length and base allow them.
+template <typename T>
+__device__ __forceinline__ bool row_vectorizable(const T* row, int64_t k) {
+  return (k * static_cast<int64_t>(sizeof(T))) % 16 == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+}
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& v, float* out) {
+  constexpr int E = 16 / sizeof(T);
+  const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+  for (int j = 0; j < E; ++j) out[j] = to_f32<T>(e[j]);
+}
+
+template <typename T>
+__device__ float row_absmax(const T* __restrict__ row, int64_t k, float* red) {
+  constexpr int E = 16 / sizeof(T);
+  float amax = 0.f;
+  if (row_vectorizable(row, k)) {
+    const uint4* v = reinterpret_cast<const uint4*>(row);
+    for (int64_t i = threadIdx.x; i < k / E; i += blockDim.x) {
+      float f[E];
+      unpack16<T>(__ldg(v + i), f);
+#pragma unroll
+      for (int j = 0; j < E; ++j) amax = fmaxf(amax, fabsf(f[j]));
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) amax = fmaxf(amax, fabsf(to_f32<T>(row[i])));
+  }
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = 0.f;
+  for (int i = 0; i < static_cast<int>(blockDim.x / 32); ++i) amax = fmaxf(amax, red[i]);
+  __syncthreads();  // red is reused by the caller
+  return amax;
+}
+
+// One CTA per row: row_amax[r] = max_k |x[r, k]|.
+template <typename T>
+__global__ void __launch_bounds__(256) row_absmax_kernel(const T* __restrict__ x, int64_t k,
+                                                         float* __restrict__ row_amax) {
+  __shared__ float red[8];
+  grid_launch_dependents();
+  const float a = row_absmax(x + static_cast<int64_t>(blockIdx.x) * k, k, red);
+  if (threadIdx.x == 0) row_amax[blockIdx.x] = a;
+}
+
+// One CTA per row: s = amax / 448 with amax over the tensor (row_amax of every row, from
+// row_absmax_kernel, which this grid may overlap until griddepcontrol.wait) or over the
+// row; q[r, :] = e4m3(x[r, :] / s) and scale[r] = s.
+template <typename T, bool kPerTensor>
+__global__ void __launch_bounds__(256) quantize_dynamic_kernel(const T* __restrict__ x, int64_t rows, int64_t k,
+                                                               const float* __restrict__ row_amax,
+                                                               uint8_t* __restrict__ q, float* __restrict__ scale) {
+  __shared__ float red[8];
+  grid_launch_dependents();
+  const int64_t r = blockIdx.x;
+  const T* row = x + r * k;
+  float amax = 0.f;
+  if (kPerTensor) {
+    grid_dependency_wait();
+    for (int64_t i = threadIdx.x; i < rows; i += blockDim.x) amax = fmaxf(amax, __ldcg(row_amax + i));
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = 0.f;
+    for (int i = 0; i < static_cast<int>(blockDim.x / 32); ++i) amax = fmaxf(amax, red[i]);
+  } else {
+    amax = row_absmax(row, k, red);
+  }
+  float s = __fdiv_rn(amax, 448.f);
+  if (!(s > 0.f)) s = 1.f;
+  uint8_t* qrow = q + r * k;
+  constexpr int E = 16 / sizeof(T);
+  if (row_vectorizable(row, k) && (reinterpret_cast<uintptr_t>(qrow) % E) == 0) {
+    const uint4* v = reinterpret_cast<const uint4*>(row);
+    for (int64_t i = threadIdx.x; i < k / E; i += blockDim.x) {
+      float f[E];
+      unpack16<T>(__ldg(v + i), f);
+      uint8_t c[E];
+#pragma unroll
+      for (int j = 0; j < E; ++j) c[j] = to_e4m3(__fdiv_rn(f[j], s));
+      if constexpr (E == 8) {
+        uint2 o;
+        o.x = c[0] | (c[1] << 8) | (c[2] << 16) | (static_cast<uint32_t>(c[3]) << 24);
+        o.y = c[4] | (c[5] << 8) | (c[6] << 16) | (static_cast<uint32_t>(c[7]) << 24);
+        *reinterpret_cast<uint2*>(qrow + i * E) = o;
+      } else {
+#pragma unroll
+        for (int j = 0; j < E; ++j) qrow[i * E + j] = c[j];
+      }
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) qrow[i] = to_e4m3(__fdiv_rn(to_f32<T>(row[i]), s));
+  }
+  if (threadIdx.x == 0) scale[r] = s;
+}
+
 // ---------------------------------------------------------------- weight packing
 // packed[(nt * KT + kt) * 16384 + r * 128 + ((c16 ^ (r & 7)) * 16) + b] =
 //     q[nt * 128 + r, kt * 128 + c16 * 16 + b]   (zero outside [N, K])
@@ -755,6 +875,23 @@ __global__ void __launch_bounds__(256) pack_weights_kernel(const uint8_t* __rest
 }
 
 // ---------------------------------------------------------------- host side
+// Launch with programmatic stream serialisation: the grid may start while the previous
+// one on the stream still runs; it calls griddepcontrol.wait before reading its output.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(dim3 grid, dim3 block, cudaStream_t s, void (*kernel)(KArgs...), Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
 // 2-D tensor map over a row-major [rows, cols] array of 1-byte (u8) or 2-byte (bf16)
 // elements with a (box_cols x box_rows) box; 128-byte swizzle optional.
 struct MapKey {
@@ -826,7 +963,9 @@ inline size_t align256_fp8(size_t v) { return (v + 255) & ~static_cast<size_t>(2
 
 // Workspace: [tile tickets: fixed region][h plane][l plane][x scales][partials].  The
 // ticket region has one size for every call, so calls of any shape can share a
-// workspace; completed calls leave the tickets at zero.
+// workspace; completed calls leave the tickets at zero.  The dynamic-scaling calls use
+// the l region for the per-row absmax; the partials region fits the plans of both kinds
+// of call, so one workspace serves both.
 constexpr int kMaxTilesFp8 = 4096;  // N <= 524288
 constexpr size_t kFp8CounterBytes = kMaxTilesFp8 * sizeof(int32_t);
 
@@ -841,14 +980,14 @@ struct Fp8Plan {
 // Weight-tile pairs of an [n, k] weight.
 inline int64_t fp8_pairs(int64_t n) { return ((n + kTileN - 1) / kTileN + 1) / 2; }
 
-inline Fp8Plan fp8_plan(int64_t rem_tokens, int64_t n, int64_t k, int sms) {
+inline Fp8Plan fp8_plan(int64_t rem_tokens, int64_t n, int64_t k, int sms, int planes) {
   Fp8Plan pl;
   const int64_t t = rem_tokens < kMaxTokTile ? rem_tokens : kMaxTokTile;
   pl.tile = static_cast<int>((t + 15) / 16 * 16);
   // two CTAs per SM while both double-buffered accumulators fit TMEM's 512 columns
-  pl.per_sm = 2 * fp8_tmem_cols(pl.tile) <= 512 ? 2 : 1;
+  pl.per_sm = 2 * fp8_tmem_cols(pl.tile, planes) <= 512 ? 2 : 1;
   const int budget = pl.per_sm == 2 ? kSmemBudget2 : kSmemBudget;
-  const int stage_bytes = kTileN * kTileK + pl.tile * kTileK;
+  const int stage_bytes = kTileN * kTileK + fp8_x_stage_bytes(pl.tile, planes);
   pl.stages = (budget - kEpiStageBytes) / stage_bytes;
   if (pl.stages > 8) pl.stages = 8;
   const int64_t pairs = fp8_pairs(n);
@@ -875,8 +1014,13 @@ inline Fp8Workspace fp8_workspace(int64_t m, int64_t n, int64_t k, int sms) {
   w.l = w.h + align256_fp8(static_cast<size_t>(m * k));
   w.scale = w.l + align256_fp8(static_cast<size_t>(m * k));
   w.part = w.scale + align256_fp8(static_cast<size_t>(m) * 4);
-  const Fp8Plan pl = fp8_plan(m, n, k, sms);  // the first launch tile is the largest
-  w.total = w.part + align256_fp8(static_cast<size_t>(2 * (pl.clusters + fp8_pairs(n))) * pl.tile * kTileN * 4);
+  size_t part = 0;
+  for (int planes = 1; planes <= 2; ++planes) {
+    const Fp8Plan pl = fp8_plan(m, n, k, sms, planes);  // the first launch tile is the largest
+    const size_t b = static_cast<size_t>(2 * (pl.clusters + fp8_pairs(n))) * pl.tile * kTileN * 4;
+    if (b > part) part = b;
+  }
+  w.total = w.part + align256_fp8(part);
   return w;
 }
 
@@ -941,9 +1085,13 @@ extern "C" int inferd_fp8_pack_weights(const void* w_e4m3, void* w_packed, int64
   return launch_status();
 }
 
-extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, const float* w_scale, int64_t m,
-                                 int64_t n, int64_t k, int32_t w_layout, void* workspace,
-                                 size_t workspace_bytes, void* stream) {
+// Activation preparation of one call: 0 = exact two-plane split (weight-only FP8),
+// 1 = one e4m3 plane scaled by the tensor's absmax, 2 = one plane scaled per row.
+enum Fp8ActMode { kActSplit = 0, kActDynTensor = 1, kActDynRow = 2 };
+
+static int fp8_linear_impl(void* y, const void* x, const void* w_e4m3, const float* w_scale, int64_t m, int64_t n,
+                           int64_t k, int32_t w_layout, int act_mode, void* workspace, size_t workspace_bytes,
+                           void* stream) {
   if (w_layout != 0 && w_layout != 1) return INFERD_ERR_INVALID_ARGUMENT;
   if (m < 0 || n <= 0 || k <= 0) return INFERD_ERR_INVALID_ARGUMENT;
   if (m == 0) return INFERD_OK;
@@ -953,6 +1101,7 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
   if ((reinterpret_cast<uintptr_t>(w_e4m3) & 15) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
     return INFERD_ERR_INVALID_ARGUMENT;  // 16-byte aligned weights and activations
   if ((n + kTileN - 1) / kTileN > kMaxTilesFp8) return INFERD_ERR_UNSUPPORTED;
+  const int planes = act_mode == kActSplit ? 2 : 1;
   const int sms = current_sm_count();
   const Fp8Workspace wl = fp8_workspace(m, n, k, sms);
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0 || workspace_bytes < wl.total)
@@ -972,19 +1121,22 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
         cudaFuncSetAttribute(fp8_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 1024);
     if (e != cudaSuccess) return cuda_status(e);
     // all of the unified L1/shared array as shared memory, so two ~110 KB CTAs fit per SM;
-    // the split kernel asks for the same carveout, so the SMs are not reconfigured
-    // between the two launches of every call
-    e = cudaFuncSetAttribute(fp8_linear_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return cuda_status(e);
-    e = cudaFuncSetAttribute(split_activations_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return cuda_status(e);
+    // the activation kernels ask for the same carveout, so the SMs are not reconfigured
+    // between the launches of a call
+    const void* kernels[] = {reinterpret_cast<const void*>(fp8_linear_kernel),
+                             reinterpret_cast<const void*>(split_activations_kernel),
+                             reinterpret_cast<const void*>(row_absmax_kernel<__nv_bfloat16>),
+                             reinterpret_cast<const void*>(quantize_dynamic_kernel<__nv_bfloat16, true>),
+                             reinterpret_cast<const void*>(quantize_dynamic_kernel<__nv_bfloat16, false>)};
+    for (const void* f : kernels) {
+      e = cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+      if (e != cudaSuccess) return cuda_status(e);
+    }
     configured[dev] = true;
   }
 
-  // encode every tensor map before the first launch so no host work separates the two
-  // kernels
+  // encode every tensor map before the first launch so no host work separates the
+  // kernels of a call
   const int n_tok_tiles = static_cast<int>((m + kMaxTokTile - 1) / kMaxTokTile);
   CUtensorMap wmap;
   int st = INFERD_OK;
@@ -1012,22 +1164,38 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
     const int64_t rem =
         i == 0 ? (m < kMaxTokTile ? m : kMaxTokTile) : m - static_cast<int64_t>(n_tok_tiles - 1) * kMaxTokTile;
     tiles[i] = static_cast<int>((rem + 15) / 16 * 16);
-    // rows each CTA of the pair loads per plane: the whole tile, or half of it above 128
-    const uint32_t box = static_cast<uint32_t>(tiles[i] <= 128 ? tiles[i] : tiles[i] / 2);
+    // rows each CTA of the pair loads per plane: the whole tile (two planes, tile <= 128)
+    // or half of it
+    const uint32_t box = static_cast<uint32_t>(planes == 2 && tiles[i] <= 128 ? tiles[i] : tiles[i] / 2);
     st = cached_u8_map(&hmaps[i], h, static_cast<uint64_t>(m), static_cast<uint64_t>(k), box);
     if (st != INFERD_OK) return st;
-    st = cached_u8_map(&lmaps[i], l, static_cast<uint64_t>(m), static_cast<uint64_t>(k), box);
-    if (st != INFERD_OK) return st;
+    if (planes == 2) {
+      st = cached_u8_map(&lmaps[i], l, static_cast<uint64_t>(m), static_cast<uint64_t>(k), box);
+      if (st != INFERD_OK) return st;
+    } else {
+      lmaps[i] = hmaps[i];  // not read
+    }
   }
 
-  split_activations_kernel<<<static_cast<unsigned>(m), kSplitThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
-                                                                             static_cast<int>(k), h, l, xs);
-  st = launch_status();
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  if (act_mode == kActSplit) {
+    split_activations_kernel<<<static_cast<unsigned>(m), kSplitThreads, 0, s>>>(xb, static_cast<int>(k), h, l, xs);
+  } else if (act_mode == kActDynRow) {
+    quantize_dynamic_kernel<__nv_bfloat16, false><<<static_cast<unsigned>(m), 256, 0, s>>>(xb, m, k, nullptr, h, xs);
+  } else {
+    float* row_amax = reinterpret_cast<float*>(l);
+    row_absmax_kernel<__nv_bfloat16><<<static_cast<unsigned>(m), 256, 0, s>>>(xb, k, row_amax);
+    st = launch_status();
+    if (st != INFERD_OK) return st;
+    st = launch_pdl(dim3(static_cast<unsigned>(m)), dim3(256), s, quantize_dynamic_kernel<__nv_bfloat16, true>, xb,
+                    m, k, static_cast<const float*>(row_amax), h, xs);
+  }
+  if (st == INFERD_OK) st = launch_status();
   if (st != INFERD_OK) return st;
 
   for (int t = 0; t < n_tok_tiles; ++t) {
     const int which = (t == n_tok_tiles - 1) ? 1 : 0;
-    const Fp8Plan pl = fp8_plan(m - static_cast<int64_t>(t) * kMaxTokTile, n, k, sms);
+    const Fp8Plan pl = fp8_plan(m - static_cast<int64_t>(t) * kMaxTokTile, n, k, sms, planes);
     const int tile = tiles[which];
     if (pl.stages < 2 || pl.tile != tile) return INFERD_ERR_UNSUPPORTED;
     // The cluster-occupancy query reports one cluster per SM pair for the two-per-SM
@@ -1049,6 +1217,7 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
     p.part = part;
     p.error_word = nullptr;
     p.y_tma = y_tma ? 1 : 0;
+    p.planes = planes;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters);
     cfg.blockDim = dim3(kFp8Threads);
@@ -1067,4 +1236,52 @@ extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, con
     if (st != INFERD_OK) return st;
   }
   return INFERD_OK;
+}
+
+extern "C" int inferd_fp8_linear(void* y, const void* x, const void* w_e4m3, const float* w_scale, int64_t m,
+                                 int64_t n, int64_t k, int32_t w_layout, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  return fp8_linear_impl(y, x, w_e4m3, w_scale, m, n, k, w_layout, kActSplit, workspace, workspace_bytes, stream);
+}
+
+extern "C" int inferd_fp8_dynamic_linear(void* y, const void* x, const void* w_e4m3, const float* w_scale,
+                                         int64_t m, int64_t n, int64_t k, int32_t w_layout, int32_t granularity,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (granularity != INFERD_FP8_PER_TENSOR && granularity != INFERD_FP8_PER_ROW) return INFERD_ERR_INVALID_ARGUMENT;
+  return fp8_linear_impl(y, x, w_e4m3, w_scale, m, n, k, w_layout,
+                         granularity == INFERD_FP8_PER_TENSOR ? kActDynTensor : kActDynRow, workspace,
+                         workspace_bytes, stream);
+}
+
+template <typename T>
+static int quantize_dynamic_launch(const T* x, int64_t rows, int64_t k, int32_t granularity, uint8_t* q,
+                                   float* scale, float* row_amax, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(rows));
+  if (granularity == INFERD_FP8_PER_ROW) {
+    quantize_dynamic_kernel<T, false><<<grid, 256, 0, s>>>(x, rows, k, nullptr, q, scale);
+    return launch_status();
+  }
+  row_absmax_kernel<T><<<grid, 256, 0, s>>>(x, k, row_amax);
+  const int st = launch_status();
+  if (st != INFERD_OK) return st;
+  return launch_pdl(grid, dim3(256), s, quantize_dynamic_kernel<T, true>, x, rows, k,
+                    static_cast<const float*>(row_amax), q, scale);
+}
+
+extern "C" int inferd_fp8_quantize_dynamic(const void* x, int32_t x_dtype, void* q, float* scale, int64_t rows,
+                                           int64_t k, int32_t granularity, float* row_amax, void* stream) {
+  if (rows < 0 || k <= 0) return INFERD_ERR_INVALID_ARGUMENT;
+  if (granularity != INFERD_FP8_PER_TENSOR && granularity != INFERD_FP8_PER_ROW) return INFERD_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return INFERD_OK;
+  if (!x || !q || !scale || (granularity == INFERD_FP8_PER_TENSOR && !row_amax)) return INFERD_ERR_INVALID_ARGUMENT;
+  if (rows > 0x7fffffff) return INFERD_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* qb = static_cast<uint8_t*>(q);
+  if (x_dtype == INFERD_BF16)
+    return quantize_dynamic_launch(static_cast<const __nv_bfloat16*>(x), rows, k, granularity, qb, scale, row_amax, s);
+  if (x_dtype == INFERD_F16)
+    return quantize_dynamic_launch(static_cast<const __half*>(x), rows, k, granularity, qb, scale, row_amax, s);
+  if (x_dtype == INFERD_F32)
+    return quantize_dynamic_launch(static_cast<const float*>(x), rows, k, granularity, qb, scale, row_amax, s);
+  return INFERD_ERR_UNSUPPORTED;
 }

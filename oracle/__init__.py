@@ -36,7 +36,9 @@ from .fp8 import (  # noqa: F401
     E4M3_MAX,
     e4m3_decode,
     e4m3_encode,
+    fp8_dynamic_linear,
     fp8_linear,
+    quantize_dynamic,
     quantize_per_channel,
 )
 from .sampling import (  # noqa: F401

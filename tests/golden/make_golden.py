@@ -274,6 +274,48 @@ def gen_cache_trace(pc) -> dict:
     return trace
 
 
+def _torchao_dynamic_quant(t: torch.Tensor, per_row: bool):
+    """torchao 0.17.0's dynamic float8 scaling restated with the torch ops it calls
+    (_choose_scale_float8 then _quantize_affine_float8): amax of |t| (per tensor or per
+    row), s = amax / 448 in fp32, q = clamp(t.float() / s, -448, 448) cast to e4m3."""
+    amax = t.abs().amax(dim=1, keepdim=True) if per_row else t.abs().amax()
+    s = amax.float() / torch.finfo(torch.float8_e4m3fn).max
+    q = (t.float() / s).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q, s
+
+
+def gen_fp8_dynamic(out: dict) -> None:
+    """The fp8-dynamic recipe (bench/model_loader.py:53-55): weights and activations
+    quantised with torchao's dynamic scaling; per tensor (torchao's default) the product
+    comes from torch._scaled_mm itself, per row from the same formula in float64 (CPU
+    _scaled_mm takes per-tensor scales only)."""
+    g = torch.Generator().manual_seed(4)
+    cases = [("tensor", 5, 96, 320), ("row", 4, 64, 256), ("tensor", 17, 48, 128)]
+    for i, (gran, m, n, k) in enumerate(cases):
+        per_row = gran == "row"
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+        x[0, 3] = 30.0  # an outlier sets the tensor's scale
+        if per_row:
+            w[7] = 0.0
+            x[1, 5:9] = torch.tensor([1e-3, -2e-3, 5e-4, 0.0]).to(torch.bfloat16)
+        qw, sw = _torchao_dynamic_quant(w, per_row)
+        qx, sx = _torchao_dynamic_quant(x, per_row)
+        if per_row:
+            y = ((qx.double() @ qw.double().T) * sx.double() * sw.double().T).to(torch.bfloat16)
+        else:
+            y = torch._scaled_mm(qx, qw.t(), scale_a=sx, scale_b=sw, out_dtype=torch.bfloat16)
+        tag = f"dyn_{i}"
+        out[tag + "_w"] = w.float().numpy()
+        out[tag + "_x"] = x.float().numpy()
+        out[tag + "_qw"] = qw.view(torch.uint8).numpy()
+        out[tag + "_sw"] = sw.reshape(-1).numpy()
+        out[tag + "_qx"] = qx.view(torch.uint8).numpy()
+        out[tag + "_sx"] = sx.reshape(-1).numpy()
+        out[tag + "_y"] = y.float().numpy()
+    out["dyn_cases"] = np.array([[0 if c[0] == "tensor" else 1, c[1], c[2], c[3]] for c in cases], dtype=np.int64)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--reference", default="/root/reference")
@@ -289,6 +331,9 @@ def main() -> int:
     gen_verify(out)
     gen_fp8(out)
     np.savez_compressed(HERE / "reference_golden.npz", **out)
+    dyn: dict = {}
+    gen_fp8_dynamic(dyn)
+    np.savez_compressed(HERE / "fp8_dynamic_golden.npz", **dyn)
     samp: dict = {}
     gen_sampling(samp)
     np.savez_compressed(HERE / "sampling_golden.npz", **samp)
