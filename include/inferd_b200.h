@@ -78,6 +78,18 @@ INFERD_API int inferd_reshape_and_cache(const void* key, const void* value,
                              int32_t* error_word, void* stream);
 
 /*
+ * Device-resident decode metadata.  master [num_rows, capacity] int32 holds the batch's
+ * page tables across steps; one call applies this step's changes and writes the packed
+ * block_tables [num_rows, width] the attention kernels read.  dense = 1: updates is the whole
+ * [num_rows, capacity] table (row_ptr unused); dense = 0: row r's changes are the
+ * (column, block) int32 pairs updates[2 * row_ptr[r] .. 2 * row_ptr[r + 1]).  Replaces the
+ * per-step block_table() rebuild and host->device copy of core/paged_cache.py:207-213.
+ */
+INFERD_API int inferd_block_tables_refresh(int32_t* master, int64_t capacity, const int32_t* row_ptr,
+                                           const int32_t* updates, int32_t dense, int32_t num_rows,
+                                           int32_t width, int32_t* block_tables, void* stream);
+
+/*
  * gather_paged_kv: copy one sequence's pages back to contiguous [seq_len, num_kv_heads,
  * head_dim] tensors.  Replaces core/paged_attn.py:20-61 (gather_paged_kv) and
  * core/paged_cache.py:191-205 (PagedKVCache.gather_layer).  Bit-exact.

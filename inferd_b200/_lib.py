@@ -72,6 +72,8 @@ _SIGNATURES = {
     "inferd_fp8_packed_weight_bytes": (_sz, [_i64, _i64]),
     "inferd_fp8_pack_weights": (ctypes.c_int, [_c_void_p, _c_void_p, _i64, _i64, _c_void_p]),
     "inferd_fp8_linear_workspace_bytes": (_sz, [_i64, _i64, _i64, _i32]),
+    "inferd_block_tables_refresh": (ctypes.c_int, [
+        _c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, _i32, _c_void_p, _c_void_p]),
     "inferd_fp8_quantize_dynamic": (ctypes.c_int, [
         _c_void_p, _i32, _c_void_p, _c_void_p, _i64, _i64, _i32, _c_void_p, _c_void_p]),
     "inferd_fp8_dynamic_linear": (ctypes.c_int, [

@@ -110,10 +110,46 @@ int launch_gather(void* ko, void* vo, const void* kc, const void* vc, const void
   return launch_status();
 }
 
+// Packed decode metadata kept on the device across steps.  Block r updates row r of the
+// master table [rows, capacity] -- dense: the whole row from src (a [rows, capacity] upload);
+// sparse: the entries src[row_ptr[r] .. row_ptr[r+1]) = (column, block) pairs -- and then
+// copies its first `width` entries to out [rows, width].  Rows are independent, so one
+// launch both applies the step's page-table changes and produces the table the attention
+// kernels read.
+__global__ void __launch_bounds__(256) block_tables_refresh_kernel(int32_t* __restrict__ master, int64_t cap,
+                                                                   const int32_t* __restrict__ row_ptr,
+                                                                   const int32_t* __restrict__ src, int32_t dense,
+                                                                   int32_t width, int32_t* __restrict__ out) {
+  const int64_t r = blockIdx.x;
+  int32_t* row = master + r * cap;
+  if (dense) {
+    for (int64_t c = threadIdx.x; c < cap; c += blockDim.x) row[c] = __ldg(src + r * cap + c);
+  } else {
+    const int32_t e0 = __ldg(row_ptr + r), e1 = __ldg(row_ptr + r + 1);
+    for (int32_t e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
+      const int32_t col = __ldg(src + 2 * e), blk = __ldg(src + 2 * e + 1);
+      if (col >= 0 && col < cap) row[col] = blk;
+    }
+  }
+  __syncthreads();
+  for (int64_t c = threadIdx.x; c < width; c += blockDim.x) out[r * width + c] = row[c];
+}
+
 }  // namespace
 }  // namespace inferd
 
 using namespace inferd;
+
+extern "C" int inferd_block_tables_refresh(int32_t* master, int64_t capacity, const int32_t* row_ptr,
+                                           const int32_t* updates, int32_t dense, int32_t num_rows,
+                                           int32_t width, int32_t* block_tables, void* stream) {
+  if (num_rows < 0 || capacity <= 0 || width < 0 || width > capacity) return INFERD_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return INFERD_OK;
+  if (!master || !updates || !block_tables || (!dense && !row_ptr)) return INFERD_ERR_INVALID_ARGUMENT;
+  block_tables_refresh_kernel<<<static_cast<unsigned>(num_rows), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      master, capacity, row_ptr, updates, dense ? 1 : 0, width, block_tables);
+  return launch_status();
+}
 
 extern "C" int inferd_reshape_and_cache(const void* key, const void* value,
                                         int64_t key_token_stride, int64_t key_head_stride,

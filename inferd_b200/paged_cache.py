@@ -78,6 +78,9 @@ class SequencePageTable:
     block_size: int
     blocks: list[int] = field(default_factory=list)
     length: int = 0
+    # lowest page index changed since decode_metadata last packed this table (tables only
+    # change at their tail: appends, rollbacks and truncations); _CLEAN when unchanged
+    dirty_from: int = field(default=0, repr=False, compare=False)
 
     @property
     def block_count(self) -> int:
@@ -101,6 +104,21 @@ class SequencePageTable:
         """Pool slots (block * block_size + offset) of positions start .. start+n-1."""
         bs = self.block_size
         return [self.blocks[p // bs] * bs + p % bs for p in range(start, start + n)]
+
+
+_CLEAN = 1 << 62
+
+
+class _MetaCache:
+    """decode_metadata's state for the last batch it packed: the host copy of the batch's
+    page tables [rows, capacity], each row's block count and list identity at that time,
+    and (CUDA pools) the device copy the refresh kernel updates in place."""
+
+    __slots__ = ("key", "cap", "host", "nblk", "ids", "master", "device")
+
+    def __init__(self, key, cap, host, nblk, ids, master, device) -> None:
+        self.key, self.cap, self.host, self.nblk, self.ids = key, cap, host, nblk, ids
+        self.master, self.device = master, device
 
 
 class _PinnedStaging:
@@ -167,8 +185,8 @@ class PagedKVCache:
         self.sequences: dict[int, SequencePageTable] = {}
         self._stage_i32 = _PinnedStaging(torch.int32)
         self._stage_i64 = _PinnedStaging(torch.int64)
-        # decode_metadata's last host table: (seq ids, column capacity, rows, row signatures)
-        self._meta_cache: tuple | None = None
+        # decode_metadata's last packed batch (host and device copies of its page tables)
+        self._meta_cache: _MetaCache | None = None
 
         shape = (num_blocks, num_kv_heads, block_size, head_dim)
         self.key_cache = [
@@ -207,6 +225,7 @@ class PagedKVCache:
         if freed:
             del table.blocks[keep:]
             self.allocator.free(freed)
+            table.dirty_from = min(table.dirty_from, keep)
         table.length = length
         return freed
 
@@ -215,7 +234,10 @@ class PagedKVCache:
         needed_capacity = table.length + n_tokens
         needed_blocks = (needed_capacity + self.block_size - 1) // self.block_size
         extra = needed_blocks - len(table.blocks)
-        new_blocks = self.allocator.allocate(extra) if extra > 0 else []
+        if extra <= 0:
+            return []
+        new_blocks = self.allocator.allocate(extra)
+        table.dirty_from = min(table.dirty_from, len(table.blocks))
         table.blocks.extend(new_blocks)
         return new_blocks
 
@@ -223,6 +245,7 @@ class PagedKVCache:
         if new_blocks:
             del table.blocks[-len(new_blocks):]
             self.allocator.free(new_blocks)
+            table.dirty_from = min(table.dirty_from, len(table.blocks))
 
     # ------------------------------------------------------------ K/V movement
     def append_tokens(
@@ -278,12 +301,22 @@ class PagedKVCache:
         if per == 0:
             return
         reserved: list[tuple[SequencePageTable, list[int]]] = []
+        bs = self.block_size
         try:
-            for t in tables:
-                reserved.append((t, self._reserve(t, per)))
             slot_list: list[int] = []
-            for t in tables:
-                slot_list.extend(t.slots(t.length, per))
+            if per == 1:
+                # decode: one token per sequence; a new block only when a page fills up
+                for t in tables:
+                    pos = t.length
+                    page = pos // bs
+                    if page >= len(t.blocks):
+                        reserved.append((t, self._reserve(t, 1)))
+                    slot_list.append(t.blocks[page] * bs + pos - page * bs)
+            else:
+                for t in tables:
+                    reserved.append((t, self._reserve(t, per)))
+                for t in tables:
+                    slot_list.extend(t.slots(t.length, per))
             slots = self._slot_tensor(slot_list)
             for layer in range(self.num_layers):
                 self._write(layer, layer_keys[layer], layer_values[layer], slots)
@@ -341,44 +374,91 @@ class PagedKVCache:
     ) -> tuple[torch.Tensor, torch.Tensor, int]:
         """Packed batch metadata for the batched attention kernels.
 
-        Returns (block_tables int32 [B, P], context_lens int32 [B], max_context_len)
-        built from the host page tables and copied to the device in one transfer.
-        extra_tokens is added to every length (for a verify window appended after this
-        call); P defaults to the widest table.
+        Returns (block_tables int32 [B, P], context_lens int32 [B], max_context_len), new
+        tensors on every call, P the widest table (or pad_pages), rows zero-padded.
+        extra_tokens is added to every length (for a verify window appended after this call).
+
+        For a batch packed by the previous call (same seq_ids, same device) only the page-
+        table entries changed since then travel: the tables are kept on the device and one
+        refresh launch applies the (column, block) changes and writes the packed table, so a
+        decode step uploads the lengths plus about one entry per block_size steps per
+        sequence instead of the whole [B, P] table (core/paged_cache.py:207-213 builds a new
+        tensor per sequence per call).  Page tables must change through this class (appends,
+        rollbacks, truncations), which records the lowest changed index; a table whose list
+        object was replaced from outside is recognised by the list's identity and re-sent
+        whole.
         """
         tables = [self._table(s) for s in seq_ids]
+        b = len(tables)
         lens = [t.length + extra_tokens for t in tables]
-        width = max([len(t.blocks) for t in tables] + [1])
+        nblk = [len(t.blocks) for t in tables]
+        width = max(nblk + [1])
         if pad_pages is not None:
             if pad_pages < width:
                 raise ValueError("pad_pages is narrower than the widest page table")
             width = pad_pages
-        b = len(tables)
-        # Page tables change only at their tail (a block appended every block_size tokens,
-        # tail blocks freed on truncation), so a row is rebuilt only when its list object,
-        # length or last block differs from the previous call's.
-        sigs = [(id(t.blocks), len(t.blocks), t.blocks[-1] if t.blocks else -1) for t in tables]
+        dev = self.device if device is None else torch.device(device)
         key = tuple(seq_ids)
-        cached = self._meta_cache
-        if cached is not None and cached[0] == key and width <= cached[1]:
-            host, old = cached[2], cached[3]
-            for i, t in enumerate(tables):
-                if sigs[i] != old[i]:
-                    host[i, :] = 0
-                    host[i, :len(t.blocks)] = t.blocks
-        else:
+        ids = [id(t.blocks) for t in tables]
+        c = self._meta_cache
+        dense = c is None or c.key != key or width > c.cap or c.device != dev
+        if dense:
             cap = (width + 63) // 64 * 64  # room to grow without a rebuild
             host = np.zeros((b, cap), dtype=np.int32)
             for i, t in enumerate(tables):
-                host[i, :len(t.blocks)] = t.blocks
-        self._meta_cache = (key, host.shape[1], host, sigs)
-        # one upload: the [b, width] tables, then the lengths
-        flat = np.concatenate([host[:, :width].reshape(-1), np.asarray(lens, dtype=np.int32)])
-        dev = self.device if device is None else torch.device(device)
-        packed = self._stage_i32.upload(flat, dev) if dev.type == "cuda" else torch.from_numpy(flat)
-        bt = packed[: b * width].view(b, width)
-        cl = packed[b * width:]
-        return bt, cl, max(lens + [0])
+                host[i, :nblk[i]] = t.blocks
+            master = torch.empty((b, cap), dtype=torch.int32, device=dev) if dev.type == "cuda" else None
+            flat = np.concatenate([np.asarray(lens, dtype=np.int32), host.reshape(-1)])
+            for t in tables:
+                t.dirty_from = _CLEAN
+        else:
+            cap, host, master = c.cap, c.host, c.master
+            # rows to send: those changed through this class since the last call, and those
+            # whose list object was replaced from outside (whole row)
+            starts = {i: t.dirty_from for i, t in enumerate(tables) if t.dirty_from != _CLEAN}
+            if ids != c.ids:
+                for i in range(b):
+                    if ids[i] != c.ids[i]:
+                        starts[i] = 0
+            counts = np.zeros(b + 1, dtype=np.int32)
+            pairs: list[int] = []
+            for i in sorted(starts):
+                start, old, n = starts[i], c.nblk[i], nblk[i]
+                blocks = tables[i].blocks
+                for col in range(start, n):
+                    pairs.append(col)
+                    pairs.append(blocks[col])
+                for col in range(max(n, start), old):
+                    pairs.append(col)
+                    pairs.append(0)
+                if start < n:
+                    host[i, start:n] = blocks[start:n]
+                if n < old:
+                    host[i, n:old] = 0
+                counts[i + 1] = len(pairs) // 2
+                tables[i].dirty_from = _CLEAN
+            row_ptr = np.maximum.accumulate(counts)  # entries of rows before each row
+            flat = np.concatenate([np.asarray(lens, dtype=np.int32), row_ptr,
+                                   np.asarray(pairs, dtype=np.int32)])
+        self._meta_cache = _MetaCache(key, cap, host, nblk, ids, master, dev)
+        mx = max(lens + [0])
+        if dev.type != "cuda":
+            return torch.from_numpy(host[:, :width].copy()), torch.tensor(lens, dtype=torch.int32), mx
+        packed = self._stage_i32.upload(flat, dev)
+        cl = packed[:b]
+        bt = torch.empty((b, width), dtype=torch.int32, device=dev)
+        if b:
+            if dense:
+                rp, upd = None, packed[b:]
+            else:
+                rp, upd = packed[b:2 * b + 1], packed[2 * b + 1:]
+            upd_ptr = upd.data_ptr() if upd.numel() else packed.data_ptr()
+            lib = _lib.load()
+            st = lib.inferd_block_tables_refresh(master.data_ptr(), cap, _lib.ptr(rp), upd_ptr,
+                                                 1 if dense else 0, b, width, bt.data_ptr(),
+                                                 _lib.stream_of(dev))
+            _lib.check(st, "block_tables_refresh")
+        return bt, cl, mx
 
     def sequence_length(self, seq_id: int) -> int:
         return self._table(seq_id).length

@@ -202,3 +202,38 @@ def test_hybrid_cache_roundtrip(cuda_device):
     for layer in [0, 2]:
         assert torch.equal(rt.conv_states[layer], fake.conv_states[layer])
         assert torch.equal(rt.recurrent_states[layer], fake.recurrent_states[layer])
+
+
+def test_decode_metadata_device_refresh_matches_rebuild(cuda_device):
+    # the device-resident tables are refreshed with sparse (column, block) updates; after
+    # appends, block-crossing growth, multi-sequence rollbacks, a replaced list and batch
+    # reorders they must equal tables rebuilt from the host page tables
+    cache = PagedKVCache(num_layers=1, num_blocks=600, block_size=4, num_kv_heads=1, head_dim=8,
+                         dtype=torch.bfloat16, device=cuda_device)
+    rng = np.random.default_rng(5)
+    ids = list(range(7))
+    for s in ids:
+        cache.create_sequence(s)
+        n = int(rng.integers(1, 40))
+        kv = torch.zeros(n, 1, 8, dtype=torch.bfloat16, device=cuda_device)
+        cache.append_tokens(s, [kv], [kv])
+    for step in range(150):
+        per = 1 if step % 5 else 3
+        kv = torch.zeros(len(ids) * per, 1, 8, dtype=torch.bfloat16, device=cuda_device)
+        cache.append_tokens_batched(ids, [kv], [kv])
+        for s in ids:
+            if rng.random() < 0.2:
+                cache.truncate_sequence(s, int(rng.integers(0, cache.sequence_length(s) + 1)))
+        if step == 60:
+            cache.sequences[3].blocks = list(cache.sequences[3].blocks)
+        if step == 90:  # a long sequence: the table outgrows the cached capacity
+            kv = torch.zeros(400, 1, 8, dtype=torch.bfloat16, device=cuda_device)
+            cache.append_tokens(2, [kv], [kv])
+        order = ids if step % 13 else ids[::-1]
+        bt, cl, mx = cache.decode_metadata(order, extra_tokens=step % 3)
+        width = max(len(cache.sequences[s].blocks) for s in order)
+        rows = [cache.sequences[s].blocks + [0] * (width - len(cache.sequences[s].blocks)) for s in order]
+        assert bt.is_cuda and bt.dtype == torch.int32 and bt.shape == (len(order), width)
+        assert bt.cpu().tolist() == rows, f"step {step}"
+        assert cl.cpu().tolist() == [cache.sequence_length(s) + step % 3 for s in order]
+        assert mx == max(cl.cpu().tolist())

@@ -225,3 +225,30 @@ def test_decode_metadata_incremental_rows_match_rebuild():
         bt, cl, mx = cache.decode_metadata(order)
         rows, lens = rebuilt(order)
         assert bt.tolist() == rows and cl.tolist() == lens and mx == max(lens)
+
+
+def test_decode_metadata_sparse_updates_after_rollbacks_across_sequences():
+    # rollbacks of several sequences, then re-growth, hand freed blocks between sequences
+    # (LIFO): rows whose last block is unchanged but whose middle moved must still be right
+    cache = RecordingCache(num_layers=1, num_blocks=64, block_size=2, num_kv_heads=1, head_dim=1,
+                           dtype=torch.float32)
+    ids = [0, 1, 2]
+    for s, n in zip(ids, (7, 5, 9)):
+        cache.create_sequence(s)
+        cache.append_tokens(s, [torch.zeros(n, 1, 1)], [torch.zeros(n, 1, 1)])
+    rng = np.random.default_rng(11)
+    for step in range(200):
+        for s in ids:
+            if rng.random() < 0.4:
+                cache.truncate_sequence(s, int(rng.integers(0, cache.sequence_length(s) + 1)))
+        per = int(rng.integers(1, 4))
+        cache.append_tokens_batched(ids, [torch.zeros(3 * per, 1, 1)], [torch.zeros(3 * per, 1, 1)])
+        if step % 23 == 7:  # a table replaced from outside the class
+            t = cache.sequences[1]
+            t.blocks = list(t.blocks)
+        bt, cl, mx = cache.decode_metadata(ids, extra_tokens=step % 2)
+        width = max(len(cache.sequences[s].blocks) for s in ids)
+        rows = [cache.sequences[s].blocks + [0] * (width - len(cache.sequences[s].blocks)) for s in ids]
+        assert bt.tolist() == rows
+        assert cl.tolist() == [cache.sequence_length(s) + step % 2 for s in ids]
+    cache.assert_consistent()
