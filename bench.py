@@ -351,22 +351,29 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
         used.update(t.blocks)
     cache.allocator._allocated = set(used)
     cache.allocator._free = [x for x in cache.allocator._free if x not in used]
-    q_h = dwl.q.cpu().pin_memory()
-    k_h = dwl.k_new.cpu().pin_memory()
-    v_h = dwl.v_new.cpu().pin_memory()
+    # the step's inputs (queries and the new K/V) sit in one pinned buffer and cross to the
+    # device in one copy, as an engine stages a step's host-produced tensors
+    parts = [dwl.q, dwl.k_new, dwl.v_new]
+    sizes = [t.numel() for t in parts]
+    inp_h = torch.empty(sum(sizes), dtype=torch.bfloat16).pin_memory()
+    inp_d = torch.empty(sum(sizes), dtype=torch.bfloat16, device=device)
+    off = 0
+    views_d = []
+    for t, n in zip(parts, sizes):
+        inp_h[off:off + n].copy_(t.reshape(-1).cpu())
+        views_d.append(inp_d[off:off + n].view(t.shape))
+        off += n
     out_rows = dwl.b * world
     out_h = torch.empty((out_rows, ql, HQ, D), dtype=torch.bfloat16).pin_memory()
     gathered = torch.empty((out_rows, ql, HQ, D), dtype=torch.bfloat16, device=device)
     stream = torch.cuda.current_stream(device)
     steps = max(1, min(args.steps, args.e2e_steps))
     h2d = d2h = 0
-    total_bytes = 0.0
 
     def one_step():
-        nonlocal h2d, d2h, total_bytes
-        q = q_h.to(device, non_blocking=True)
-        k = k_h.to(device, non_blocking=True)
-        v = v_h.to(device, non_blocking=True)
+        nonlocal h2d, d2h
+        inp_d.copy_(inp_h, non_blocking=True)
+        q, k, v = views_d
         cache.append_tokens_batched(ids, [k], [v])
         bt, cl, mx = cache.decode_metadata(ids)
         out = paged_attention_batched(q, cache.key_cache[0], cache.value_cache[0], bt, cl,
@@ -378,18 +385,17 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
             res = out
         out_h[: res.shape[0]].copy_(res, non_blocking=True)
         stream.synchronize()
-        ctx = [cache.sequence_length(i) for i in ids]
-        total_bytes += step_bytes(ctx, ql)["total"]
         if ql > 1:
             # speculative verify: keep one accepted token, roll the rest of the window back
-            for i, n in zip(ids, ctx):
-                cache.truncate_sequence(i, n - ql + 1)
-        h2d = (q.numel() + k.numel() + v.numel()) * ELEM + dwl.b * ql * 8 \
-            + bt.numel() * 4 + cl.numel() * 4
+            for i in ids:
+                cache.truncate_sequence(i, cache.sequence_length(i) - ql + 1)
         d2h = res.numel() * ELEM
 
     one_step()  # warm the path (pinned staging, workspace)
-    total_bytes = 0.0
+    # every step grows each context by one token net, so the bytes of the timed steps are
+    # known up front: step s attends over base + s + q_len keys per sequence
+    base = np.asarray([cache.sequence_length(i) for i in ids], dtype=np.int64)
+    meta0 = cache.uploaded_bytes()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
@@ -400,6 +406,12 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
     e1.record(stream)
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1)
+    if [cache.sequence_length(i) for i in ids] != (base + steps).tolist():
+        raise RuntimeError("context lengths after the timed steps differ from the byte count's")
+    total_bytes = float(sum(step_bytes(base + s + ql, ql)["total"] for s in range(steps)))
+    # the inputs' one copy, plus what the cache uploaded (slot mappings, sparse table updates
+    # and lengths), averaged over the timed steps
+    h2d = inp_h.numel() * ELEM + (cache.uploaded_bytes() - meta0) / steps
     t = torch.tensor([ms, total_bytes], dtype=torch.float64, device=device)
     if world > 1:
         mx = t.clone()
@@ -408,7 +420,7 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         ms, total_bytes = float(mx[0]), float(sm[1])
     return {"value": round(total_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "h2d_bytes_per_step": int(round(h2d)), "d2h_bytes_per_step": int(d2h),
             "steps": steps, "ms_per_step": round(ms / steps, 5),
             "note": "contexts grow by one token per step (verify: the window is appended, "
                     "verified, and all but one token rolled back); bytes counted per step"}

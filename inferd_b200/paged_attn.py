@@ -212,6 +212,9 @@ def paged_attention(
     return out.reshape(query.shape)
 
 
+_WS_BYTES: dict[tuple, int] = {}  # workspace size per launch shape (a pure function of it)
+
+
 def paged_attention_batched(
     query: torch.Tensor,
     key_cache: torch.Tensor,
@@ -265,8 +268,14 @@ def paged_attention_batched(
     kc, vc = _contig(key_cache), _contig(value_cache)
     bt = block_tables if block_tables.stride(1) == 1 else block_tables.contiguous()
     lib = _lib.load()
-    ws_bytes = lib.inferd_paged_attention_workspace_bytes(
-        b, q_len, q_heads, kv_heads, head_dim, dev.index if dev.index is not None else 0)
+    dev_index = dev.index if dev.index is not None else 0
+    ws_key = (b, q_len, q_heads, kv_heads, head_dim, dev_index)
+    ws_bytes = _WS_BYTES.get(ws_key)
+    if ws_bytes is None:
+        ws_bytes = lib.inferd_paged_attention_workspace_bytes(b, q_len, q_heads, kv_heads, head_dim, dev_index)
+        if len(_WS_BYTES) > 256:
+            _WS_BYTES.clear()
+        _WS_BYTES[ws_key] = ws_bytes
     ws = _lib.workspace(dev, ws_bytes)
     st = lib.inferd_paged_attention(
         out.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(),

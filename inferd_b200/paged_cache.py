@@ -132,7 +132,9 @@ class _PinnedStaging:
         self.dtype = dtype
         self._bufs: list[torch.Tensor | None] = [None, None]
         self._events: list[torch.cuda.Event | None] = [None, None]
+        self._recorded = [False, False]
         self._next = 0
+        self.bytes_uploaded = 0
 
     def upload(self, arr: np.ndarray, device: torch.device) -> torch.Tensor:
         i = self._next
@@ -143,13 +145,15 @@ class _PinnedStaging:
             buf = torch.empty(max(n, 2 * (0 if buf is None else buf.numel()), 1024),
                               dtype=self.dtype, pin_memory=True)
             self._bufs[i] = buf
-        elif self._events[i] is not None:
+        elif self._recorded[i]:
             self._events[i].synchronize()
         buf[:n].numpy()[...] = arr.reshape(-1)
         out = buf[:n].to(device, non_blocking=True)
-        ev = torch.cuda.Event()
-        ev.record(torch.cuda.current_stream(device))
-        self._events[i] = ev
+        self.bytes_uploaded += n * buf.element_size()
+        if self._events[i] is None:
+            self._events[i] = torch.cuda.Event()
+        self._events[i].record(torch.cuda.current_stream(device))
+        self._recorded[i] = True
         return out
 
 
@@ -459,6 +463,11 @@ class PagedKVCache:
                                                  _lib.stream_of(dev))
             _lib.check(st, "block_tables_refresh")
         return bt, cl, mx
+
+    def uploaded_bytes(self) -> int:
+        """Host-to-device bytes this cache has copied so far (slot mappings and decode
+        metadata), for end-to-end accounting."""
+        return self._stage_i32.bytes_uploaded + self._stage_i64.bytes_uploaded
 
     def sequence_length(self, seq_id: int) -> int:
         return self._table(seq_id).length
