@@ -328,8 +328,11 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
 
 def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.device) -> dict:
     """Same step through the public API with pinned host inputs and a host read of the
-    result every step: PagedKVCache.append_tokens_batched -> decode_metadata ->
-    paged_attention_batched -> (all-gather) -> device-to-host copy."""
+    result every step: one host-to-device copy of the step's inputs ->
+    PagedKVCache.commit_append (the K/V write of a plan_append plan: pages, slots, attention
+    metadata) -> paged_attention_batched -> (all-gather) -> device-to-host copy -> sync.
+    Decode plans step N + 1 between step N's launches and its sync, as an engine that
+    schedules ahead does; verify plans after its rollback."""
     import torch.distributed as dist
 
     from inferd_b200.paged_attn import paged_attention_batched
@@ -369,26 +372,34 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
     stream = torch.cuda.current_stream(device)
     steps = max(1, min(args.steps, args.e2e_steps))
     h2d = d2h = 0
+    plan = None
 
     def one_step():
-        nonlocal h2d, d2h
+        # plan_append reserves the step's pages, uploads its slots and builds the attention
+        # metadata; commit_append writes the K/V.  Decode plans the next step while this
+        # step's attention runs (pages depend only on lengths); verify plans after its
+        # rollback, which needs the step's result.
+        nonlocal d2h, plan
         inp_d.copy_(inp_h, non_blocking=True)
         q, k, v = views_d
-        cache.append_tokens_batched(ids, [k], [v])
-        bt, cl, mx = cache.decode_metadata(ids)
-        out = paged_attention_batched(q, cache.key_cache[0], cache.value_cache[0], bt, cl,
-                                      max_context_len=mx)
+        if plan is None:
+            plan = cache.plan_append(ids, ql)
+        cur, plan = plan, None
+        cache.commit_append(cur, [k], [v])
+        out = paged_attention_batched(q, cache.key_cache[0], cache.value_cache[0], cur.block_tables,
+                                      cur.context_lens, max_context_len=cur.max_context_len)
         if world > 1:
             gather_outputs(out, out=gathered)
             res = gathered
         else:
             res = out
         out_h[: res.shape[0]].copy_(res, non_blocking=True)
+        if ql == 1:
+            plan = cache.plan_append(ids, ql)
         stream.synchronize()
         if ql > 1:
             # speculative verify: keep one accepted token, roll the rest of the window back
-            for i in ids:
-                cache.truncate_sequence(i, cache.sequence_length(i) - ql + 1)
+            cache.truncate_batched(ids, [cache.sequence_length(i) - ql + 1 for i in ids])
         d2h = res.numel() * ELEM
 
     one_step()  # warm the path (pinned staging, workspace)
@@ -406,6 +417,8 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
     e1.record(stream)
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1)
+    if plan is not None:
+        cache.abort_append(plan)  # the plan made for a step that does not run
     if [cache.sequence_length(i) for i in ids] != (base + steps).tolist():
         raise RuntimeError("context lengths after the timed steps differ from the byte count's")
     total_bytes = float(sum(step_bytes(base + s + ql, ql)["total"] for s in range(steps)))
@@ -423,7 +436,8 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
             "h2d_bytes_per_step": int(round(h2d)), "d2h_bytes_per_step": int(d2h),
             "steps": steps, "ms_per_step": round(ms / steps, 5),
             "note": "contexts grow by one token per step (verify: the window is appended, "
-                    "verified, and all but one token rolled back); bytes counted per step"}
+                    "verified, and all but one token rolled back); bytes counted per step; "
+                    "decode plans the next step's pages while the current step runs"}
 
 
 # ------------------------------------------------------------------ FP8 linear (config 4)

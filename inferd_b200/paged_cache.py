@@ -121,6 +121,23 @@ class _MetaCache:
         self.master, self.device = master, device
 
 
+@dataclass
+class AppendPlan:
+    """Pages reserved, slots and attention metadata for an append not yet written
+    (PagedKVCache.plan_append).  block_tables / context_lens / max_context_len describe the
+    sequences as they will be once the append is committed."""
+
+    seq_ids: list[int]
+    tokens_per_seq: int
+    slots: torch.Tensor
+    block_tables: torch.Tensor
+    context_lens: torch.Tensor
+    max_context_len: int
+    _tables: list = field(repr=False, default_factory=list)
+    _reserved: list = field(repr=False, default_factory=list)
+    _open: bool = field(repr=False, default=True)
+
+
 class _PinnedStaging:
     """Two reusable pinned host buffers for the small per-step uploads (slots, block tables).
 
@@ -233,6 +250,29 @@ class PagedKVCache:
         table.length = length
         return freed
 
+    def truncate_batched(self, seq_ids: list[int], lengths: list[int]) -> list[int]:
+        """truncate_sequence for several sequences (the rollback of a batched verify step);
+        all lengths are checked before any table changes.  Returns every freed block."""
+        if len(seq_ids) != len(lengths):
+            raise ValueError("one length per sequence")
+        tables = [self._table(s) for s in seq_ids]
+        for t, n in zip(tables, lengths):
+            if n < 0 or n > t.length:
+                raise ValueError(f"cannot truncate a sequence of length {t.length} to {n}")
+        bs = self.block_size
+        freed_all: list[int] = []
+        for t, n in zip(tables, lengths):
+            keep = (n + bs - 1) // bs
+            if keep < len(t.blocks):
+                freed = t.blocks[keep:]
+                del t.blocks[keep:]
+                self.allocator.free(freed)
+                freed_all.extend(freed)
+                if keep < t.dirty_from:
+                    t.dirty_from = keep
+            t.length = n
+        return freed_all
+
     def _reserve(self, table: SequencePageTable, n_tokens: int) -> list[int]:
         """Extend a page table to hold n_tokens more tokens (core/paged_cache.py:170-176)."""
         needed_capacity = table.length + n_tokens
@@ -316,6 +356,18 @@ class PagedKVCache:
                     if page >= len(t.blocks):
                         reserved.append((t, self._reserve(t, 1)))
                     slot_list.append(t.blocks[page] * bs + pos - page * bs)
+            elif per <= bs:
+                # a short window (speculative verify): its tokens span at most two pages
+                for t in tables:
+                    pos = t.length
+                    last = pos + per - 1
+                    if last // bs >= len(t.blocks):
+                        reserved.append((t, self._reserve(t, per)))
+                    blocks = t.blocks
+                    p0, p1 = pos // bs, last // bs
+                    b0, b1 = blocks[p0] * bs - p0 * bs, blocks[p1] * bs - p1 * bs
+                    split = (p0 + 1) * bs  # first position on page p1 when p1 > p0
+                    slot_list.extend([(b0 if q < split else b1) + q for q in range(pos, pos + per)])
             else:
                 for t in tables:
                     reserved.append((t, self._reserve(t, per)))
@@ -330,6 +382,74 @@ class PagedKVCache:
             for t, nb in reversed(reserved):
                 self._rollback(t, nb)
             raise
+
+    # ------------------------------------------------------------ planned appends
+    def plan_append(self, seq_ids: list[int], tokens_per_seq: int) -> AppendPlan:
+        """Reserve the pages for tokens_per_seq new tokens of every sequence, upload their
+        slots and build the attention metadata of the state after the append -- everything
+        but the K/V write, which commit_append does once the tokens exist.
+
+        A decode engine plans step N + 1 while step N runs on the GPU: the pages and slots
+        depend only on the lengths.  Until the plan is committed or aborted, these
+        sequences must not change otherwise.  Reservation is all-or-nothing (MemoryError
+        leaves the cache unchanged), as in append_tokens."""
+        if len(set(seq_ids)) != len(seq_ids):
+            raise ValueError("duplicate sequence in batched append")
+        per = int(tokens_per_seq)
+        if per <= 0:
+            raise ValueError("tokens_per_seq must be positive")
+        tables = [self._table(s) for s in seq_ids]
+        bs = self.block_size
+        reserved: list[tuple[SequencePageTable, list[int]]] = []
+        slot_list: list[int] = []
+        try:
+            for t in tables:
+                pos = t.length
+                last = pos + per - 1
+                if last // bs >= len(t.blocks):
+                    reserved.append((t, self._reserve(t, per)))
+                blocks = t.blocks
+                if per == 1:
+                    page = pos // bs
+                    slot_list.append(blocks[page] * bs + pos - page * bs)
+                else:
+                    slot_list.extend(blocks[q // bs] * bs + q % bs for q in range(pos, pos + per))
+        except Exception:
+            for t, nb in reversed(reserved):
+                self._rollback(t, nb)
+            raise
+        slots = self._slot_tensor(slot_list)
+        bt, cl, mx = self.decode_metadata(seq_ids, extra_tokens=per)
+        return AppendPlan(list(seq_ids), per, slots, bt, cl, mx, tables, reserved)
+
+    def commit_append(self, plan: AppendPlan, layer_keys: list[torch.Tensor],
+                      layer_values: list[torch.Tensor]) -> None:
+        """Write the planned tokens (layer_keys[layer]: [len(seq_ids) * tokens_per_seq,
+        num_kv_heads, head_dim], seq_ids[0]'s tokens first) and advance the lengths.  On a
+        failure the plan's pages are released (abort_append) and the error re-raised."""
+        if not plan._open:
+            raise ValueError("this plan was already committed or aborted")
+        try:
+            self._validate_layers(layer_keys, layer_values)
+            if int(layer_keys[0].shape[0]) != len(plan.seq_ids) * plan.tokens_per_seq:
+                raise ValueError("token count differs from the plan's")
+            for layer in range(self.num_layers):
+                self._write(layer, layer_keys[layer], layer_values[layer], plan.slots)
+        except Exception:
+            self.abort_append(plan)
+            raise
+        per = plan.tokens_per_seq
+        for t in plan._tables:
+            t.length += per
+        plan._open = False
+
+    def abort_append(self, plan: AppendPlan) -> None:
+        """Release the pages an uncommitted plan reserved."""
+        if not plan._open:
+            return
+        for t, nb in reversed(plan._reserved):
+            self._rollback(t, nb)
+        plan._open = False
 
     def _slot_tensor(self, slots: list[int]) -> torch.Tensor:
         arr = np.asarray(slots, dtype=np.int64)

@@ -158,8 +158,7 @@ class PagedRuntimeCache(DynamicCache):
             self._conv[k][:n].copy_(v)
         for k, v in snap["rec"].items():
             self._rec[k][:n].copy_(v)
-        for s, length in zip(self.rows, lengths if lengths is not None else snap["lengths"]):
-            self.pool.truncate_sequence(s, length)
+        self.pool.truncate_batched(self.rows, lengths if lengths is not None else snap["lengths"])
         self._use_rows()
 
     def position_ids(self) -> torch.Tensor:

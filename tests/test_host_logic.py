@@ -252,3 +252,72 @@ def test_decode_metadata_sparse_updates_after_rollbacks_across_sequences():
         assert bt.tolist() == rows
         assert cl.tolist() == [cache.sequence_length(s) + step % 2 for s in ids]
     cache.assert_consistent()
+
+
+def test_truncate_batched_matches_per_sequence_truncation():
+    rng = np.random.default_rng(2)
+    a = RecordingCache(num_layers=1, num_blocks=300, block_size=4, num_kv_heads=1, head_dim=1,
+                       dtype=torch.float32)
+    b = RecordingCache(num_layers=1, num_blocks=300, block_size=4, num_kv_heads=1, head_dim=1,
+                       dtype=torch.float32)
+    ids = [3, 1, 4, 0]
+    for cache in (a, b):
+        for s in ids:
+            cache.create_sequence(s)
+    for step in range(60):
+        per = int(rng.integers(1, 7))
+        for cache in (a, b):
+            cache.append_tokens_batched(ids, [torch.zeros(4 * per, 1, 1)], [torch.zeros(4 * per, 1, 1)])
+        lens = [int(rng.integers(0, a.sequence_length(s) + 1)) for s in ids]
+        freed = a.truncate_batched(ids, lens)
+        freed_ref = []
+        for s, n in zip(ids, lens):
+            freed_ref += b.truncate_sequence(s, n)
+        assert freed == freed_ref
+        assert [a.sequences[s].blocks for s in ids] == [b.sequences[s].blocks for s in ids]
+        assert a.allocator._free == b.allocator._free
+    with pytest.raises(ValueError):  # checked before any table changes
+        a.truncate_batched(ids, [0, 0, 0, a.sequence_length(0) + 1])
+    assert [a.sequence_length(s) for s in ids] == [b.sequence_length(s) for s in ids]
+    with pytest.raises(ValueError):
+        a.truncate_batched(ids, [0])
+    a.assert_consistent()
+
+
+def test_plan_and_commit_equal_append_then_metadata():
+    from inferd_b200.paged_cache import AppendPlan  # noqa: F401
+    rng = np.random.default_rng(4)
+    a = RecordingCache(num_layers=2, num_blocks=200, block_size=4, num_kv_heads=1, head_dim=1,
+                       dtype=torch.float32)
+    b = RecordingCache(num_layers=2, num_blocks=200, block_size=4, num_kv_heads=1, head_dim=1,
+                       dtype=torch.float32)
+    ids = [5, 2, 9]
+    for cache in (a, b):
+        for s in ids:
+            cache.create_sequence(s)
+    for step in range(40):
+        per = int(rng.integers(1, 6))
+        kv = [torch.zeros(3 * per, 1, 1)] * 2
+        plan = a.plan_append(ids, per)
+        a.commit_append(plan, kv, kv)
+        b.append_tokens_batched(ids, kv, kv)
+        bt, cl, mx = b.decode_metadata(ids)
+        assert plan.block_tables.tolist() == bt.tolist() and plan.context_lens.tolist() == cl.tolist()
+        assert plan.max_context_len == mx and a.writes[-1] == b.writes[-1]
+        assert [a.sequences[s].blocks for s in ids] == [b.sequences[s].blocks for s in ids]
+        with pytest.raises(ValueError):
+            a.commit_append(plan, kv, kv)
+    # abort releases the reservation; a failed commit aborts
+    free = a.allocator.free_count
+    plan = a.plan_append(ids, 9)
+    assert a.allocator.free_count < free
+    a.abort_append(plan)
+    assert a.allocator.free_count == free and [a.sequence_length(s) for s in ids] == [b.sequence_length(s) for s in ids]
+    plan = a.plan_append(ids, 2)
+    with pytest.raises(ValueError):
+        a.commit_append(plan, [torch.zeros(5, 1, 1)] * 2, [torch.zeros(5, 1, 1)] * 2)
+    assert a.allocator.free_count == free
+    with pytest.raises(MemoryError):
+        a.plan_append(ids, 10_000)
+    assert a.allocator.free_count == free
+    a.assert_consistent()
