@@ -303,6 +303,11 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
   const uint32_t ncols = fp8_tmem_cols(T, p.planes);
 
   if (tid == 0) {
+    // descriptor fetches overlap the set-up below
+    prefetch_tensormap(&wmap);
+    prefetch_tensormap(&hmap);
+    if (p.planes == 2) prefetch_tensormap(&lmap);
+    if (p.y_tma) prefetch_tensormap(&ymap);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -327,9 +332,6 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer (both CTAs)
-      prefetch_tensormap(&wmap);
-      prefetch_tensormap(&hmap);
-      prefetch_tensormap(&lmap);
       const uint64_t pol_w = l2_policy_evict_first();
       uint64_t pol_x;
       asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_x));
@@ -374,6 +376,9 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
         load_w(st, g0 + j, full_of(s));
         load_x(st, g0 + j, full_of(s));
       }
+      // every load of this CTA is issued: the next call's first kernel may launch (it
+      // waits for this grid to finish before it touches anything this grid reads)
+      grid_launch_dependents();
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -450,7 +455,6 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
     __nv_bfloat16* ystage = reinterpret_cast<__nv_bfloat16*>(smem + S * stage_bytes) + (warp - 2) * 4 * kEpiBlockElems;
     float* xsm = reinterpret_cast<float*>(smem + S * stage_bytes + 4 * 4 * kEpiBlockElems * 2);
     int ychunk = 0;  // store groups committed by this warp
-    if (lane == 0 && p.y_tma) prefetch_tensormap(&ymap);
     grid_dependency_wait();  // x_scale comes from the split grid
     for (int i = ep; i < T; i += 128) xsm[i] = p.tok0 + i < p.m ? __ldg(p.x_scale + p.tok0 + i) : 0.f;
     named_barrier_sync(1, 128);
@@ -649,6 +653,10 @@ __global__ void __launch_bounds__(kSplitThreads) split_activations_kernel(const 
                                                                          uint8_t* __restrict__ h, uint8_t* __restrict__ l,
                                                                          float* __restrict__ x_scale) {
   __shared__ float red[kSplitThreads / 32];
+  // Launched early (programmatic dependent launch): x and the workspace planes may belong
+  // to the previous grid until it completes.  Only then may the GEMM launch, so its early
+  // weight loads also see every write made before this call.
+  grid_dependency_wait();
   grid_launch_dependents();
   const int m = blockIdx.x;
   const __nv_bfloat16* row = x + static_cast<int64_t>(m) * k;
@@ -788,6 +796,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) row_absmax_kernel(const T* __restrict__ x, int64_t k,
                                                          float* __restrict__ row_amax) {
   __shared__ float red[8];
+  grid_dependency_wait();  // first kernel of a call: as split_activations_kernel
   grid_launch_dependents();
   const float a = row_absmax(x + static_cast<int64_t>(blockIdx.x) * k, k, red);
   if (threadIdx.x == 0) row_amax[blockIdx.x] = a;
@@ -801,6 +810,9 @@ __global__ void __launch_bounds__(256) quantize_dynamic_kernel(const T* __restri
                                                                const float* __restrict__ row_amax,
                                                                uint8_t* __restrict__ q, float* __restrict__ scale) {
   __shared__ float red[8];
+  // per tensor: second kernel, its primary is row_absmax_kernel; per row: the call's first
+  // kernel, so it waits for the previous grid before letting the GEMM launch
+  if (!kPerTensor) grid_dependency_wait();
   grid_launch_dependents();
   const int64_t r = blockIdx.x;
   const T* row = x + r * k;
@@ -1178,14 +1190,16 @@ static int fp8_linear_impl(void* y, const void* x, const void* w_e4m3, const flo
   }
 
   const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  // every kernel of the call is a programmatic dependent launch; see the kernels' waits
   if (act_mode == kActSplit) {
-    split_activations_kernel<<<static_cast<unsigned>(m), kSplitThreads, 0, s>>>(xb, static_cast<int>(k), h, l, xs);
+    st = launch_pdl(dim3(static_cast<unsigned>(m)), dim3(kSplitThreads), s, split_activations_kernel, xb,
+                    static_cast<int>(k), h, l, xs);
   } else if (act_mode == kActDynRow) {
-    quantize_dynamic_kernel<__nv_bfloat16, false><<<static_cast<unsigned>(m), 256, 0, s>>>(xb, m, k, nullptr, h, xs);
+    st = launch_pdl(dim3(static_cast<unsigned>(m)), dim3(256), s, quantize_dynamic_kernel<__nv_bfloat16, false>, xb,
+                    m, k, static_cast<const float*>(nullptr), h, xs);
   } else {
     float* row_amax = reinterpret_cast<float*>(l);
-    row_absmax_kernel<__nv_bfloat16><<<static_cast<unsigned>(m), 256, 0, s>>>(xb, k, row_amax);
-    st = launch_status();
+    st = launch_pdl(dim3(static_cast<unsigned>(m)), dim3(256), s, row_absmax_kernel<__nv_bfloat16>, xb, k, row_amax);
     if (st != INFERD_OK) return st;
     st = launch_pdl(dim3(static_cast<unsigned>(m)), dim3(256), s, quantize_dynamic_kernel<__nv_bfloat16, true>, xb,
                     m, k, static_cast<const float*>(row_amax), h, xs);
