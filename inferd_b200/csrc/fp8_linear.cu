@@ -336,14 +336,16 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
       uint64_t pol_x;
       asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_x));
       const int x_row = merged ? p.tok0 : p.tok0 + static_cast<int>(rank) * (T / 2);
-      auto load_w = [&](uint8_t* st, int64_t g, uint32_t bar) {
-        const int tp = static_cast<int>(g / KS), ks = static_cast<int>(g - static_cast<int64_t>(tp) * KS);
+      // Work unit g0 + j is (tile pair tp, K step ks); both advance with the loop, so no
+      // unit pays for a 64-bit division.
+      const int tp0 = static_cast<int>(g0 / KS);
+      const int ks0 = static_cast<int>(g0 - static_cast<int64_t>(tp0) * KS);
+      auto load_w = [&](uint8_t* st, int tp, int ks, uint32_t bar) {
         const int t = 2 * tp + static_cast<int>(rank);
         if (p.w_packed) tma_load_2d_pair(st, &wmap, 0, (t * KS + ks) * kTileN, bar, pol_w);
         else tma_load_2d_pair(st, &wmap, ks * kTileK, t * kTileN, bar, pol_w);
       };
-      auto load_x = [&](uint8_t* st, int64_t g, uint32_t bar) {
-        const int ks = static_cast<int>(g % KS);
+      auto load_x = [&](uint8_t* st, int ks, uint32_t bar) {
         if (merged) {
           tma_load_2d_pair(st + w_bytes, leader ? &hmap : &lmap, ks * kTileK, x_row, bar, pol_x);
         } else if (two) {
@@ -357,24 +359,35 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
       // The weight tiles of the first ring do not depend on the activation split: issue
       // them before waiting for it.
       const int first = n_units < S ? n_units : S;
+      int tp = tp0, ks = ks0;
       for (int j = 0; j < first; ++j) {
         if (leader) mbar_arrive_expect_tx(&full[j], 2 * stage_bytes);
-        load_w(smem + j * stage_bytes, g0 + j, full_of(j));
+        load_w(smem + j * stage_bytes, tp, ks, full_of(j));
+        if (++ks == KS) { ks = 0; ++tp; }
       }
       grid_dependency_wait();
-      for (int j = 0; j < first; ++j) load_x(smem + j * stage_bytes, g0 + j, full_of(j));
+      ks = ks0;
+      for (int j = 0; j < first; ++j) {
+        load_x(smem + j * stage_bytes, ks, full_of(j));
+        if (++ks == KS) ks = 0;
+      }
+      // from unit S on: stage s = j % S, refilled once its previous fill (parity
+      // j / S - 1) has been consumed
+      int s = 0;
+      uint32_t par = 0;
       for (int j = first; j < n_units; ++j) {
-        const int s = j % S;
         if (*vabort) break;
-        if (!mbar_wait(&empty[s], ((j / S) - 1) & 1u)) {
+        if (!mbar_wait(&empty[s], par)) {
           report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
           *vabort = 1;
           break;
         }
         uint8_t* st = smem + s * stage_bytes;
         if (leader) mbar_arrive_expect_tx(&full[s], 2 * stage_bytes);
-        load_w(st, g0 + j, full_of(s));
-        load_x(st, g0 + j, full_of(s));
+        load_w(st, tp, ks, full_of(s));
+        load_x(st, ks, full_of(s));
+        if (++ks == KS) { ks = 0; ++tp; }
+        if (++s == S) { s = 0; par ^= 1u; }
       }
       // every load of this CTA is issued: the next call's first kernel may launch (it
       // waits for this grid to finish before it touches anything this grid reads)
@@ -388,9 +401,10 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
       int seg = 0;        // segments started
       int in_seg = 0;     // K steps issued in the current segment
       uint32_t acc = tmem;
+      int ks = static_cast<int>(g0 % KS);  // K step of unit j, advanced with the loop
+      int s = 0;                           // its stage, j % S, and the fill's parity
+      uint32_t par = 0;
       for (int j = 0; j < n_units; ++j) {
-        const int64_t g = g0 + j;
-        const int ks = static_cast<int>(g % KS);
         const bool seg_begin = (j == 0) || (ks == 0);
         const bool seg_end = (j == n_units - 1) || (ks == KS - 1);
         // Waits are done by lane 0 and broadcast, so every branch below is warp-uniform
@@ -413,10 +427,9 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
           in_seg = 0;
           tc_fence_after();
         }
-        const int s = j % S;
         int ok = 0;
         if (lane == 0 && !*vabort) {
-          ok = mbar_wait(&full[s], (j / S) & 1u) ? 1 : 0;
+          ok = mbar_wait(&full[s], par) ? 1 : 0;
           if (!ok) {
             report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
             *vabort = 1;
@@ -443,6 +456,8 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
           __syncwarp();
           ++seg;
         }
+        if (++ks == KS) ks = 0;
+        if (++s == S) { s = 0; par ^= 1u; }
       }
     }
   } else {
