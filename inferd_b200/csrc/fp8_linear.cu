@@ -533,12 +533,22 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
                 if (jj < 16 || wide) v[jj] += __ldcg(src + jj * kTileN);
             }
           }
+          // the chunk's 32 token scales (entries past the tile are never stored)
+          const float4* xs4 = reinterpret_cast<const float4*>(xsm + c0);
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) v[jj] *= sw * xsm[c0 + (jj < 16 || wide ? jj : 0)];
+          for (int i4 = 0; i4 < 8; ++i4) {
+            const float4 f = xs4[i4];
+            v[4 * i4 + 0] *= sw * f.x;
+            v[4 * i4 + 1] *= sw * f.y;
+            v[4 * i4 + 2] *= sw * f.z;
+            v[4 * i4 + 3] *= sw * f.w;
+          }
           const int n0 = t * kTileN + q * 32, m0 = p.tok0 + c0;
           if (p.y_tma) {
             if (n0 < p.n && m0 < p.m) {
-              // blocks [16 tokens][32 rows] of y in shared memory, then TMA stores
+              // a [32 tokens][32 rows] block of y in shared memory, then one TMA store (a
+              // 16-token chunk only occurs at the end of the last launch tile, where the
+              // tensor map clips the block's rows past M)
               __nv_bfloat16* blk = ystage + (ychunk & 1) * 2 * kEpiBlockElems;
               if (lane == 0) bulk_wait_read_le1();  // the group that last read these blocks is done
               __syncwarp();
@@ -549,7 +559,6 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
               __syncwarp();
               if (lane == 0) {
                 tma_store_2d(&ymap, blk, n0, m0);
-                if (wide && m0 + 16 < p.m) tma_store_2d(&ymap, blk + kEpiBlockElems, n0, m0 + 16);
                 bulk_commit_group();
               }
               ++ychunk;
@@ -1179,7 +1188,7 @@ static int fp8_linear_impl(void* y, const void* x, const void* w_e4m3, const flo
   CUtensorMap ymap;
   const bool y_tma = (n * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
   if (y_tma) {
-    st = cached_map(&ymap, MapKey{y, static_cast<uint64_t>(m), static_cast<uint64_t>(n), 32, 16, 2, false,
+    st = cached_map(&ymap, MapKey{y, static_cast<uint64_t>(m), static_cast<uint64_t>(n), 32, 32, 2, false,
                                   current_device()});
     if (st != INFERD_OK) return st;
   } else {
