@@ -1020,22 +1020,31 @@ inline Fp8Plan fp8_plan(int64_t rem_tokens, int64_t n, int64_t k, int sms, int p
   Fp8Plan pl;
   const int64_t t = rem_tokens < kMaxTokTile ? rem_tokens : kMaxTokTile;
   pl.tile = static_cast<int>((t + 15) / 16 * 16);
-  // two CTAs per SM while both double-buffered accumulators fit TMEM's 512 columns
-  pl.per_sm = 2 * fp8_tmem_cols(pl.tile, planes) <= 512 ? 2 : 1;
-  const int budget = pl.per_sm == 2 ? kSmemBudget2 : kSmemBudget;
   const int stage_bytes = kTileN * kTileK + fp8_x_stage_bytes(pl.tile, planes);
-  pl.stages = (budget - kEpiStageBytes) / stage_bytes;
-  if (pl.stages > 8) pl.stages = 8;
   const int64_t pairs = fp8_pairs(n);
   const int64_t work = pairs * ((k + kTileK - 1) / kTileK);
-  int64_t c = static_cast<int64_t>(sms / 2) * pl.per_sm;
-  // at least four K steps per cluster, so small problems are not cut into many pieces
-  const int64_t cap = work / 4 > 0 ? work / 4 : 1;
-  if (c > cap) c = cap;
-  // whole tile pairs per cluster (no partials to merge) when that still keeps three
-  // quarters of the clusters busy
-  if (pairs <= c && 4 * pairs >= 3 * c) c = pairs;
-  pl.clusters = static_cast<int>(c);
+  const int64_t c1 = sms / 2;  // clusters at one CTA per SM
+  if (pairs <= c1 && 4 * pairs >= 3 * c1) {
+    // Whole tile pairs, one per cluster, one CTA per SM with the deepest ring: no partials
+    // to merge and the most loads in flight per CTA (measured faster than two stream-K
+    // CTAs per SM at every token count) -- used when the pairs keep three quarters of the
+    // SM pairs busy.
+    pl.per_sm = 1;
+    pl.clusters = static_cast<int>(pairs);
+  } else {
+    // stream-K: two CTAs per SM while both double-buffered accumulators fit TMEM's 512
+    // columns, at least four K steps per cluster
+    pl.per_sm = 2 * fp8_tmem_cols(pl.tile, planes) <= 512 ? 2 : 1;
+    int64_t c = c1 * pl.per_sm;
+    const int64_t cap = work / 4 > 0 ? work / 4 : 1;
+    if (c > cap) c = cap;
+    // whole tile pairs at two CTAs per SM when they keep three quarters of those busy
+    if (pairs <= c && 4 * pairs >= 3 * c) c = pairs;
+    pl.clusters = static_cast<int>(c);
+  }
+  const int budget = pl.per_sm == 2 ? kSmemBudget2 : kSmemBudget;
+  pl.stages = (budget - kEpiStageBytes) / stage_bytes;
+  if (pl.stages > 8) pl.stages = 8;
   pl.smem = 1024 + static_cast<size_t>(pl.stages) * stage_bytes + kEpiStageBytes;
   return pl;
 }
