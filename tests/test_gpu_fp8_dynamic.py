@@ -185,3 +185,22 @@ def test_c_abi_rejects_bad_granularity(cuda_device):
     st = lib.inferd_fp8_dynamic_linear(None, None, None, None, 1, 1, 16, 0, 3, None, ctypes.c_size_t(0),
                                        _lib.stream_of(cuda_device))
     assert st == _lib.ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("n,k", [(200, 144), (130, 5136), (17408 - 128, 272)])
+@pytest.mark.parametrize("gran", ["tensor", "row"])
+def test_dynamic_linear_ragged_shapes(cuda_device, n, k, gran):
+    # K not a multiple of the 128-byte K step (TMA zero-fills the tail), N ending in a half
+    # empty tile pair, and a config-4-wide N whose last pair holds one tile (whole-tile plan)
+    g = torch.Generator().manual_seed(n + k)
+    w = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16).to(cuda_device)
+    for m in (3, 40):
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(cuda_device)
+        qw, sw = quantize_fp8_dynamic(w, gran)
+        for packed in (False, True):
+            wt = pack_fp8_weight(qw) if packed else qw
+            y = fp8_dynamic_linear(x, wt, sw, granularity=gran, packed_shape=(n, k) if packed else None)
+            qx, sx = _quant(x, gran)
+            cols = slice(0, n) if n <= 2048 else slice(n - 1536, n)
+            ref = oracle.fp8_dynamic_linear(qx, sx, qw.view(torch.uint8).cpu().numpy()[cols], sw.cpu().numpy()[cols])
+            assert_gemm_exact(y.float().cpu().numpy()[:, cols], ref, f"n={n} k={k} m={m} packed={packed}")

@@ -140,3 +140,19 @@ def test_quantize_model_keeps_lm_head(cuda_device):
         out = model(x).float()
     rel = float((out - ref).norm() / ref.norm())
     assert rel < 5e-2  # weight quantisation error, not a kernel tolerance
+
+
+@pytest.mark.parametrize("n,k", [(200, 144), (130, 5136), (17408 - 128, 272)])
+def test_fp8_linear_ragged_shapes(cuda_device, n, k):
+    # K tails inside a 128-byte step, a half-empty last tile pair, and the whole-tile plan
+    g = torch.Generator().manual_seed(7 * n + k)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    q, s = quantize_fp8_per_channel(w.to(cuda_device))
+    for m in (5, 64, 130):
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+        for packed in (False, True):
+            wt = pack_fp8_weight(q) if packed else q
+            y = fp8_linear(x.to(cuda_device), wt, s, packed_shape=(n, k) if packed else None)
+            rows = slice(0, n) if n <= 2048 else slice(n - 1536, n)
+            ref = oracle.fp8_linear(x.float().numpy(), q.view(torch.uint8).cpu().numpy()[rows], s.cpu().numpy()[rows])
+            assert_linear_close(y.float().cpu().numpy()[:, rows], ref, f"n={n} k={k} m={m} packed={packed}")
