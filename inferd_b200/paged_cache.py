@@ -412,8 +412,13 @@ class PagedKVCache:
                 if per == 1:
                     page = pos // bs
                     slot_list.append(blocks[page] * bs + pos - page * bs)
+                elif per <= bs:  # the window spans at most two pages
+                    p0, p1 = pos // bs, last // bs
+                    b0, b1 = blocks[p0] * bs - p0 * bs, blocks[p1] * bs - p1 * bs
+                    split = (p0 + 1) * bs
+                    slot_list.extend([(b0 if q < split else b1) + q for q in range(pos, pos + per)])
                 else:
-                    slot_list.extend(blocks[q // bs] * bs + q % bs for q in range(pos, pos + per))
+                    slot_list.extend([blocks[q // bs] * bs + q % bs for q in range(pos, pos + per)])
         except Exception:
             for t, nb in reversed(reserved):
                 self._rollback(t, nb)
@@ -537,6 +542,7 @@ class PagedKVCache:
                 t.dirty_from = _CLEAN
         else:
             cap, host, master = c.cap, c.host, c.master
+            keep_host = master is None  # a CUDA cache's tables live on the device after the rebuild
             # rows to send: those changed through this class since the last call, and those
             # whose list object was replaced from outside (whole row)
             starts = {i: t.dirty_from for i, t in enumerate(tables) if t.dirty_from != _CLEAN}
@@ -555,10 +561,11 @@ class PagedKVCache:
                 for col in range(max(n, start), old):
                     pairs.append(col)
                     pairs.append(0)
-                if start < n:
-                    host[i, start:n] = blocks[start:n]
-                if n < old:
-                    host[i, n:old] = 0
+                if keep_host:
+                    if start < n:
+                        host[i, start:n] = blocks[start:n]
+                    if n < old:
+                        host[i, n:old] = 0
                 counts[i + 1] = len(pairs) // 2
                 tables[i].dirty_from = _CLEAN
             row_ptr = np.maximum.accumulate(counts)  # entries of rows before each row
