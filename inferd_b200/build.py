@@ -1,4 +1,5 @@
-"""Build libinferd_sm100a.so from inferd_b200/csrc with nvcc (sm_100a only).
+"""Build libinferd_sm100a.so from inferd_b200/csrc with nvcc (sm_100a only), and the small
+host-side extension module _hostops (page-table loops, CPython C API) with g++.
 
 The library is a plain C-ABI shared object (no torch symbols), built in-tree into
 inferd_b200/lib/ so it travels with the source tree.  Usage:
@@ -14,6 +15,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
@@ -25,6 +27,8 @@ INCLUDE_DIR = REPO_DIR / "include"
 
 SOURCES = ["runtime.cu", "cache_ops.cu", "paged_attention.cu", "paged_attention_noalloc.cu",
            "fp8_linear.cu", "sampling.cu"]
+HOSTOPS_SRC = CSRC / "host_ops.cpp"
+HOSTOPS_PATH = PKG_DIR / ("_hostops" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -57,6 +61,24 @@ def _inputs() -> list[Path]:
     return _sources() + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE_DIR.glob("*.h")) + [Path(__file__)]
 
 
+def build_hostops(force: bool = False) -> Path:
+    """Compile the _hostops extension module in place (g++, CPython headers)."""
+    if (not force and HOSTOPS_PATH.exists()
+            and HOSTOPS_PATH.stat().st_mtime >= max(HOSTOPS_SRC.stat().st_mtime, Path(__file__).stat().st_mtime)):
+        return HOSTOPS_PATH
+    cxx = shutil.which("g++") or shutil.which("c++")
+    if cxx is None:
+        raise RuntimeError("g++ not found; the _hostops module needs a C++ compiler")
+    tmp = HOSTOPS_PATH.with_name(HOSTOPS_PATH.name + ".tmp")
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
+           f"-I{sysconfig.get_paths()['include']}", str(HOSTOPS_SRC), "-o", str(tmp)]
+    proc = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
+    if proc.returncode != 0:
+        raise RuntimeError(f"g++ failed:\n{proc.stdout.decode(errors='replace')}")
+    os.replace(tmp, HOSTOPS_PATH)
+    return HOSTOPS_PATH
+
+
 def needs_build() -> bool:
     if not LIB_PATH.exists():
         return True
@@ -65,7 +87,9 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -> Path:
-    """Compile every .cu to an object for sm_100a and link the shared library."""
+    """Compile every .cu to an object for sm_100a and link the shared library; build the
+    _hostops module."""
+    build_hostops(force=force)
     if not force and not needs_build():
         return LIB_PATH
     nvcc = nvcc_path()

@@ -25,6 +25,13 @@ import torch
 from . import _lib
 from .paged_attn import gather_paged_kv
 
+try:  # page-table loops in C (csrc/host_ops.cpp); the Python loops below are their twins
+    from . import _hostops
+except ImportError:  # not built: the same bookkeeping in Python
+    _hostops = None
+
+_NATIVE = _hostops is not None  # tests switch this off to compare the two
+
 
 class BlockAllocator:
     """LIFO allocator for fixed-size KV blocks (core/paged_cache.py:27-64).
@@ -256,6 +263,9 @@ class PagedKVCache:
         if len(seq_ids) != len(lengths):
             raise ValueError("one length per sequence")
         tables = [self._table(s) for s in seq_ids]
+        if _NATIVE:
+            return _hostops.truncate(tables, [int(n) for n in lengths], self.block_size,
+                                     self.allocator._free, self.allocator._allocated)
         for t, n in zip(tables, lengths):
             if n < 0 or n > t.length:
                 raise ValueError(f"cannot truncate a sequence of length {t.length} to {n}")
@@ -400,6 +410,20 @@ class PagedKVCache:
             raise ValueError("tokens_per_seq must be positive")
         tables = [self._table(s) for s in seq_ids]
         bs = self.block_size
+        if _NATIVE:
+            slots_np = np.empty(len(tables) * per, dtype=np.int64)
+            reserved, failed = _hostops.plan_slots(tables, per, bs, self.allocator._free,
+                                                   self.allocator._allocated, slots_np)
+            if failed >= 0:
+                t = tables[failed]
+                need = (t.length + per + bs - 1) // bs - len(t.blocks)
+                msg = f"requested {need} blocks, only {self.allocator.free_count} free"
+                for tt, nb in reversed(reserved):
+                    self._rollback(tt, nb)
+                raise MemoryError(msg)
+            slots = self._slot_tensor(slots_np)
+            bt, cl, mx = self._metadata(tables, seq_ids, per, None, None)
+            return AppendPlan(list(seq_ids), per, slots, bt, cl, mx, tables, reserved)
         reserved: list[tuple[SequencePageTable, list[int]]] = []
         slot_list: list[int] = []
         try:
@@ -444,8 +468,11 @@ class PagedKVCache:
             self.abort_append(plan)
             raise
         per = plan.tokens_per_seq
-        for t in plan._tables:
-            t.length += per
+        if _NATIVE:
+            _hostops.advance(plan._tables, per)
+        else:
+            for t in plan._tables:
+                t.length += per
         plan._open = False
 
     def abort_append(self, plan: AppendPlan) -> None:
@@ -517,20 +544,28 @@ class PagedKVCache:
         object was replaced from outside is recognised by the list's identity and re-sent
         whole.
         """
-        tables = [self._table(s) for s in seq_ids]
+        return self._metadata([self._table(s) for s in seq_ids], seq_ids, extra_tokens, pad_pages, device)
+
+    def _metadata(self, tables, seq_ids, extra_tokens, pad_pages, device):
         b = len(tables)
-        lens = [t.length + extra_tokens for t in tables]
-        nblk = [len(t.blocks) for t in tables]
-        width = max(nblk + [1])
+        if _NATIVE:
+            lens_np = np.empty(b, dtype=np.int32)
+            nblk, width, mx = _hostops.scan(tables, extra_tokens, lens_np)
+            lens = lens_np
+        else:
+            lens = [t.length + extra_tokens for t in tables]
+            nblk = [len(t.blocks) for t in tables]
+            width = max(nblk + [1])
+            mx = max(lens + [0])
         if pad_pages is not None:
             if pad_pages < width:
                 raise ValueError("pad_pages is narrower than the widest page table")
             width = pad_pages
         dev = self.device if device is None else torch.device(device)
         key = tuple(seq_ids)
-        ids = [id(t.blocks) for t in tables]
         c = self._meta_cache
         dense = c is None or c.key != key or width > c.cap or c.device != dev
+        ids = [id(t.blocks) for t in tables] if (dense or not _NATIVE) else None
         if dense:
             cap = (width + 63) // 64 * 64  # room to grow without a rebuild
             host = np.zeros((b, cap), dtype=np.int32)
@@ -543,6 +578,16 @@ class PagedKVCache:
         else:
             cap, host, master = c.cap, c.host, c.master
             keep_host = master is None  # a CUDA cache's tables live on the device after the rebuild
+        if not dense and _NATIVE:
+            counts = np.zeros(b + 1, dtype=np.int32)
+            pair_bytes, ids, _ = _hostops.pack_changes(tables, c.ids, c.nblk, _CLEAN, counts[1:])
+            pairs_np = np.frombuffer(pair_bytes, dtype=np.int32)
+            row_ptr = np.cumsum(counts, dtype=np.int32)
+            if keep_host and pairs_np.size:
+                rows = np.repeat(np.arange(b), counts[1:])
+                host[rows, pairs_np[0::2]] = pairs_np[1::2]
+            flat = np.concatenate([np.asarray(lens, dtype=np.int32), row_ptr, pairs_np])
+        elif not dense:
             # rows to send: those changed through this class since the last call, and those
             # whose list object was replaced from outside (whole row)
             starts = {i: t.dirty_from for i, t in enumerate(tables) if t.dirty_from != _CLEAN}
@@ -572,9 +617,8 @@ class PagedKVCache:
             flat = np.concatenate([np.asarray(lens, dtype=np.int32), row_ptr,
                                    np.asarray(pairs, dtype=np.int32)])
         self._meta_cache = _MetaCache(key, cap, host, nblk, ids, master, dev)
-        mx = max(lens + [0])
         if dev.type != "cuda":
-            return torch.from_numpy(host[:, :width].copy()), torch.tensor(lens, dtype=torch.int32), mx
+            return torch.from_numpy(host[:, :width].copy()), torch.as_tensor(np.asarray(lens, dtype=np.int32)), mx
         packed = self._stage_i32.upload(flat, dev)
         cl = packed[:b]
         bt = torch.empty((b, width), dtype=torch.int32, device=dev)

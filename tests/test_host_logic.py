@@ -321,3 +321,68 @@ def test_plan_and_commit_equal_append_then_metadata():
         a.plan_append(ids, 10_000)
     assert a.allocator.free_count == free
     a.assert_consistent()
+
+
+def test_native_page_table_loops_match_python():
+    # csrc/host_ops.cpp walks the same Python page tables and allocator as the pure-Python
+    # loops: identical tables, free lists, slots and metadata on a random decode / verify /
+    # rollback sequence, including an exhausted pool (MemoryError with nothing taken)
+    from inferd_b200 import paged_cache
+    if paged_cache._hostops is None:
+        pytest.skip("_hostops not built")
+    caches = {}
+    for native in (True, False):
+        caches[native] = RecordingCache(num_layers=1, num_blocks=120, block_size=4, num_kv_heads=1,
+                                        head_dim=1, dtype=torch.float32)
+    ids = [7, 3, 11, 5]
+
+    def run(native, fn):
+        old = paged_cache._NATIVE
+        paged_cache._NATIVE = native
+        try:
+            return fn(caches[native])
+        except MemoryError as e:
+            return ("MemoryError", str(e))
+        finally:
+            paged_cache._NATIVE = old
+
+    for native in (True, False):
+        for s in ids:
+            caches[native].create_sequence(s)
+    rng = np.random.default_rng(17)
+    for step in range(300):
+        per = int(rng.choice([1, 1, 2, 5, 9]))
+        def plan_commit(c, per=per):
+            plan = c.plan_append(ids, per)
+            c.commit_append(plan, [torch.zeros(4 * per, 1, 1)], [torch.zeros(4 * per, 1, 1)])
+            return (plan.slots.tolist(), plan.block_tables.tolist(), plan.context_lens.tolist(),
+                    plan.max_context_len)
+        a, b = run(True, plan_commit), run(False, plan_commit)
+        assert a == b, f"step {step}"
+        if rng.random() < 0.5:
+            lens = [int(rng.integers(0, caches[True].sequence_length(s) + 1)) for s in ids]
+            fa = run(True, lambda c: c.truncate_batched(ids, lens))
+            fb = run(False, lambda c: c.truncate_batched(ids, lens))
+            assert fa == fb
+        if step % 50 == 25:  # the pool runs out part-way: earlier tables' pages roll back
+            free = caches[True].allocator.free_count
+            big = 4 * (free // 3 + 1)
+            def plan_big(c, big=big):
+                c.plan_append(ids, big)
+            ea, eb = run(True, plan_big), run(False, plan_big)
+            assert ea == eb and ea is not None and ea[0] == "MemoryError"
+            assert caches[True].allocator.free_count == free
+        if step % 37 == 5:  # a list replaced from outside the class
+            for native in (True, False):
+                t = caches[native].sequences[3]
+                t.blocks = list(t.blocks)
+        ma = run(True, lambda c: [x.tolist() if hasattr(x, "tolist") else x for x in c.decode_metadata(ids)])
+        mb = run(False, lambda c: [x.tolist() if hasattr(x, "tolist") else x for x in c.decode_metadata(ids)])
+        assert ma == mb
+        assert [caches[True].sequences[s].blocks for s in ids] == [caches[False].sequences[s].blocks for s in ids]
+        assert caches[True].allocator._free == caches[False].allocator._free
+        assert caches[True].allocator._allocated == caches[False].allocator._allocated
+    for native in (True, False):
+        caches[native].assert_consistent()
+    with pytest.raises(ValueError):
+        run(True, lambda c: c.truncate_batched(ids, [10 ** 6] * 4))
