@@ -168,7 +168,7 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // wait until at most one committed store group still reads shared memory
 __device__ __forceinline__ void bulk_wait_read_le1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // make this thread's generic-proxy shared-memory writes visible to the TMA (async proxy)
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -628,7 +628,9 @@ __global__ void __launch_bounds__(kFp8Threads, 2)
       ++seg;
       g = s_end;
     }
-    if (lane == 0 && ychunk > 0) bulk_wait_all();  // y written before the CTA retires
+    // the CTA may retire once its store groups have read their shared-memory blocks; the
+    // global writes complete with the grid
+    if (lane == 0 && ychunk > 0) bulk_wait_read_all();
     __syncwarp();
   }
 
