@@ -328,14 +328,16 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
 
 def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.device) -> dict:
     """Same step through the public API with pinned host inputs and a host read of the
-    result every step: one host-to-device copy of the step's inputs ->
-    PagedKVCache.commit_append (the K/V write of a plan_append plan: pages, slots, attention
-    metadata) -> paged_attention_batched -> (all-gather) -> device-to-host copy -> sync.
-    Decode plans step N + 1 between step N's launches and its sync, as an engine that
-    schedules ahead does; verify plans after its rollback."""
+    result every step: a DecodeGraph replay -- the host-to-device copy of the step's inputs
+    (queries and new K/V from pinned memory), the page-table update, the KV append, paged
+    attention and the device-to-host copy of the output -- then (N > 1) the all-gather and
+    its copy to the host, and a stream sync.  The host side of a step (pages, slots, table
+    changes) is DecodeGraph.prepare; decode prepares step N + 1 while step N runs, as an
+    engine that schedules ahead does, and verify after its rollback, which needs the step's
+    result."""
     import torch.distributed as dist
 
-    from inferd_b200.paged_attn import paged_attention_batched
+    from inferd_b200.decode_graph import DecodeGraph
     from inferd_b200.paged_cache import PagedKVCache
     from inferd_b200.sharded import gather_outputs
 
@@ -354,59 +356,38 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
         used.update(t.blocks)
     cache.allocator._allocated = set(used)
     cache.allocator._free = [x for x in cache.allocator._free if x not in used]
-    # the step's inputs (queries and the new K/V) sit in one pinned buffer and cross to the
-    # device in one copy, as an engine stages a step's host-produced tensors
-    parts = [dwl.q, dwl.k_new, dwl.v_new]
-    sizes = [t.numel() for t in parts]
-    inp_h = torch.empty(sum(sizes), dtype=torch.bfloat16).pin_memory()
-    inp_d = torch.empty(sum(sizes), dtype=torch.bfloat16, device=device)
-    off = 0
-    views_d = []
-    for t, n in zip(parts, sizes):
-        inp_h[off:off + n].copy_(t.reshape(-1).cpu())
-        views_d.append(inp_d[off:off + n].view(t.shape))
-        off += n
+    graph = DecodeGraph(cache, ids, num_q_heads=HQ, q_len=ql, copy_out=world == 1)
+    # the step's inputs: the same data every step, staged once in both pinned sets; every
+    # replay copies them to the device
+    for q_h, k_h, v_h in graph.input_buffers():
+        q_h.copy_(dwl.q.cpu())
+        k_h.copy_(dwl.k_new.cpu())
+        v_h.copy_(dwl.v_new.cpu())
     out_rows = dwl.b * world
     out_h = torch.empty((out_rows, ql, HQ, D), dtype=torch.bfloat16).pin_memory()
     gathered = torch.empty((out_rows, ql, HQ, D), dtype=torch.bfloat16, device=device)
     stream = torch.cuda.current_stream(device)
     steps = max(1, min(args.steps, args.e2e_steps))
-    h2d = d2h = 0
-    plan = None
+    d2h = out_rows * ql * HQ * D * ELEM
 
     def one_step():
-        # plan_append reserves the step's pages, uploads its slots and builds the attention
-        # metadata; commit_append writes the K/V.  Decode plans the next step while this
-        # step's attention runs (pages depend only on lengths); verify plans after its
-        # rollback, which needs the step's result.
-        nonlocal d2h, plan
-        inp_d.copy_(inp_h, non_blocking=True)
-        q, k, v = views_d
-        if plan is None:
-            plan = cache.plan_append(ids, ql)
-        cur, plan = plan, None
-        cache.commit_append(cur, [k], [v])
-        out = paged_attention_batched(q, cache.key_cache[0], cache.value_cache[0], cur.block_tables,
-                                      cur.context_lens, max_context_len=cur.max_context_len)
+        graph.launch()
         if world > 1:
-            gather_outputs(out, out=gathered)
-            res = gathered
-        else:
-            res = out
-        out_h[: res.shape[0]].copy_(res, non_blocking=True)
+            gather_outputs(graph.output, out=gathered)
+            out_h.copy_(gathered, non_blocking=True)
         if ql == 1:
-            plan = cache.plan_append(ids, ql)
+            graph.prepare()  # step N + 1's pages and slots while step N runs
         stream.synchronize()
         if ql > 1:
             # speculative verify: keep one accepted token, roll the rest of the window back
             cache.truncate_batched(ids, [cache.sequence_length(i) - ql + 1 for i in ids])
-        d2h = res.numel() * ELEM
+            graph.prepare()
 
-    one_step()  # warm the path (pinned staging, workspace)
+    graph.prepare()
+    one_step()  # warm the path
     # every step grows each context by one token net, so the bytes of the timed steps are
     # known up front: step s attends over base + s + q_len keys per sequence
     base = np.asarray([cache.sequence_length(i) for i in ids], dtype=np.int64)
-    meta0 = cache.uploaded_bytes()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
@@ -417,14 +398,11 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
     e1.record(stream)
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1)
-    if plan is not None:
-        cache.abort_append(plan)  # the plan made for a step that does not run
+    graph.abort()  # the step prepared for after the last timed one
     if [cache.sequence_length(i) for i in ids] != (base + steps).tolist():
         raise RuntimeError("context lengths after the timed steps differ from the byte count's")
     total_bytes = float(sum(step_bytes(base + s + ql, ql)["total"] for s in range(steps)))
-    # the inputs' one copy, plus what the cache uploaded (slot mappings, sparse table updates
-    # and lengths), averaged over the timed steps
-    h2d = inp_h.numel() * ELEM + (cache.uploaded_bytes() - meta0) / steps
+    h2d = graph.staged_bytes()  # inputs, slots, lengths and table changes of one replay
     t = torch.tensor([ms, total_bytes], dtype=torch.float64, device=device)
     if world > 1:
         mx = t.clone()
@@ -433,11 +411,12 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         ms, total_bytes = float(mx[0]), float(sm[1])
     return {"value": round(total_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-            "h2d_bytes_per_step": int(round(h2d)), "d2h_bytes_per_step": int(d2h),
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "steps": steps, "ms_per_step": round(ms / steps, 5),
-            "note": "contexts grow by one token per step (verify: the window is appended, "
-                    "verified, and all but one token rolled back); bytes counted per step; "
-                    "decode plans the next step's pages while the current step runs"}
+            "note": "one DecodeGraph replay per step (inputs H2D from pinned memory, page-table "
+                    "update, KV append, attention, output D2H); contexts grow by one token per "
+                    "step (verify: the window is appended, verified, and all but one token "
+                    "rolled back); decode prepares the next step while the current one runs"}
 
 
 # ------------------------------------------------------------------ FP8 linear (config 4)
