@@ -280,8 +280,12 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
     }
   };
 
+  // Segments this warp merges after its page loop: at most the one its range opens
+  // inside and the one it closes inside.
+  int n_merge = 0, merge_b0 = 0, merge_h0 = 0, merge_b1 = 0, merge_h1 = 0;
+
   // Finish the piece [piece_start, piece_end) of the current segment: store the output
-  // if the piece is the whole segment, else publish a partial and maybe merge.
+  // if the piece is the whole segment, else publish a partial and take a ticket.
   auto end_piece = [&](int64_t piece_end) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -342,57 +346,101 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
     if (lane == 0) last = atomicAdd(p.counters + seg_id, 1) == u_last - u_first;
     last = __shfl_sync(0xffffffffu, last, 0);
     if (!last) return;
+    // this warp finished the segment last: merge it after the page loop
+    if (n_merge == 0) { merge_b0 = b; merge_h0 = h; } else { merge_b1 = b; merge_h1 = h; }
+    ++n_merge;
+  };
+
+  // ---- merge the partials of segment (mb, mh).  Merges run after the warp's page loop,
+  // where none of the loop's registers are live; those of the segments cut at the end of
+  // warp ranges run after every warp's loop, so each dependent L2 round trip here
+  // lengthens the launch: a piece's (m, l) is read once, and two pieces' O partials are
+  // in flight together.
+  auto merge_segment = [&](int mb, int mh) {
     __threadfence();
-    // ---- merge the segment's partials (this warp finished it last)
+    const int mpb = prefix[mb + 1] - prefix[mb];
+    const int64_t mstart = static_cast<int64_t>(Hkv) * prefix[mb] + static_cast<int64_t>(mh) * mpb;
+    const int u_first = unit_of(mstart, T_pages, U);
+    const int u_last = unit_of(mstart + mpb - 1, T_pages, U);
+    const int seg_id = mb * Hkv + mh;
     const int np = u_last - u_first + 1;
+    const int cp = 2 * (lane & 3);
     for (int nt = 0; nt < NT; ++nt) {
-      // column maxima and normalisers over all pieces, 8 columns of this n-tile
-      float M[8], Ls[8];
+      // column maxima over all pieces, 8 columns of this n-tile; lane q keeps piece q's
+      // (m, l) of the first 32 pieces in mq / lq
+      float M[8], Ls[8], mq[8], lq[8];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) M[c] = -INFINITY, Ls[c] = 0.f;
+      for (int c = 0; c < 8; ++c) M[c] = -INFINITY, Ls[c] = 0.f, mq[c] = -INFINITY, lq[c] = 0.f;
       for (int p0 = 0; p0 < np; p0 += 32) {
         if (p0 + lane < np) {
-          const float* ml = p.part_ml + ((static_cast<int64_t>(u_first) + p0 + lane + seg_id) * NQP + nt * 8) * 2;
+          const float2* ml = reinterpret_cast<const float2*>(
+              p.part_ml + ((static_cast<int64_t>(u_first) + p0 + lane + seg_id) * NQP + nt * 8) * 2);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) M[c] = fmaxf(M[c], __ldcg(ml + 2 * c));
+          for (int c = 0; c < 8; ++c) {
+            const float2 v = __ldcg(ml + c);
+            M[c] = fmaxf(M[c], v.x);
+            if (p0 == 0) { mq[c] = v.x; lq[c] = v.y; }
+          }
         }
       }
 #pragma unroll
       for (int c = 0; c < 8; ++c)
 #pragma unroll
         for (int o2 = 16; o2 > 0; o2 >>= 1) M[c] = fmaxf(M[c], __shfl_xor_sync(0xffffffffu, M[c], o2));
-      // each lane: the two columns 2*(lane&3), +1 of this n-tile and rows d = k*8 + lane/4
+      // each lane: the two columns cp, cp + 1 of this n-tile and rows d = k*8 + lane/4
       float2 acc[16];
 #pragma unroll
       for (int k = 0; k < 16; ++k) acc[k] = make_float2(0.f, 0.f);
-      const int cp = 2 * (lane & 3);
       for (int p0 = 0; p0 < np; p0 += 32) {
+        const bool have = p0 + lane < np;
+        if (p0 > 0) {
+          const float2* ml = reinterpret_cast<const float2*>(
+              p.part_ml + ((static_cast<int64_t>(u_first) + p0 + lane + seg_id) * NQP + nt * 8) * 2);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float2 v = have ? __ldcg(ml + c) : make_float2(-INFINITY, 0.f);
+            mq[c] = v.x;
+            lq[c] = v.y;
+          }
+        }
         // lane q of the chunk holds piece p0+q's weights exp2(m - M) for all 8 columns
         float fq[8];
-        const bool have = p0 + lane < np;
-        const float* ml = p.part_ml + ((static_cast<int64_t>(u_first) + p0 + lane + seg_id) * NQP + nt * 8) * 2;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const float mc = have ? __ldcg(ml + 2 * c) : -INFINITY;
-          const float lc = have ? __ldcg(ml + 2 * c + 1) : 0.f;
-          fq[c] = ex2(mc - (M[c] == -INFINITY ? 0.f : M[c]));
-          Ls[c] += lc * fq[c];
+          fq[c] = ex2(mq[c] - (M[c] == -INFINITY ? 0.f : M[c]));
+          Ls[c] += lq[c] * fq[c];
         }
         const int nq_chunk = min(32, np - p0);
-        for (int q = 0; q < nq_chunk; ++q) {
-          float f0 = 0.f, f1 = 0.f;
+        for (int q0 = 0; q0 < nq_chunk; q0 += 2) {
+          float2 v[2][16];
+          float f0[2], f1[2];
 #pragma unroll
-          for (int c = 0; c < 8; c += 2) {
-            const float a0 = __shfl_sync(0xffffffffu, fq[c], q);
-            const float a1 = __shfl_sync(0xffffffffu, fq[c + 1], q);
-            if (c == cp) { f0 = a0; f1 = a1; }
+          for (int i = 0; i < 2; ++i) {
+            const int q = q0 + i;
+            f0[i] = f1[i] = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; c += 2) {
+              const float a0 = __shfl_sync(0xffffffffu, fq[c], q & 31);
+              const float a1 = __shfl_sync(0xffffffffu, fq[c + 1], q & 31);
+              if (c == cp) { f0[i] = a0; f1[i] = a1; }
+            }
+            if (q < nq_chunk) {
+              const float* po2 = p.part_o + (static_cast<int64_t>(u_first) + p0 + q + seg_id) * kHeadDim * NQP + nt * 8 + cp;
+#pragma unroll
+              for (int k = 0; k < 16; ++k)
+                v[i][k] = __ldcg(reinterpret_cast<const float2*>(po2 + (k * 8 + (lane >> 2)) * NQP));
+            }
           }
-          const float* po2 = p.part_o + (static_cast<int64_t>(u_first) + p0 + q + seg_id) * kHeadDim * NQP + nt * 8 + cp;
+          // pieces in order, as one piece at a time would add them
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const float2 v = __ldcg(reinterpret_cast<const float2*>(po2 + (k * 8 + (lane >> 2)) * NQP));
-            acc[k].x += f0 * v.x;
-            acc[k].y += f1 * v.y;
+          for (int i = 0; i < 2; ++i) {
+            if (q0 + i < nq_chunk) {
+#pragma unroll
+              for (int k = 0; k < 16; ++k) {
+                acc[k].x += f0[i] * v[i][k].x;
+                acc[k].y += f1[i] * v[i][k].y;
+              }
+            }
           }
         }
       }
@@ -410,7 +458,7 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
         const int c = nt * 8 + cp + j;
         if (c >= p.nq) continue;
         const int qi = c / p.group, gi = c - qi * p.group;
-        T* dst = optr + ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) * kHeadDim;
+        T* dst = optr + ((static_cast<int64_t>(mb) * p.q_len + qi) * p.num_q_heads + mh * p.group + gi) * kHeadDim;
 #pragma unroll
         for (int k = 0; k < 16; ++k)
           dst[k * 8 + (lane >> 2)] = from_f32<T>(j == 0 ? acc[k].x * i0 : acc[k].y * i1);
@@ -553,6 +601,8 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
   }
   // (also after an abort, so the ticket counters return to zero)
   end_piece(g1);
+  if (n_merge > 0) merge_segment(merge_b0, merge_h0);
+  if (n_merge > 1) merge_segment(merge_b1, merge_h1);
 
   // Drain: never leave the warp with a TMA write still in flight into its smem.
   if (abort && lane == 0) {
