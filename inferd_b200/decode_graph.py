@@ -4,7 +4,8 @@ The reference's decode loop issues, per step and per sequence, Python-level cach
 and attention calls (core/scheduler.py:142-159, core/paged_attn_interface.py:25-62).  Here a
 step of a whole batch is one graph replay:
 
-    host->device copy of the step's inputs (queries, new K and V) from pinned memory
+    one host->device copy of the step's inputs (queries, new K and V, slots, lengths and
+    page-table changes) from pinned memory
     -> sparse page-table update of a device-resident [B, capacity] table
     -> KV append (reshape_and_cache) -> paged attention over the table
     -> device->host copy of the output
@@ -72,13 +73,21 @@ class DecodeGraph:
         # per step each row gains at most ceil(q_len / block) + 1 pages and may lose as many
         self._max_pairs = b * (2 * (ql // cache.block_size + 2)) + 64
         n_meta = 2 * b + 1 + 2 * self._max_pairs
-        self._inp_h = [torch.empty(n_in, dtype=dt).pin_memory() for _ in range(2)]
-        self._slots_h = [torch.full((b * ql,), -1, dtype=torch.int64).pin_memory() for _ in range(2)]
-        self._meta_h = [torch.zeros(n_meta, dtype=torch.int32).pin_memory() for _ in range(2)]
-        self._out_h = [torch.empty((b, ql, num_q_heads, d), dtype=dt).pin_memory() for _ in range(2)]
-        self._inp_d = torch.empty(n_in, dtype=dt, device=dev)
-        self._slots_d = torch.empty(b * ql, dtype=torch.int64, device=dev)
-        self._meta_d = torch.zeros(n_meta, dtype=torch.int32, device=dev)
+        # One staging area per set, [inputs | slots (int64) | lengths, row offsets, changes
+        # (int32)], so a step's inputs cross the host link as ONE copy: each copy costs a
+        # few microseconds of its own, which three small copies paid three times.
+        es = torch.empty(0, dtype=dt).element_size()
+        self._off_slots = _align(n_in * es)
+        self._off_meta = _align(self._off_slots + b * ql * 8)
+        self._nbytes = self._off_meta + n_meta * 4
+        self._stage_h = [torch.empty(self._nbytes, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+        self._stage_d = torch.zeros(self._nbytes, dtype=torch.uint8, device=dev)
+        self._inp_h, self._slots_h, self._meta_h = zip(*(self._views(h, n_in, n_meta) for h in self._stage_h))
+        self._inp_d, self._slots_d, self._meta_d = self._views(self._stage_d, n_in, n_meta)
+        for i in range(2):
+            self._slots_h[i].fill_(-1)
+            self._meta_h[i].zero_()
+        self._out_h = [torch.empty((b, ql, num_q_heads, d), dtype=dt, pin_memory=True) for _ in range(2)]
         self._out_d = torch.empty((b, ql, num_q_heads, d), dtype=dt, device=dev)
         self._events = [torch.cuda.Event(), torch.cuda.Event()]
         self._recorded = [False, False]
@@ -91,6 +100,14 @@ class DecodeGraph:
         self._build(max(len(t.blocks) for t in self.tables))
 
     # ------------------------------------------------------------ set-up
+    def _views(self, buf: torch.Tensor, n_in: int, n_meta: int):
+        """(inputs, slots, metadata) views of one staging byte buffer."""
+        b, ql, dt = self._b, self.q_len, self.cache.dtype
+        es = torch.empty(0, dtype=dt).element_size()
+        return (buf[:n_in * es].view(dt),
+                buf[self._off_slots:self._off_slots + b * ql * 8].view(torch.int64),
+                buf[self._off_meta:self._off_meta + n_meta * 4].view(torch.int32))
+
     def _upload_dense(self) -> None:
         """Copy every table to the device master (stream-ordered after earlier replays)."""
         host = np.zeros((self._b, self._cap), dtype=np.int32)
@@ -128,9 +145,7 @@ class DecodeGraph:
     def _body(self, i: int) -> None:
         cache, b, ql, hq, d = self.cache, self._b, self.q_len, self.num_q_heads, self.cache.head_dim
         dev = cache.device
-        self._inp_d.copy_(self._inp_h[i], non_blocking=True)
-        self._slots_d.copy_(self._slots_h[i], non_blocking=True)
-        self._meta_d.copy_(self._meta_h[i], non_blocking=True)
+        self._stage_d.copy_(self._stage_h[i], non_blocking=True)
         lib = _lib.load()
         rp = self._meta_d[b:2 * b + 1]
         upd = self._meta_d[2 * b + 1:]
@@ -250,6 +265,10 @@ class DecodeGraph:
         return self._out_d
 
     def staged_bytes(self) -> int:
-        """Host-to-device bytes one replay copies (inputs, slots, lengths and changes)."""
-        return (self._inp_h[0].numel() * self._inp_h[0].element_size() + self._slots_h[0].numel() * 8
-                + self._meta_h[0].numel() * 4)
+        """Host-to-device bytes one replay copies (inputs, slots, lengths and changes, with
+        the alignment gaps between them)."""
+        return self._nbytes
+
+
+def _align(n: int, a: int = 256) -> int:
+    return (n + a - 1) // a * a
