@@ -149,7 +149,8 @@ def ncu_traffic(workload: str) -> float | None:
 class DeviceWorkload:
     """One rank's share of the workload, resident on its GPU."""
 
-    def __init__(self, workload: str, rank: int, world: int, device: torch.device) -> None:
+    def __init__(self, workload: str, rank: int, world: int, device: torch.device,
+                 growth_tokens: int = 0) -> None:
         w = WORKLOADS[workload]
         self.q_len = w["q_len"]
         from inferd_b200.sharded import shard_range
@@ -161,7 +162,10 @@ class DeviceWorkload:
         # context after the append = base + q_len (the appended tokens sit at base .. )
         self.ctx = self.base + self.q_len
         pages = (self.ctx + BS - 1) // BS
-        self.num_blocks = int(math.ceil(1.1 * pages.sum()))
+        # 10 % spare blocks, plus room for every sequence to grow by growth_tokens (the e2e
+        # steps keep one token per step)
+        grow = (growth_tokens + self.q_len + BS - 1) // BS + 1
+        self.num_blocks = int(math.ceil(1.1 * pages.sum())) + self.b * grow
         g = torch.Generator(device=device).manual_seed(1234 + rank)
         shape = (self.num_blocks, HKV, BS, D)
         self.kc = torch.randn(shape, generator=g, device=device, dtype=torch.bfloat16)
@@ -201,7 +205,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     from inferd_b200.sharded import gather_outputs
 
     lib = _lib.load()
-    wl = DeviceWorkload(args.workload, rank, world, device)
+    wl = DeviceWorkload(args.workload, rank, world, device, growth_tokens=args.e2e_steps + 64)
     stream = torch.cuda.current_stream(device)
     err = _lib.error_word(device)
     gathered = torch.empty((world * wl.b,) + tuple(wl.out.shape[1:]), dtype=wl.out.dtype,

@@ -176,6 +176,14 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Programmatic dependent launch.  griddepcontrol.wait blocks until the grids this one
+// depends on have finished and their writes are visible (a no-op in a grid launched
+// without the programmatic-serialization attribute); launch_dependents lets a grid
+// launched after this one with that attribute be scheduled before this one ends.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

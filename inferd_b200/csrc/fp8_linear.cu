@@ -86,13 +86,6 @@ __device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t adesc, uin
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// Programmatic dependent launch: the GEMM may start while the activation split still
-// runs; griddepcontrol.wait blocks until the split grid has finished and its writes are
-// visible, launch_dependents lets the dependent grid be scheduled early.
-__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void grid_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
 // The mbarrier at the same shared-memory offset in both CTAs of the pair receives one
 // arrival once every tcgen05.mma issued so far by this thread has completed.
 __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {

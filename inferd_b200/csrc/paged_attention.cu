@@ -65,7 +65,8 @@ struct FastParams {
   int32_t num_seqs, q_len, num_q_heads, num_kv_heads, group, nq;
   int64_t num_blocks;
   float scale_log2;
-  int32_t* counters;  // per (sequence, kv head) ticket counters, 0 between launches
+  int32_t defer_merge;  // cut segments: partials only, merged by merge_cut_segments_kernel
+  int32_t* counters;  // per (sequence, kv head) ticket counters / cut markers, 0 between launches
   float* part_ml;     // [slot][NQP][2]    (m, l) per query row
   float* part_o;      // [slot][128][NQP]  unnormalised O, query row fastest
   int32_t* error_word;
@@ -338,10 +339,16 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
           *reinterpret_cast<float2*>(p.part_ml + (slot * NQP + c) * 2) = make_float2(m[nt][j], l[nt][j]);
         }
     }
-    __threadfence();
-    __syncwarp();
     const int u_first = unit_of(seg_start, T_pages, U);
     const int u_last = unit_of(seg_end - 1, T_pages, U);
+    if (p.defer_merge) {
+      // partials only: merge_cut_segments_kernel merges every cut segment after this grid.
+      // Every piece of the segment stores the same marker (piece count, first unit).
+      if (lane == 0) p.counters[seg_id] = ((u_last - u_first + 1) << 20) | u_first;
+      return;
+    }
+    __threadfence();
+    __syncwarp();
     int last = 0;
     if (lane == 0) last = atomicAdd(p.counters + seg_id, 1) == u_last - u_first;
     last = __shfl_sync(0xffffffffu, last, 0);
@@ -603,6 +610,9 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
   end_piece(g1);
   if (n_merge > 0) merge_segment(merge_b0, merge_h0);
   if (n_merge > 1) merge_segment(merge_b1, merge_h1);
+  // the merge kernel that follows (deferred merging) may be scheduled once every CTA has a
+  // warp past this point; it waits for the whole grid before it reads anything
+  grid_launch_dependents();
 
   // Drain: never leave the warp with a TMA write still in flight into its smem.
   if (abort && lane == 0) {
@@ -611,6 +621,96 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
       mbar_wait(&full[s], static_cast<uint32_t>((rounds - 1) & 1));
     }
   }
+}
+
+// One CTA per (sequence, kv head) segment; the segments the attention grid cut into pieces
+// (marker in counters) are merged, the others skipped.  Thread d owns row d of O for all
+// NQP query rows.  Launched after paged_attn_tc_kernel when the pieces carry several
+// n-tiles: there one warp merging a segment alone at the end of the attention grid took
+// 6-12 us of dependent L2 round trips, while here every segment merges at once.
+template <typename T, int NQP>
+__global__ void __launch_bounds__(kHeadDim) merge_cut_segments_kernel(const FastParams p) {
+  grid_dependency_wait();  // the attention grid's partials and markers
+  const int seg_id = blockIdx.x;
+  const int code = p.counters[seg_id];
+  if (code == 0) return;
+  const int u_first = code & 0xfffff, np = code >> 20;
+  const int b = seg_id / p.num_kv_heads, h = seg_id - b * p.num_kv_heads;
+  const int d = threadIdx.x;
+  __shared__ float2 mls[32][NQP];  // (m, l) of up to 32 pieces, loaded in one round trip
+  __shared__ float f[32][NQP];     // their weights exp2(m - M)
+  __shared__ float Ms[NQP], Linv[NQP];
+  // slots of the pieces: unit + segment id, consecutive units
+  const float2* ml = reinterpret_cast<const float2*>(p.part_ml) + (static_cast<int64_t>(u_first) + seg_id) * NQP;
+  const float* po = p.part_o + (static_cast<int64_t>(u_first) + seg_id) * kHeadDim * NQP;
+  auto load_ml = [&](int q0, int nqc) {
+    for (int i = d; i < nqc * NQP; i += kHeadDim) mls[i / NQP][i % NQP] = __ldcg(ml + q0 * NQP + i);
+  };
+  // column maxima over all pieces
+  float mx = -INFINITY;
+  for (int q0 = 0; q0 < np; q0 += 32) {
+    const int nqc = min(32, np - q0);
+    __syncthreads();
+    load_ml(q0, nqc);
+    __syncthreads();
+    if (d < NQP)
+      for (int q = 0; q < nqc; ++q) mx = fmaxf(mx, mls[q][d].x);
+  }
+  if (d < NQP) Ms[d] = mx == -INFINITY ? 0.f : mx;
+  float L = 0.f, acc[NQP];
+#pragma unroll
+  for (int c = 0; c < NQP; ++c) acc[c] = 0.f;
+  for (int q0 = 0; q0 < np; q0 += 32) {
+    const int nqc = min(32, np - q0);
+    __syncthreads();  // Ms visible; f (and mls) free
+    if (np > 32) {    // the first pass left only the last chunk in mls
+      load_ml(q0, nqc);
+      __syncthreads();
+    }
+    for (int i = d; i < nqc * NQP; i += kHeadDim) {
+      const int q = i / NQP, c = i - q * NQP;
+      f[q][c] = ex2(mls[q][c].x - Ms[c]);
+    }
+    __syncthreads();
+    if (d < NQP)
+      for (int q = 0; q < nqc; ++q) L += mls[q][d].y * f[q][d];
+    // row d of O, pieces in order, four pieces' loads in flight together
+    for (int q = 0; q < nqc; q += 4) {
+      float4 v[4][NQP / 4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (q + i < nqc) {
+          const float4* row =
+              reinterpret_cast<const float4*>(po + (static_cast<int64_t>(q0 + q + i) * kHeadDim + d) * NQP);
+#pragma unroll
+          for (int c4 = 0; c4 < NQP / 4; ++c4) v[i][c4] = __ldcg(row + c4);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (q + i < nqc) {
+#pragma unroll
+          for (int c4 = 0; c4 < NQP / 4; ++c4) {
+            acc[4 * c4 + 0] += f[q + i][4 * c4 + 0] * v[i][c4].x;
+            acc[4 * c4 + 1] += f[q + i][4 * c4 + 1] * v[i][c4].y;
+            acc[4 * c4 + 2] += f[q + i][4 * c4 + 2] * v[i][c4].z;
+            acc[4 * c4 + 3] += f[q + i][4 * c4 + 3] * v[i][c4].w;
+          }
+        }
+      }
+    }
+  }
+  if (d < NQP) Linv[d] = L > 0.f ? 1.f / L : 0.f;
+  __syncthreads();
+  T* optr = static_cast<T*>(p.out);
+#pragma unroll
+  for (int c = 0; c < NQP; ++c) {
+    if (c >= p.nq) break;
+    const int qi = c / p.group, gi = c - qi * p.group;
+    optr[((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) * kHeadDim + d] =
+        from_f32<T>(acc[c] * Linv[c]);
+  }
+  if (d == 0) p.counters[seg_id] = 0;
 }
 
 // ------------------------------------------------------------------ generic path
@@ -858,6 +958,32 @@ int launch_fast(const CUtensorMap& km, const CUtensorMap& vm, const FastParams& 
   }
 }
 
+template <bool kBf16, int NQP>
+int launch_merge_t(const FastParams& fp, int segs, cudaStream_t s) {
+  using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(segs));
+  cfg.blockDim = dim3(kHeadDim);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, merge_cut_segments_kernel<T, NQP>, fp));
+}
+
+template <bool kBf16>
+int launch_merge(const FastParams& fp, int nt, int segs, cudaStream_t s) {
+  switch (nt) {
+    case 1: return launch_merge_t<kBf16, 8>(fp, segs, s);
+    case 2: return launch_merge_t<kBf16, 16>(fp, segs, s);
+    case 3: return launch_merge_t<kBf16, 24>(fp, segs, s);
+    default: return launch_merge_t<kBf16, 32>(fp, segs, s);
+  }
+}
+
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 }  // namespace
@@ -993,6 +1119,8 @@ extern "C" int inferd_paged_attention(void* out, const void* query, const void* 
     fp.part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + wl.ml);
     fp.part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + wl.o);
     fp.error_word = error_word;
+    // Several n-tiles: merge the cut segments in a second, fully parallel kernel
+    fp.defer_merge = nqp > 8 ? 1 : 0;
     // grid: persistent, but no more CTAs than pages can feed (upper bound from the host)
     const int64_t pages_ub = static_cast<int64_t>(nb) * num_kv_heads *
                              ((static_cast<int64_t>(max_context_len) + kPage - 1) / kPage);
@@ -1003,6 +1131,11 @@ extern "C" int inferd_paged_attention(void* out, const void* query, const void* 
     st = dtype == INFERD_BF16 ? launch_fast<true>(km, vm, fp, nqp / 8, g, smem, s)
                               : launch_fast<false>(km, vm, fp, nqp / 8, g, smem, s);
     if (st != INFERD_OK) return st;
+    if (fp.defer_merge) {
+      st = dtype == INFERD_BF16 ? launch_merge<true>(fp, nqp / 8, nb * num_kv_heads, s)
+                                : launch_merge<false>(fp, nqp / 8, nb * num_kv_heads, s);
+      if (st != INFERD_OK) return st;
+    }
   }
   return INFERD_OK;
 }

@@ -272,6 +272,17 @@ def test_verify_config3_shape(cuda_device):
     assert_bf16_close(out, ref, "verify config-3 shape")
 
 
+@pytest.mark.parametrize("q_len", [5, 8])
+def test_verify_single_long_sequence_many_pieces(cuda_device, q_len):
+    # one 20k-key sequence over all warps: each kv head's segment is cut into ~150 pieces,
+    # more than one 32-piece chunk of the merge kernel; repeated calls are bitwise identical
+    # (the cut markers are cleared by every call)
+    out, ref = run_batched(cuda_device, [20000], q_len, 32, 8, torch.bfloat16, seed=50 + q_len)
+    assert_bf16_close(out, ref, f"long verify q_len {q_len}")
+    out2, _ = run_batched(cuda_device, [20000], q_len, 32, 8, torch.bfloat16, seed=50 + q_len)
+    assert np.array_equal(out, out2)
+
+
 @pytest.mark.parametrize("q_len", [2, 3, 4, 8])
 def test_verify_window_sizes(cuda_device, q_len):
     lens = [q_len, q_len + 1, 17, 40, 513]
