@@ -17,8 +17,10 @@
 //   block-level barrier after set-up.
 //
 //   A (sequence, kv head) segment that lies inside one warp's range is normalised and
-//   stored directly.  A segment cut by warp ranges gets one partial (m, l, O) per warp;
-//   the warp that finishes the segment last (atomic ticket, no spinning) merges them.
+//   stored directly.  A segment cut by warp ranges gets one partial (m, l, O) per warp.
+//   With one n-tile (decode) the warp that finishes the segment last (atomic ticket, no
+//   spinning) merges them; with several (verify windows) merge_cut_segments_kernel, launched
+//   right after, merges every cut segment in parallel.
 //
 // Generic path (fp32 and any other size): one CTA per (sequence, query row), fp32 CUDA
 // core arithmetic.  Used for fp32 pools and small head dims such as the reference's
