@@ -345,7 +345,8 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
     const int u_last = unit_of(seg_end - 1, T_pages, U);
     if (p.defer_merge) {
       // partials only: merge_cut_segments_kernel merges every cut segment after this grid.
-      // Every piece of the segment stores the same marker (piece count, first unit).
+      // Every piece of the segment stores the same marker (piece count, first unit); both
+      // fit (the host keeps the grid below 2048 warps).
       if (lane == 0) p.counters[seg_id] = ((u_last - u_first + 1) << 20) | u_first;
       return;
     }
@@ -1086,6 +1087,8 @@ extern "C" int inferd_paged_attention(void* out, const void* query, const void* 
 
   const int nqp = nq_pad(nq);
   const int grid = fast_grid(current_sm_count());
+  // the cut-segment marker of the merge kernel packs a piece count below 2^11
+  if (nqp > 8 && grid * kWarps >= (1 << 11)) return INFERD_ERR_UNSUPPORTED;
   const int chunk_max = kMaxSeqsFast;
   const WorkspaceLayout wl = workspace_layout(num_seqs < chunk_max ? num_seqs : chunk_max,
                                               num_kv_heads, nqp, grid);
