@@ -123,6 +123,10 @@ INFERD_API int inferd_gather_paged_kv(void* key_out, void* value_out,
  * left zero by every completed call -- zero the region once when the workspace is
  * allocated and it can be shared by calls of any shape.  Calls that share a workspace
  * must be ordered on one stream.
+ * A call with q_len * (num_q_heads / num_kv_heads) > 8 enqueues two kernels on `stream`:
+ * the paged attention kernel, and a kernel that merges the sequences it split across
+ * warps (launched with programmatic stream serialization; both are captured together by
+ * a CUDA graph).
  */
 INFERD_API int inferd_paged_attention(void* out, const void* query,
                            const void* key_cache, const void* value_cache,
