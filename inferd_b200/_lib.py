@@ -158,6 +158,14 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
     return dev
 
 
+def check_out(out: torch.Tensor, device: torch.device, what: str) -> None:
+    """An output tensor the kernels write through its raw pointer must be on the inputs'
+    CUDA device: a host tensor (pinned or not) or another GPU's would hand the kernel an
+    address it must not write."""
+    if out.device != device:
+        raise ValueError(f"{what}: out is on {out.device}, the inputs on {device}")
+
+
 def stream_of(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 

@@ -139,6 +139,14 @@ def _linear_args(x, w_e4m3, w_scale, packed_shape, name):
     return dev, x2, n, k, layout
 
 
+def _out_view(out: torch.Tensor, dev: torch.device, m: int, n: int, what: str) -> torch.Tensor:
+    """out as the kernel's [m, n] bf16 output: contiguous, bf16, m * n elements, on dev."""
+    _lib.check_out(out, dev, what)
+    if out.dtype != torch.bfloat16 or out.numel() != m * n or not out.is_contiguous():
+        raise ValueError(f"{what}: out must be a contiguous bf16 tensor of {m} x {n} elements")
+    return out.view(m, n)
+
+
 def fp8_dynamic_linear(x: torch.Tensor, w_e4m3: torch.Tensor, w_scale: torch.Tensor,
                        bias: torch.Tensor | None = None, *, granularity: str = "tensor",
                        out: torch.Tensor | None = None,
@@ -150,7 +158,7 @@ def fp8_dynamic_linear(x: torch.Tensor, w_e4m3: torch.Tensor, w_scale: torch.Ten
     g = _granularity(granularity)
     dev, x2, n, k, layout = _linear_args(x, w_e4m3, w_scale, packed_shape, "fp8_dynamic_linear")
     m = x2.shape[0]
-    y = torch.empty((m, n), dtype=torch.bfloat16, device=dev) if out is None else out.view(m, n)
+    y = torch.empty((m, n), dtype=torch.bfloat16, device=dev) if out is None else _out_view(out, dev, m, n, "fp8_dynamic_linear")
     if m:
         lib = _lib.load()
         ws = _workspace(dev, lib.inferd_fp8_linear_workspace_bytes(m, n, k, dev.index or 0))
@@ -176,7 +184,7 @@ def fp8_linear(x: torch.Tensor, w_e4m3: torch.Tensor, w_scale: torch.Tensor,
     if out is None:
         y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
     else:
-        y = out.view(m, n)
+        y = _out_view(out, dev, m, n, "fp8_linear")
     if m:
         lib = _lib.load()
         ws_bytes = lib.inferd_fp8_linear_workspace_bytes(m, n, k, dev.index or 0)

@@ -263,6 +263,8 @@ def paged_attention_batched(
         out = torch.empty_like(q)
     elif out.shape != q.shape or out.dtype != q.dtype or not out.is_contiguous():
         raise ValueError("out must be a contiguous tensor shaped and typed like query")
+    else:
+        _lib.check_out(out, dev, "paged_attention")
     if b == 0:
         return out
     kc, vc = _contig(key_cache), _contig(value_cache)

@@ -156,3 +156,20 @@ def test_fp8_linear_ragged_shapes(cuda_device, n, k):
             rows = slice(0, n) if n <= 2048 else slice(n - 1536, n)
             ref = oracle.fp8_linear(x.float().numpy(), q.view(torch.uint8).cpu().numpy()[rows], s.cpu().numpy()[rows])
             assert_linear_close(y.float().cpu().numpy()[:, rows], ref, f"n={n} k={k} m={m} packed={packed}")
+
+
+def test_fp8_linear_out_must_be_on_device(cuda_device):
+    # the GEMM writes `out` through its raw pointer: host tensors and wrong dtypes or sizes
+    # are refused before anything is launched
+    w = torch.zeros(384, 512, dtype=torch.bfloat16, device=cuda_device)
+    q, s = quantize_fp8_per_channel(w)
+    x = torch.zeros(2, 512, dtype=torch.bfloat16, device=cuda_device)
+    bad = [torch.empty(2, 384, dtype=torch.bfloat16),
+           torch.empty(2, 384, dtype=torch.bfloat16, pin_memory=True),
+           torch.empty(2, 384, dtype=torch.float32, device=cuda_device),
+           torch.empty(2, 383, dtype=torch.bfloat16, device=cuda_device)]
+    for out in bad:
+        with pytest.raises(ValueError):
+            fp8_linear(x, q, s, out=out)
+    good = torch.empty(2, 384, dtype=torch.bfloat16, device=cuda_device)
+    assert fp8_linear(x, q, s, out=good).data_ptr() == good.data_ptr()

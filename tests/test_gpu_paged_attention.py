@@ -234,6 +234,19 @@ def test_argument_errors_match_reference(cuda_device):
         paged_attention(q[:30], kb, kb, torch.tensor([0]), 1)       # 30 % 8 != 0
 
 
+def test_out_off_device_is_rejected(cuda_device):
+    # the kernel writes `out` through its raw pointer: a host tensor, even pinned, is refused
+    # before anything is launched
+    kb = torch.zeros(4, 2, 16, 128, dtype=torch.bfloat16, device=cuda_device)
+    q = torch.zeros(1, 1, 8, 128, dtype=torch.bfloat16, device=cuda_device)
+    bt = torch.zeros(1, 1, dtype=torch.int32, device=cuda_device)
+    cl = torch.ones(1, dtype=torch.int32, device=cuda_device)
+    for out in (torch.empty(1, 1, 8, 128, dtype=torch.bfloat16),
+                torch.empty(1, 1, 8, 128, dtype=torch.bfloat16, pin_memory=True)):
+        with pytest.raises(ValueError):
+            paged_attention_batched(q, kb, kb, bt, cl, out=out)
+
+
 # ------------------------------------------------------------- verify (q_len > 1)
 @pytest.mark.parametrize("case", range(4))
 def test_verify_matches_hf_eager_golden(cuda_device, golden, case):
