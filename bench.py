@@ -373,6 +373,7 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
     stream = torch.cuda.current_stream(device)
     steps = max(1, min(args.steps, args.e2e_steps))
     d2h = out_rows * ql * HQ * D * ELEM
+    keep_one = [1] * len(ids)
 
     def one_step():
         graph.launch()
@@ -384,7 +385,7 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
         stream.synchronize()
         if ql > 1:
             # speculative verify: keep one accepted token, roll the rest of the window back
-            cache.truncate_batched(ids, [cache.sequence_length(i) - ql + 1 for i in ids])
+            graph.rollback(keep_one)
             graph.prepare()
 
     graph.prepare()

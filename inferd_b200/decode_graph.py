@@ -24,7 +24,8 @@ next step can be prepared while the current one runs.
     out = g.result()                                     # pinned [B, q_len, Hq, D]
 
 While a DecodeGraph drives a batch, its sequences change only through prepare/launch and
-PagedKVCache.truncate_batched / truncate_sequence (the rollback of a verify window); other
+DecodeGraph.rollback or PagedKVCache.truncate_batched / truncate_sequence (the rollback of a
+verify window); other
 page-table consumers (decode_metadata, plan_append) must not run on the same sequences.
 A table that outgrows the captured capacity, or a step with more table changes than the
 staging holds, is handled by re-uploading the table (and re-capturing when the capacity
@@ -242,6 +243,30 @@ class DecodeGraph:
         self._prepared = None
         self._last = i
         self._set = i ^ 1
+
+    def rollback(self, keep) -> list[int]:
+        """Roll back the verify window of the last launched step: sequence i keeps the first
+        keep[i] (0 .. q_len) tokens of the window and releases the rest, with any pages only
+        they used (PagedKVCache.truncate_batched on this graph's sequences, without the
+        per-sequence lookups).  Call it between launch() and the next prepare(); the pages
+        it frees are reused only by later steps, which the stream orders after this one.
+        Returns the freed blocks."""
+        if self._prepared is not None:
+            raise RuntimeError("rollback() comes before prepare()")
+        if self._last is None:
+            raise RuntimeError("no step has been launched")
+        if len(keep) != len(self.tables):
+            raise ValueError("one keep count per sequence")
+        ql = self.q_len
+        lengths = []
+        for t, k in zip(self.tables, keep):
+            k = int(k)
+            if k < 0 or k > ql:
+                raise ValueError(f"keep counts lie in 0 .. {ql}")
+            lengths.append(t.length - ql + k)
+        cache = self.cache
+        return _hostops.truncate(self.tables, lengths, cache.block_size, cache.allocator._free,
+                                 cache.allocator._allocated)
 
     def abort(self) -> None:
         """Release the pages of a prepared step that will not be launched."""

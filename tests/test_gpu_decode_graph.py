@@ -68,12 +68,37 @@ def test_graph_steps_equal_eager_steps(cuda_device, q_len):
         assert torch.equal(out_g, out_e), f"step {step}"
         assert [a.sequence_length(s) for s in ids] == [b.sequence_length(s) for s in ids]
         if q_len > 1:  # verify: keep 1..q_len tokens of the window, roll the rest back
-            keep = [a.sequence_length(s) - q_len + int(rng.integers(1, q_len + 1)) for s in ids]
-            a.truncate_batched(ids, keep)
-            b.truncate_batched(ids, keep)
+            accepted = [int(rng.integers(1, q_len + 1)) for _ in ids]
+            if step % 2:
+                graph.rollback(accepted)
+            else:
+                a.truncate_batched(ids, [a.sequence_length(s) - q_len + k for s, k in zip(ids, accepted)])
+            b.truncate_batched(ids, [b.sequence_length(s) - q_len + k for s, k in zip(ids, accepted)])
     assert [a.sequences[s].blocks for s in ids] == [b.sequences[s].blocks for s in ids]
     assert torch.equal(a.key_cache[0], b.key_cache[0]) and torch.equal(a.value_cache[0], b.value_cache[0])
     assert len(caps) > 1, "the capacity never grew: the re-capture path was not exercised"
+
+
+def test_rollback_argument_checks(cuda_device):
+    (a, _), g = _twin_caches(cuda_device, [30, 31])
+    graph = DecodeGraph(a, [0, 1], num_q_heads=HQ, q_len=3)
+    with pytest.raises(RuntimeError):
+        graph.rollback([1, 1])  # nothing launched yet
+    graph.prepare()
+    graph.launch()
+    torch.cuda.synchronize()
+    with pytest.raises(ValueError):
+        graph.rollback([1])  # one count per sequence
+    with pytest.raises(ValueError):
+        graph.rollback([4, 1])  # more than the window
+    assert [a.sequence_length(s) for s in (0, 1)] == [33, 34]
+    graph.rollback([0, 3])
+    assert [a.sequence_length(s) for s in (0, 1)] == [30, 34]
+    graph.prepare()
+    with pytest.raises(RuntimeError):
+        graph.rollback([1, 1])  # a step is prepared
+    graph.abort()
+    a.assert_consistent()
 
 
 def test_abort_and_exhausted_pool(cuda_device):
