@@ -27,6 +27,11 @@
 //     and (column, 0) for pages it lost; row i's count goes to out[i] (int32).  Resets
 //     dirty_from.  Returns the flat pair list (int32 buffer bytes) and the current list ids
 //     and lengths.
+//   pack_staged(tables, prev_ids, prev_nblk, clean, row_ptr, pairs_out) -> (total, ids, nblk)
+//     pack_changes written straight into staging: row_ptr[0 .. n] (int32) the exclusive
+//     prefix of the per-row pair counts, pairs_out (int32) the flat (column, block) pairs
+//     while they fit.  total is the number of pairs; above pairs_out's capacity the caller
+//     sends whole tables instead (the pairs past the capacity are counted, not written).
 #define PY_SSIZE_T_CLEAN
 #include <Python.h>
 
@@ -243,6 +248,75 @@ error:
   return nullptr;
 }
 
+// Walk the tables for pack_changes / pack_staged: emit(row, column, block) for every changed
+// entry, counts[row] = the row's pair count; resets dirty_from.  Fills ids / nblk (new
+// references) with the current list ids and lengths.
+template <typename Emit>
+bool walk_changes(PyObject* tables, PyObject* prev_ids, PyObject* prev_nblk, long long clean,
+                  int32_t* counts, PyObject* ids, PyObject* nblk, Emit emit) {
+  const Py_ssize_t n = PyList_GET_SIZE(tables);
+  for (Py_ssize_t i = 0; i < n; ++i) {
+    PyObject* t = PyList_GET_ITEM(tables, i);
+    PyObject* blocks = PyObject_GetAttr(t, s_blocks);
+    if (!blocks) return false;
+    if (!PyList_Check(blocks)) {
+      Py_DECREF(blocks);
+      PyErr_SetString(PyExc_TypeError, "page table blocks must be a list");
+      return false;
+    }
+    const Py_ssize_t nb = PyList_GET_SIZE(blocks);
+    PyObject* id = PyLong_FromVoidPtr(blocks);
+    PyObject* nbo = PyLong_FromSsize_t(nb);
+    if (!id || !nbo) {
+      Py_XDECREF(id);
+      Py_XDECREF(nbo);
+      Py_DECREF(blocks);
+      return false;
+    }
+    PyList_SET_ITEM(ids, i, id);
+    PyList_SET_ITEM(nblk, i, nbo);
+    long long dirty;
+    if (!get_long(t, s_dirty, &dirty)) {
+      Py_DECREF(blocks);
+      return false;
+    }
+    const int same = PyObject_RichCompareBool(id, PyList_GET_ITEM(prev_ids, i), Py_EQ);
+    if (same < 0) {
+      Py_DECREF(blocks);
+      return false;
+    }
+    const long long start = same ? dirty : 0;
+    int32_t count = 0;
+    if (start != clean) {
+      const long long old = PyLong_AsLongLong(PyList_GET_ITEM(prev_nblk, i));
+      if (old == -1 && PyErr_Occurred()) {
+        Py_DECREF(blocks);
+        return false;
+      }
+      for (long long c = start; c < nb; ++c) {
+        const long long b = PyLong_AsLongLong(PyList_GET_ITEM(blocks, static_cast<Py_ssize_t>(c)));
+        if (b == -1 && PyErr_Occurred()) {
+          Py_DECREF(blocks);
+          return false;
+        }
+        emit(static_cast<int32_t>(c), static_cast<int32_t>(b));
+        ++count;
+      }
+      for (long long c = (nb > start ? nb : start); c < old; ++c) {
+        emit(static_cast<int32_t>(c), 0);
+        ++count;
+      }
+      if (!set_long(t, s_dirty, clean)) {
+        Py_DECREF(blocks);
+        return false;
+      }
+    }
+    counts[i] = count;
+    Py_DECREF(blocks);
+  }
+  return true;
+}
+
 PyObject* pack_changes(PyObject*, PyObject* args) {
   PyObject *tables, *prev_ids, *prev_nblk, *out_obj;
   long long clean;
@@ -256,86 +330,75 @@ PyObject* pack_changes(PyObject*, PyObject* args) {
   }
   Py_buffer view;
   if (!get_buffer(out_obj, &view, static_cast<Py_ssize_t>(n * 4))) return nullptr;
-  int32_t* counts = static_cast<int32_t*>(view.buf);
   std::vector<int32_t> pairs;
   PyObject* ids = PyList_New(n);
   PyObject* nblk = PyList_New(n);
-  if (!ids || !nblk) goto error;
-  for (Py_ssize_t i = 0; i < n; ++i) {
-    PyObject* t = PyList_GET_ITEM(tables, i);
-    PyObject* blocks = PyObject_GetAttr(t, s_blocks);
-    if (!blocks) goto error;
-    if (!PyList_Check(blocks)) {
-      Py_DECREF(blocks);
-      PyErr_SetString(PyExc_TypeError, "page table blocks must be a list");
-      goto error;
-    }
-    const Py_ssize_t nb = PyList_GET_SIZE(blocks);
-    PyObject* id = PyLong_FromVoidPtr(blocks);
-    PyObject* nbo = PyLong_FromSsize_t(nb);
-    if (!id || !nbo) {
-      Py_XDECREF(id);
-      Py_XDECREF(nbo);
-      Py_DECREF(blocks);
-      goto error;
-    }
-    PyList_SET_ITEM(ids, i, id);
-    PyList_SET_ITEM(nblk, i, nbo);
-    long long dirty;
-    if (!get_long(t, s_dirty, &dirty)) {
-      Py_DECREF(blocks);
-      goto error;
-    }
-    const int same = PyObject_RichCompareBool(id, PyList_GET_ITEM(prev_ids, i), Py_EQ);
-    if (same < 0) {
-      Py_DECREF(blocks);
-      goto error;
-    }
-    long long start = same ? dirty : 0;
-    const size_t before = pairs.size();
-    if (start != clean) {
-      const long long old = PyLong_AsLongLong(PyList_GET_ITEM(prev_nblk, i));
-      if (old == -1 && PyErr_Occurred()) {
-        Py_DECREF(blocks);
-        goto error;
-      }
-      for (long long c = start; c < nb; ++c) {
-        const long long b = PyLong_AsLongLong(PyList_GET_ITEM(blocks, static_cast<Py_ssize_t>(c)));
-        if (b == -1 && PyErr_Occurred()) {
-          Py_DECREF(blocks);
-          goto error;
-        }
-        pairs.push_back(static_cast<int32_t>(c));
-        pairs.push_back(static_cast<int32_t>(b));
-      }
-      for (long long c = (nb > start ? nb : start); c < old; ++c) {
-        pairs.push_back(static_cast<int32_t>(c));
-        pairs.push_back(0);
-      }
-      if (!set_long(t, s_dirty, clean)) {
-        Py_DECREF(blocks);
-        goto error;
-      }
-    }
-    counts[i] = static_cast<int32_t>((pairs.size() - before) / 2);
-    Py_DECREF(blocks);
+  if (!ids || !nblk ||
+      !walk_changes(tables, prev_ids, prev_nblk, clean, static_cast<int32_t*>(view.buf), ids, nblk,
+                    [&](int32_t c, int32_t b) {
+                      pairs.push_back(c);
+                      pairs.push_back(b);
+                    })) {
+    PyBuffer_Release(&view);
+    Py_XDECREF(ids);
+    Py_XDECREF(nblk);
+    return nullptr;
   }
   PyBuffer_Release(&view);
-  {
-    PyObject* pb = PyBytes_FromStringAndSize(reinterpret_cast<const char*>(pairs.data()),
-                                             static_cast<Py_ssize_t>(pairs.size() * sizeof(int32_t)));
-    if (!pb) {
-      Py_DECREF(ids);
-      Py_DECREF(nblk);
-      return nullptr;
-    }
-    return Py_BuildValue("(NNN)", pb, ids, nblk);
+  PyObject* pb = PyBytes_FromStringAndSize(reinterpret_cast<const char*>(pairs.data()),
+                                           static_cast<Py_ssize_t>(pairs.size() * sizeof(int32_t)));
+  if (!pb) {
+    Py_DECREF(ids);
+    Py_DECREF(nblk);
+    return nullptr;
   }
-error:
-  PyBuffer_Release(&view);
-  Py_XDECREF(ids);
-  Py_XDECREF(nblk);
-  return nullptr;
+  return Py_BuildValue("(NNN)", pb, ids, nblk);
+}
+
+PyObject* pack_staged(PyObject*, PyObject* args) {
+  PyObject *tables, *prev_ids, *prev_nblk, *rp_obj, *pairs_obj;
+  long long clean;
+  if (!PyArg_ParseTuple(args, "O!O!O!LOO", &PyList_Type, &tables, &PyList_Type, &prev_ids, &PyList_Type,
+                        &prev_nblk, &clean, &rp_obj, &pairs_obj))
+    return nullptr;
+  const Py_ssize_t n = PyList_GET_SIZE(tables);
+  if (PyList_GET_SIZE(prev_ids) != n || PyList_GET_SIZE(prev_nblk) != n) {
+    PyErr_SetString(PyExc_ValueError, "previous batch state does not match the tables");
+    return nullptr;
+  }
+  Py_buffer rp_view, pv;
+  if (!get_buffer(rp_obj, &rp_view, static_cast<Py_ssize_t>((n + 1) * 4))) return nullptr;
+  if (!get_buffer(pairs_obj, &pv, 0)) {
+    PyBuffer_Release(&rp_view);
+    return nullptr;
+  }
+  int32_t* row_ptr = static_cast<int32_t*>(rp_view.buf);
+  int32_t* out = static_cast<int32_t*>(pv.buf);
+  const long long cap = static_cast<long long>(pv.len / 8);  // pairs that fit
+  long long total = 0;
+  PyObject* ids = PyList_New(n);
+  PyObject* nblk = PyList_New(n);
+  const bool ok = ids && nblk &&
+                  walk_changes(tables, prev_ids, prev_nblk, clean, row_ptr + 1, ids, nblk,
+                               [&](int32_t c, int32_t b) {
+                                 if (total < cap) {
+                                   out[2 * total] = c;
+                                   out[2 * total + 1] = b;
+                                 }
+                                 ++total;
+                               });
+  if (ok) {  // counts -> exclusive prefix
+    row_ptr[0] = 0;
+    for (Py_ssize_t i = 0; i < n; ++i) row_ptr[i + 1] += row_ptr[i];
+  }
+  PyBuffer_Release(&rp_view);
+  PyBuffer_Release(&pv);
+  if (!ok) {
+    Py_XDECREF(ids);
+    Py_XDECREF(nblk);
+    return nullptr;
+  }
+  return Py_BuildValue("(LNN)", total, ids, nblk);
 }
 
 // scan(tables, extra, lens_out) -> (nblk, width, max_len): lens_out[i] = length + extra
@@ -387,6 +450,7 @@ PyMethodDef kMethods[] = {
     {"advance", advance, METH_VARARGS, "advance every table's length"},
     {"truncate", truncate, METH_VARARGS, "batched truncation returning the freed blocks"},
     {"pack_changes", pack_changes, METH_VARARGS, "sparse page-table changes since the last call"},
+    {"pack_staged", pack_staged, METH_VARARGS, "pack_changes written straight into staging buffers"},
     {nullptr, nullptr, 0, nullptr}};
 
 PyModuleDef kModule = {PyModuleDef_HEAD_INIT, "_hostops", "Page-table loops of the decode path.", -1, kMethods};

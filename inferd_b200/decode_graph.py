@@ -211,17 +211,14 @@ class DecodeGraph:
             self._rebuild_for(width, i)
             slots[:] = saved_slots
             meta[:b] = saved_lens
-        meta[b] = 0
-        pairs, ids, _ = _hostops.pack_changes(self.tables, self._prev_ids, self._prev_nblk, _CLEAN,
-                                              meta[b + 1:2 * b + 1])
-        np.cumsum(meta[b + 1:2 * b + 1], out=meta[b + 1:2 * b + 1])
-        pair_np = np.frombuffer(pairs, dtype=np.int32)
-        if pair_np.size > 2 * self._max_pairs:
+        # row offsets and (column, block) pairs of the table changes, written in place
+        total, ids, _ = _hostops.pack_staged(self.tables, self._prev_ids, self._prev_nblk, _CLEAN,
+                                             meta[b:2 * b + 1], meta[2 * b + 1:])
+        if total > self._max_pairs:
             # more changes than the staging holds: send the whole table before the replay
             meta[b:2 * b + 1] = 0
             self._upload_dense()
         else:
-            meta[2 * b + 1:2 * b + 1 + pair_np.size] = pair_np
             self._prev_ids, self._prev_nblk = ids, nblk
         self._prepared = (i, reserved)
 

@@ -386,3 +386,61 @@ def test_native_page_table_loops_match_python():
         caches[native].assert_consistent()
     with pytest.raises(ValueError):
         run(True, lambda c: c.truncate_batched(ids, [10 ** 6] * 4))
+
+
+def test_pack_staged_matches_pack_changes():
+    # DecodeGraph's staging path: pack_staged writes the exclusive row offsets and the
+    # (column, block) pairs in place; it must equal pack_changes + a prefix sum, and past
+    # the pairs buffer's capacity it counts without writing
+    from inferd_b200.paged_cache import _CLEAN, _hostops
+    if _hostops is None:
+        pytest.skip("_hostops not built")
+    rng = np.random.default_rng(23)
+
+    def make():
+        tabs = []
+        for s in range(6):
+            t = SequencePageTable(seq_id=s, block_size=4)
+            t.blocks = [int(x) for x in rng.integers(0, 1000, int(rng.integers(0, 9)))]
+            t.length = 4 * len(t.blocks)
+            t.dirty_from = _CLEAN
+            tabs.append(t)
+        return tabs
+
+    a = make()
+    b = [SequencePageTable(seq_id=t.seq_id, block_size=4, blocks=list(t.blocks), length=t.length) for t in a]
+    for t in b:
+        t.dirty_from = _CLEAN
+    prev_a = ([id(t.blocks) for t in a], [len(t.blocks) for t in a])
+    prev_b = ([id(t.blocks) for t in b], [len(t.blocks) for t in b])
+    for step in range(200):
+        for ta, tb in zip(a, b):  # the same random tail edits on both sets
+            r = rng.random()
+            if r < 0.3:
+                new = [int(x) for x in rng.integers(0, 1000, int(rng.integers(1, 4)))]
+                for t in (ta, tb):
+                    t.dirty_from = min(t.dirty_from, len(t.blocks))
+                    t.blocks.extend(new)
+            elif r < 0.5 and ta.blocks:
+                keep = int(rng.integers(0, len(ta.blocks)))
+                for t in (ta, tb):
+                    del t.blocks[keep:]
+                    t.dirty_from = min(t.dirty_from, keep)
+            elif r < 0.55:
+                ta.blocks = list(ta.blocks)  # a list replaced from outside
+                tb.blocks = list(tb.blocks)
+        counts = np.zeros(len(a), dtype=np.int32)
+        pairs, ids_a, nb_a = _hostops.pack_changes(a, prev_a[0], prev_a[1], _CLEAN, counts)
+        want_pairs = np.frombuffer(pairs, dtype=np.int32)
+        want_rp = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+        cap = int(rng.choice([0, 3, 1000]))
+        rp = np.full(len(b) + 1, -7, dtype=np.int32)
+        buf = np.full(2 * cap, -7, dtype=np.int32)
+        total, ids_b, nb_b = _hostops.pack_staged(b, prev_b[0], prev_b[1], _CLEAN, rp, buf)
+        assert total == want_pairs.size // 2
+        assert np.array_equal(rp, want_rp)
+        n_written = min(total, cap)
+        assert np.array_equal(buf[:2 * n_written], want_pairs[:2 * n_written])
+        assert np.all(buf[2 * n_written:] == -7)
+        assert nb_a == nb_b and [t.dirty_from for t in a] == [t.dirty_from for t in b] == [_CLEAN] * len(a)
+        prev_a, prev_b = (ids_a, nb_a), (ids_b, nb_b)
