@@ -48,10 +48,15 @@ HQ, HKV, D, BS = 32, 8, 128, 16
 ELEM = 2  # bf16
 
 WORKLOADS = {
-    "decode": dict(seqs=64, lo=512, hi=8192, q_len=1, config_index=1),
-    "long": dict(seqs=32, lo=16384, hi=32768, q_len=1, config_index=4),
-    "verify": dict(seqs=32, lo=1024, hi=4096, q_len=5, config_index=2),
+    "decode": dict(seqs=64, lo=512, hi=8192, q_len=1,
+                   label="config 2: batched paged decode"),
+    "long": dict(seqs=32, lo=16384, hi=32768, q_len=1,
+                 label="config 5: long-context sharded decode"),
+    "verify": dict(seqs=32, lo=1024, hi=4096, q_len=5,
+                   label="config 3: speculative verify"),
 }
+E2E_STEPS = 200            # default number of end-to-end steps
+POOL_GROWTH = E2E_STEPS + 64  # spare tokens per sequence in the pool for the e2e steps
 
 
 # ------------------------------------------------------------------ workload
@@ -147,11 +152,15 @@ def ncu_traffic(workload: str) -> float | None:
 
 # ------------------------------------------------------------------ our arm
 class DeviceWorkload:
-    """One rank's share of the workload, resident on its GPU."""
+    """One rank's share of the workload, resident on its GPU.  The data depend only on
+    (workload, rank, world, growth_tokens); with the default growth they are the bytes the
+    benchmark times, so tests can rebuild them and check the kernels' outputs."""
 
     def __init__(self, workload: str, rank: int, world: int, device: torch.device,
-                 growth_tokens: int = 0) -> None:
+                 growth_tokens: int = POOL_GROWTH) -> None:
         w = WORKLOADS[workload]
+        self.workload = workload
+        self.device = device
         self.q_len = w["q_len"]
         from inferd_b200.sharded import shard_range
 
@@ -196,42 +205,69 @@ class DeviceWorkload:
         self.max_ctx = int(self.ctx.max())
         self.bytes = step_bytes(self.ctx, self.q_len)
 
+    def append(self) -> None:
+        """The step's KV append: one reshape_and_cache launch through the C ABI."""
+        from inferd_b200 import _lib
+
+        lib = _lib.load()
+        st = lib.inferd_reshape_and_cache(
+            self.k_new.data_ptr(), self.v_new.data_ptr(), self.k_new.stride(0),
+            self.k_new.stride(1), self.v_new.stride(0), self.v_new.stride(1),
+            self.kc.data_ptr(), self.vc.data_ptr(), self.slots.data_ptr(), self.slots.numel(),
+            HKV, D, BS, self.num_blocks, 2, _lib.error_word(self.device).data_ptr(),
+            torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(st, "reshape_and_cache")
+
+    def attend(self) -> None:
+        """The step's paged attention over every sequence, into self.out."""
+        from inferd_b200.paged_attn import paged_attention_batched
+
+        paged_attention_batched(self.q, self.kc, self.vc, self.bt, self.cl,
+                                max_context_len=self.max_ctx, out=self.out)
+
+    def sequence_pages(self, i: int) -> tuple[np.ndarray, np.ndarray]:
+        """Sequence i's K and V pages, read back from the pool in table order as float32
+        [pages, kv_heads, block_size, head_dim] (a compact pool whose table is arange)."""
+        p = int((self.ctx[i] + BS - 1) // BS)
+        ids = self.bt[i, :p].long()
+        return (self.kc[ids].float().cpu().numpy(), self.vc[ids].float().cpu().numpy())
+
+    def appended_bit_exact(self) -> bool:
+        """The pool holds the step's new K/V bit for bit at every appended slot."""
+        s = self.slots.long()
+        blk, off = s // BS, s % BS
+        return bool(torch.equal(self.kc[blk, :, off, :], self.k_new)
+                    and torch.equal(self.vc[blk, :, off, :], self.v_new))
+
 
 def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     import torch.distributed as dist
 
     from inferd_b200 import _lib
-    from inferd_b200.paged_attn import paged_attention_batched
-    from inferd_b200.sharded import gather_outputs
+    from inferd_b200.sharded import OutputGather
 
-    lib = _lib.load()
-    wl = DeviceWorkload(args.workload, rank, world, device, growth_tokens=args.e2e_steps + 64)
+    wl = DeviceWorkload(args.workload, rank, world, device,
+                        growth_tokens=args.e2e_steps + POOL_GROWTH - E2E_STEPS)
+    gather = None
+    if world > 1:
+        # The step's kernels run on a high-priority stream and the all-gather of step N's
+        # outputs (NCCL's own stream, normal priority) overlaps step N + 1: its CTAs take
+        # the SMs the attention kernel's tail frees instead of delaying the kernel's start.
+        torch.cuda.set_stream(torch.cuda.Stream(device, priority=-1))
+        gather = OutputGather(tuple(wl.out.shape[1:]), wl.out.dtype, device, [wl.b] * world)
     stream = torch.cuda.current_stream(device)
-    err = _lib.error_word(device)
-    gathered = torch.empty((world * wl.b,) + tuple(wl.out.shape[1:]), dtype=wl.out.dtype,
-                           device=device) if world > 1 else None
-
-    def append():
-        st = lib.inferd_reshape_and_cache(
-            wl.k_new.data_ptr(), wl.v_new.data_ptr(), wl.k_new.stride(0), wl.k_new.stride(1),
-            wl.v_new.stride(0), wl.v_new.stride(1), wl.kc.data_ptr(), wl.vc.data_ptr(),
-            wl.slots.data_ptr(), wl.slots.numel(), HKV, D, BS, wl.num_blocks, 2,
-            err.data_ptr(), stream.cuda_stream)
-        _lib.check(st, "reshape_and_cache")
-
-    def attend():
-        paged_attention_batched(wl.q, wl.kc, wl.vc, wl.bt, wl.cl, max_context_len=wl.max_ctx,
-                                out=wl.out)
 
     def step(ev=None):
-        append()
+        wl.append()
         if ev is not None:
             ev[0].record(stream)
-        attend()
+        if gather is not None:
+            wl.out = gather.local()  # double-buffered: the gather of step N - 1 may still read
+        wl.attend()
         if ev is not None:
             ev[1].record(stream)
-        if gathered is not None:
-            gather_outputs(wl.out, out=gathered)
+        if gather is not None:
+            gather.start()
 
     for _ in range(args.warmup):
         step()
@@ -252,6 +288,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     t0.record(stream)
     for i in range(k):
         step(attn_ev[i])
+    if gather is not None:
+        gather.wait_all()  # the last steps' all-gathers belong to the timed region
     t1.record(stream)
     torch.cuda.synchronize(device)
     clocks = sampler.stop()
@@ -277,6 +315,36 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     ms_per_step = elapsed_ms / k
     value_gbs = total_bytes / (ms_per_step * 1e-3) / 1e9
 
+    # checks of the last timed step, before the e2e steps reuse the pool: the append wrote
+    # its K/V bit for bit; at N > 1 every rank's rows of the gathered output equal its own
+    # output; at N = 1 the CPU leg compares every sequence's output with the oracle
+    checks = {"append_bit_exact": wl.appended_bit_exact()}
+    gather_us = None
+    if gather is not None:
+        mine = torch.equal(gather.result()[rank * wl.b:(rank + 1) * wl.b], wl.out)
+        flag = torch.tensor([int(mine and checks["append_bit_exact"])], device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        checks["gathered_rows_equal_rank_outputs"] = bool(flag.item())
+        # the all-gather alone, back to back, for the record (max over ranks)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize(device)
+        g0.record(stream)
+        for _ in range(k):
+            gather.local()
+            gather.start()
+        gather.wait_all()
+        g1.record(stream)
+        torch.cuda.synchronize(device)
+        t = torch.tensor([g0.elapsed_time(g1) * 1000.0 / k], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        gather_us = round(float(t.item()), 2)
+    parity = cpu = None
+    if world == 1:
+        parity, cpu = cpu_leg(wl, budget_s=0.0 if args.no_cpu_baseline else args.cpu_budget)
+    if not all(checks.values()) or (parity is not None and not parity["ok"]):
+        raise RuntimeError(f"output check failed: {checks} {parity}")
+
     e2e = run_e2e(args, wl, rank, world, device)
 
     if rank != 0:
@@ -298,19 +366,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) Q/K/V in bf16, seeded uniform context lengths, "
                 "randomly permuted block tables)",
-        "config": {
-            "workload": {"decode": "config 2: batched paged decode",
-                         "long": "config 5: long-context sharded decode",
-                         "verify": "config 3: speculative verify"}[args.workload],
-            "seqs_per_gpu": wl.b, "context_lo": WORKLOADS[args.workload]["lo"],
-            "context_hi": WORKLOADS[args.workload]["hi"], "q_len": wl.q_len,
-            "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "block_size": BS,
-            "pool_blocks_per_gpu": wl.num_blocks,
-            "parallelism": f"sequence shards x{world}, outputs all-gathered over NCCL"
-            if world > 1 else "single GPU",
-            "l2": "no flush: each step reads >= %.2f GB of KV per GPU (L2 is 126 MB)"
-                  % (wl.bytes["attention"] / 1e9),
-        },
+        "config": config_block(args.workload, world),
         "decode_tok_s": round(seqs * wl.q_len / (ms_per_step * 1e-3), 1),
         "attention_ms": round(attn_ms, 5),
         "attention_gbs_per_gpu": round(achieved, 1),
@@ -325,9 +381,33 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         "e2e": e2e,
         "gpu_launches": 2 * k,
     }
-    if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.workload, budget_s=args.cpu_budget)
+    line["checks"] = checks
+    if gather_us is not None:
+        line["allgather_us_alone"] = gather_us
+        line["allgather_bytes_per_rank"] = int(wl.out.numel() * wl.out.element_size())
+    if parity is not None:
+        line["parity"] = parity
+    if cpu is not None and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu
     return line
+
+
+def config_block(workload: str, world: int) -> dict:
+    """The `config` object of both arms' lines: the workload and its sizes per GPU."""
+    w = WORKLOADS[workload]
+    ctx = context_lengths(workload, world)[:w["seqs"]] + w["q_len"]
+    pages = (ctx + BS - 1) // BS
+    grow = (POOL_GROWTH + w["q_len"] + BS - 1) // BS + 1
+    attn_gb = step_bytes(ctx, w["q_len"])["attention"] / 1e9
+    return {
+        "workload": w["label"], "seqs_per_gpu": w["seqs"], "context_lo": w["lo"],
+        "context_hi": w["hi"], "q_len": w["q_len"], "q_heads": HQ, "kv_heads": HKV,
+        "head_dim": D, "block_size": BS,
+        "pool_blocks_per_gpu": int(math.ceil(1.1 * pages.sum())) + w["seqs"] * grow,
+        "parallelism": f"sequence shards x{world}, outputs all-gathered over NCCL"
+        if world > 1 else "single GPU",
+        "l2": "no flush: each step reads >= %.2f GB of KV per GPU (L2 is 126 MB)" % attn_gb,
+    }
 
 
 def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.device) -> dict:
@@ -621,22 +701,66 @@ class CpuWork:
         return step_bytes([L], self.q_len)["total"]
 
 
-def cpu_baseline(workload: str, budget_s: float = 15.0) -> dict:
-    work = CpuWork(workload)
+ATOL_BF16, RTOL_BF16 = 2e-2, 1e-2  # attention tolerance against the fp32 oracle
+
+
+def _oracle_sequence(q: np.ndarray, kp: np.ndarray, vp: np.ndarray, ctx: int) -> np.ndarray:
+    """The oracle's output for one sequence: q [q_len, Hq, D] over its compact pages
+    kp / vp [pages, Hkv, BS, D] (table = arange)."""
+    import oracle
+
+    table = np.arange(kp.shape[0])
+    if q.shape[0] == 1:
+        return oracle.paged_attention(q[0], kp, vp, table, ctx)[None]
+    k, v = oracle.gather_paged_kv(kp, vp, table, ctx)
+    return oracle.verify_attention(q, k, v)
+
+
+def cpu_leg(wl: DeviceWorkload, budget_s: float = 15.0) -> tuple[dict, dict | None]:
+    """The CPU leg at N = 1, run on the benchmarked sequences themselves (their pages read
+    back from HBM after the timed steps, bf16 widened to fp32).
+
+    parity: the oracle (numpy restatement of the reference's per-sequence gather + GQA
+    attention, causal inside a verify window) against the last timed step's output, every
+    sequence, at 2e-2 max-abs and 1e-2 relative (max-abs error over max |oracle|).
+    cpu_baseline: the same oracle timed on the host cores for about budget_s seconds,
+    cycling over the first sequences (up to 8, at most 512 MB of fp32 pages held)."""
+    out = wl.out.float().cpu().numpy()
+    q = wl.q.float().cpu().numpy()
+    worst_abs = worst_rel = 0.0
+    kept, kept_bytes = [], 0
+    for i in range(wl.b):
+        kp, vp = wl.sequence_pages(i)
+        ctx = int(wl.ctx[i])
+        ref = _oracle_sequence(q[i], kp, vp, ctx)
+        err = float(np.abs(out[i] - ref).max())
+        worst_abs = max(worst_abs, err)
+        worst_rel = max(worst_rel, err / max(float(np.abs(ref).max()), 1e-6))
+        if len(kept) < 8 and kept_bytes + kp.nbytes + vp.nbytes <= 512 << 20:
+            kept.append((q[i], kp, vp, ctx))
+            kept_bytes += kp.nbytes + vp.nbytes
+        del kp, vp
+    parity = {"ok": worst_abs <= ATOL_BF16 and worst_rel <= RTOL_BF16,
+              "max_abs_err": round(worst_abs, 6), "max_rel_err": round(worst_rel, 6),
+              "seqs_checked": wl.b, "append_checked": "bit-exact at every appended slot",
+              "tolerance": "max-abs <= 2e-2 and max-abs / max|oracle| <= 1e-2 per sequence",
+              "oracle": "numpy fp32 restatement of the reference's gather + attention"}
+    if budget_s <= 0:
+        return parity, None
     t0 = time.perf_counter()
-    done = 0
-    nbytes = 0
-    i = 0
+    done = nbytes = 0
     while time.perf_counter() - t0 < budget_s or done == 0:
-        nbytes += work.run_seq(i % work.lens.size)
+        qi, kp, vp, ctx = kept[done % len(kept)]
+        _oracle_sequence(qi, kp, vp, ctx)
+        nbytes += step_bytes([ctx], wl.q_len)["total"]
         done += 1
-        i += 1
     dt = time.perf_counter() - t0
-    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": _cpu_threads(),
-            "kind": "port",
-            "sample": f"{done} single-sequence decode steps (oracle: per-sequence gather + "
-                      f"GQA attention in numpy fp32, cycling over {work.lens.size} sequences of "
-                      f"the workload), {dt:.1f} s"}
+    cpu = {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": _cpu_threads(),
+           "kind": "port",
+           "sample": f"{done} single-sequence steps of the oracle (numpy fp32 per-sequence gather "
+                     f"+ GQA attention{', causal window' if wl.q_len > 1 else ''}) over the first "
+                     f"{len(kept)} benchmarked sequences, read back from HBM, {dt:.1f} s"}
+    return parity, cpu
 
 
 def _cpu_threads() -> int:
@@ -669,8 +793,7 @@ def run_reference(args, rank: int, world: int) -> dict | None:
         "impl": "reference", "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": args.workload, "q_heads": HQ,
-                                        "kv_heads": HKV, "head_dim": D, "block_size": BS},
+        "data": "synthetic", "config": config_block(args.workload, world),
         "cpu_baseline": {"value": v, "unit": "GB/s", "cores": _cpu_threads(), "kind": "port",
                          "sample": "one sequence of the workload per step, cycling over the "
                                    f"first {work.lens.size} sequences"},
@@ -689,7 +812,7 @@ def main(argv=None) -> int:
     ap.add_argument("--fp8-m", default="1,8,32,128,256", help="token counts for --workload fp8")
     ap.add_argument("--fp8-layout", choices=["packed", "rowmajor"], default="packed")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--e2e-steps", type=int, default=E2E_STEPS)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)

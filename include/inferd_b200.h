@@ -152,12 +152,16 @@ INFERD_API size_t inferd_paged_attention_counter_bytes(int32_t num_seqs, int32_t
  * memory budget is fixed at start-up).  It calls no cudaMalloc/cudaFree and no
  * allocating library routine.
  * Scratch: a 32 MiB static device array inside the library, held by every GPU that loads
- * the library until the process exits.  A call whose needs exceed it
- * (inferd_paged_attention_workspace_bytes(...) > 32 MiB) returns INFERD_ERR_WORKSPACE.
+ * the library until the process exits.  A call that runs on the tensor-core path and
+ * needs more than that (inferd_paged_attention_workspace_bytes(...) > 32 MiB) returns
+ * INFERD_ERR_WORKSPACE; calls on the generic path (fp32, head_dim != 128, block_size != 16,
+ * more than 32 query rows per kv head) use no scratch and are not limited.
  * The first call on a device looks up the array's device address (once per device, with
- * that device current); make that first call before any stream capture.  Every call
- * clears the ticket counters itself; all calls share the array, so calls that overlap on
- * the GPU race -- order them on one stream.
+ * that device current); make that first call before any stream capture.  The address is
+ * kept for the life of the process and is not looked up again after cudaDeviceReset() or
+ * another change of the device's primary context: do not call this entry point on that
+ * device after one.  Every call clears the ticket counters itself; all calls share the
+ * array, so calls that overlap on the GPU race -- order them on one stream.
  */
 INFERD_API int inferd_paged_attention_noalloc(void* out, const void* query,
                            const void* key_cache, const void* value_cache,

@@ -61,9 +61,32 @@ bool set_long(PyObject* obj, PyObject* name, long long value) {
   return r == 0;
 }
 
-// writable contiguous buffer of at least `bytes` bytes
-bool get_buffer(PyObject* obj, Py_buffer* view, Py_ssize_t bytes) {
-  if (PyObject_GetBuffer(obj, view, PyBUF_WRITABLE | PyBUF_C_CONTIGUOUS) != 0) return false;
+// True for a struct-module format naming a signed integer of `itemsize` bytes in native
+// byte order ("i", "l", "q", optionally prefixed with "@" or "=").
+bool signed_int_format(const char* fmt, Py_ssize_t itemsize) {
+  if (fmt == nullptr) return false;
+  if (*fmt == '@' || *fmt == '=') ++fmt;
+  if (fmt[0] == '\0' || fmt[1] != '\0') return false;
+  switch (fmt[0]) {
+    case 'i': return itemsize == static_cast<Py_ssize_t>(sizeof(int));
+    case 'l': return itemsize == static_cast<Py_ssize_t>(sizeof(long));
+    case 'q': return itemsize == static_cast<Py_ssize_t>(sizeof(long long));
+    default: return false;
+  }
+}
+
+// writable C-contiguous buffer of signed integers of `itemsize` bytes (int32 or int64),
+// at least `bytes` bytes long; anything else (another item size, floats, unsigned) is a
+// TypeError, so a mistyped view can never be read or written as the wrong integer width
+bool get_buffer(PyObject* obj, Py_buffer* view, Py_ssize_t bytes, Py_ssize_t itemsize) {
+  if (PyObject_GetBuffer(obj, view, PyBUF_WRITABLE | PyBUF_C_CONTIGUOUS | PyBUF_FORMAT) != 0)
+    return false;
+  if (view->itemsize != itemsize || !signed_int_format(view->format, view->itemsize)) {
+    PyErr_Format(PyExc_TypeError, "expected a buffer of int%d, got format '%s' with %zd-byte items",
+                 static_cast<int>(itemsize * 8), view->format ? view->format : "B", view->itemsize);
+    PyBuffer_Release(view);
+    return false;
+  }
   if (view->len < bytes) {
     PyBuffer_Release(view);
     PyErr_SetString(PyExc_ValueError, "output buffer too small");
@@ -84,7 +107,7 @@ PyObject* plan_slots(PyObject*, PyObject* args) {
   }
   const Py_ssize_t n = PyList_GET_SIZE(tables);
   Py_buffer view;
-  if (!get_buffer(slots_obj, &view, static_cast<Py_ssize_t>(n * per * 8))) return nullptr;
+  if (!get_buffer(slots_obj, &view, static_cast<Py_ssize_t>(n * per * 8), 8)) return nullptr;
   int64_t* slots = static_cast<int64_t*>(view.buf);
   PyObject* reserved = PyList_New(0);
   Py_ssize_t failed = -1;
@@ -329,7 +352,7 @@ PyObject* pack_changes(PyObject*, PyObject* args) {
     return nullptr;
   }
   Py_buffer view;
-  if (!get_buffer(out_obj, &view, static_cast<Py_ssize_t>(n * 4))) return nullptr;
+  if (!get_buffer(out_obj, &view, static_cast<Py_ssize_t>(n * 4), 4)) return nullptr;
   std::vector<int32_t> pairs;
   PyObject* ids = PyList_New(n);
   PyObject* nblk = PyList_New(n);
@@ -367,8 +390,8 @@ PyObject* pack_staged(PyObject*, PyObject* args) {
     return nullptr;
   }
   Py_buffer rp_view, pv;
-  if (!get_buffer(rp_obj, &rp_view, static_cast<Py_ssize_t>((n + 1) * 4))) return nullptr;
-  if (!get_buffer(pairs_obj, &pv, 0)) {
+  if (!get_buffer(rp_obj, &rp_view, static_cast<Py_ssize_t>((n + 1) * 4), 4)) return nullptr;
+  if (!get_buffer(pairs_obj, &pv, 0, 4)) {
     PyBuffer_Release(&rp_view);
     return nullptr;
   }
@@ -409,7 +432,7 @@ PyObject* scan(PyObject*, PyObject* args) {
   if (!PyArg_ParseTuple(args, "O!LO", &PyList_Type, &tables, &extra, &out_obj)) return nullptr;
   const Py_ssize_t n = PyList_GET_SIZE(tables);
   Py_buffer view;
-  if (!get_buffer(out_obj, &view, static_cast<Py_ssize_t>(n * 4))) return nullptr;
+  if (!get_buffer(out_obj, &view, static_cast<Py_ssize_t>(n * 4), 4)) return nullptr;
   int32_t* lens = static_cast<int32_t*>(view.buf);
   PyObject* nblk = PyList_New(n);
   if (!nblk) {

@@ -990,6 +990,17 @@ int launch_merge(const FastParams& fp, int nt, int segs, cudaStream_t s) {
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 }  // namespace
+
+bool paged_attention_fast_path(int32_t dtype, int32_t head_dim, int32_t block_size, int32_t nq,
+                               int64_t num_blocks, int32_t num_kv_heads, const void* key_cache,
+                               const void* value_cache, const void* query, const void* out) {
+  const int64_t rows = num_blocks * num_kv_heads * kPage;
+  return (dtype == INFERD_BF16 || dtype == INFERD_F16) && head_dim == kHeadDim &&
+         block_size == kPage && nq <= kMaxRowsFast && rows < (int64_t{1} << 31) &&
+         num_kv_heads <= kMaxKvHeadsFast && aligned(key_cache, 16) && aligned(value_cache, 16) &&
+         aligned(query, 16) && aligned(out, 16);
+}
+
 }  // namespace inferd
 
 using namespace inferd;
@@ -1041,11 +1052,8 @@ extern "C" int inferd_paged_attention(void* out, const void* query, const void* 
   const int nq = q_len * group;
   const int64_t rows = num_blocks * num_kv_heads * kPage;
 
-  const bool fast = (dtype == INFERD_BF16 || dtype == INFERD_F16) && head_dim == kHeadDim &&
-                    block_size == kPage && nq <= kMaxRowsFast && rows < (int64_t{1} << 31) &&
-                    num_kv_heads <= kMaxKvHeadsFast &&
-                    aligned(key_cache, 16) && aligned(value_cache, 16) && aligned(query, 16) &&
-                    aligned(out, 16);
+  const bool fast = paged_attention_fast_path(dtype, head_dim, block_size, nq, num_blocks,
+                                              num_kv_heads, key_cache, value_cache, query, out);
   if (!fast) {
     if (head_dim > kGenMaxDim) return INFERD_ERR_UNSUPPORTED;
     if (static_cast<int64_t>(q_len) * num_q_heads > 65535 * 1024) return INFERD_ERR_UNSUPPORTED;

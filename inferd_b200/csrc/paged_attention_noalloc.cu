@@ -13,6 +13,13 @@
 //   * each call clears the ticket counters at its head before launching;
 //   * calls whose executions overlap on the GPU (different streams, no ordering) race
 //     on the scratch and give wrong results -- order them on one stream.
+// Only the tensor-core path uses scratch; shapes that run on the generic path (fp32,
+// head_dim != 128, block_size != 16, more than 32 query rows per kv head) need none and
+// are never refused for their size.
+// The scratch's device address is looked up on a device's first call and kept for the
+// life of the process.  It is not looked up again after cudaDeviceReset() or anything
+// else that replaces the device's primary context, so such a process must not call this
+// entry point again on that device.
 #include <mutex>
 
 #include "common.cuh"
@@ -60,18 +67,26 @@ extern "C" int inferd_paged_attention_noalloc(
   if (num_seqs < 0 || q_len <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
     return INFERD_ERR_INVALID_ARGUMENT;
   if (num_seqs == 0) return INFERD_OK;
-  const size_t need = inferd_paged_attention_workspace_bytes(
-      num_seqs, q_len, num_q_heads, num_kv_heads, head_dim, current_device());
-  if (need > kNoAllocScratchBytes) return INFERD_ERR_WORKSPACE;  // beyond the static area
+  if (num_q_heads % num_kv_heads != 0) return INFERD_ERR_INVALID_ARGUMENT;
+  const int32_t nq = q_len * (num_q_heads / num_kv_heads);
+  const bool fast = paged_attention_fast_path(dtype, head_dim, block_size, nq, num_blocks,
+                                              num_kv_heads, key_cache, value_cache, query, out);
+  if (fast) {
+    const size_t need = inferd_paged_attention_workspace_bytes(
+        num_seqs, q_len, num_q_heads, num_kv_heads, head_dim, current_device());
+    if (need > kNoAllocScratchBytes) return INFERD_ERR_WORKSPACE;  // beyond the static area
+  }
   void* scratch = nullptr;
   int st = scratch_for_current_device(&scratch);
   if (st != INFERD_OK) return st;
-  // The ticket counters must start at zero; an earlier call that did not complete
-  // could have left them otherwise, so clear them on the caller's stream every time.
-  const size_t counters = inferd_paged_attention_counter_bytes(
-      num_seqs < 4096 ? num_seqs : 4096, num_kv_heads);
-  st = cuda_status(cudaMemsetAsync(scratch, 0, counters, static_cast<cudaStream_t>(stream)));
-  if (st != INFERD_OK) return st;
+  if (fast) {
+    // The ticket counters must start at zero; an earlier call that did not complete
+    // could have left them otherwise, so clear them on the caller's stream every time.
+    // The counter size is that of one launch chunk (the function clamps to it).
+    const size_t counters = inferd_paged_attention_counter_bytes(num_seqs, num_kv_heads);
+    st = cuda_status(cudaMemsetAsync(scratch, 0, counters, static_cast<cudaStream_t>(stream)));
+    if (st != INFERD_OK) return st;
+  }
   return inferd_paged_attention(out, query, key_cache, value_cache, block_tables,
                                 block_table_bytes, block_table_stride, context_lens, num_seqs,
                                 q_len, num_q_heads, num_kv_heads, head_dim, block_size,

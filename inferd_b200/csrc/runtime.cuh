@@ -25,4 +25,10 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn encode_tiled_fn();
 
+// True when inferd_paged_attention runs these arguments on its tensor-core fast path,
+// the only path that uses the workspace (nq = q_len * q_heads / kv_heads).
+bool paged_attention_fast_path(int32_t dtype, int32_t head_dim, int32_t block_size, int32_t nq,
+                               int64_t num_blocks, int32_t num_kv_heads, const void* key_cache,
+                               const void* value_cache, const void* query, const void* out);
+
 }  // namespace inferd

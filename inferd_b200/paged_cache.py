@@ -644,51 +644,80 @@ class PagedKVCache:
         return self._table(seq_id).length
 
     def _table(self, seq_id: int) -> SequencePageTable:
-        try:
-            return self.sequences[seq_id]
-        except KeyError:
-            raise KeyError(f"unknown sequence: {seq_id}") from None
+        table = self.sequences.get(seq_id)
+        if table is None:
+            raise KeyError(f"no sequence {seq_id!r} in this cache")
+        return table
 
     def _check_layer(self, layer: int) -> None:
-        if layer < 0 or layer >= self.num_layers:
-            raise IndexError(f"layer {layer} outside [0, {self.num_layers})")
+        if not 0 <= layer < self.num_layers:
+            raise IndexError(f"layer index {layer} is not below num_layers={self.num_layers}")
 
-    def _validate_layers(
-        self, layer_keys: list[torch.Tensor], layer_values: list[torch.Tensor]
-    ) -> None:
-        if len(layer_keys) != self.num_layers or len(layer_values) != self.num_layers:
-            raise ValueError("layer key/value lists must match num_layers")
-        expected_shape = layer_keys[0].shape
-        if len(expected_shape) != 3:
-            raise ValueError("layer tensors must be [tokens, kv_heads, head_dim]")
-        if expected_shape[1:] != (self.num_kv_heads, self.head_dim):
-            raise ValueError(
-                f"expected [tokens, {self.num_kv_heads}, {self.head_dim}], "
-                f"got {tuple(expected_shape)}"
-            )
-        for tensor in [*layer_keys, *layer_values]:
-            if tensor.shape != expected_shape:
-                raise ValueError("all layer tensors must have the same shape")
-            if tensor.device != self.device:
-                raise ValueError(f"tensor device {tensor.device} != cache device {self.device}")
+    def _validate_layers(self, layer_keys: list[torch.Tensor],
+                         layer_values: list[torch.Tensor]) -> None:
+        """One [tokens, kv_heads, head_dim] tensor per layer for keys and for values, all of
+        one shape and on the cache's device; ValueError otherwise (the reference's
+        exception type for these checks, core/paged_cache.py:225-242)."""
+        n_layers = self.num_layers
+        if (len(layer_keys), len(layer_values)) != (n_layers, n_layers):
+            raise ValueError(f"need {n_layers} key and {n_layers} value tensors, got "
+                             f"{len(layer_keys)} and {len(layer_values)}")
+        want_tail = (self.num_kv_heads, self.head_dim)
+        shape = None
+        for t in (*layer_keys, *layer_values):
+            if t.ndim != 3 or tuple(t.shape[1:]) != want_tail:
+                raise ValueError(f"token tensors are [tokens, {want_tail[0]}, {want_tail[1]}], "
+                                 f"got {tuple(t.shape)}")
+            if shape is None:
+                shape = t.shape
+            elif t.shape != shape:
+                raise ValueError(f"token tensors differ in shape: {tuple(shape)} and {tuple(t.shape)}")
+            if t.device != self.device:
+                raise ValueError(f"token tensor on {t.device}, cache on {self.device}")
 
     def assert_consistent(self) -> None:
-        owned = [block for table in self.sequences.values() for block in table.blocks]
-        if len(owned) != len(set(owned)):
-            raise AssertionError("a physical block is owned by multiple sequences")
-        if len(owned) != self.allocator.allocated_count:
-            raise AssertionError("allocator/table allocation counts disagree")
-        for block in owned:
-            if block < 0 or block >= self.num_blocks:
-                raise AssertionError(f"invalid block id: {block}")
+        """Every block is owned by at most one sequence, the owned blocks are exactly the
+        allocator's allocated set, and free + allocated partition the pool."""
+        owners: dict[int, int] = {}
+        for seq_id, table in self.sequences.items():
+            for blk in table.blocks:
+                if not 0 <= blk < self.num_blocks:
+                    raise AssertionError(f"sequence {seq_id} holds block {blk}, outside the pool")
+                if blk in owners:
+                    raise AssertionError(f"block {blk} held by sequences {owners[blk]} and {seq_id}")
+                owners[blk] = seq_id
+        allocated = self.allocator._allocated
+        if owners.keys() != allocated:
+            raise AssertionError(f"{len(owners)} blocks in page tables, "
+                                 f"{len(allocated)} marked allocated")
+        free = self.allocator._free
+        if len(free) + len(allocated) != self.num_blocks or allocated.intersection(free):
+            raise AssertionError("free and allocated blocks do not partition the pool")
+
+
+def _full_attention_layers(kv) -> list[int]:
+    """Indices of the layers whose K/V a Qwen3.5 hybrid cache holds: its own
+    transformer_layers when it lists them, else every 4-D key tensor with tokens in it."""
+    listed = list(getattr(kv, "transformer_layers", None) or [])
+    if listed:
+        return listed
+    return [i for i, k in enumerate(kv.key_cache)
+            if isinstance(k, torch.Tensor) and k.ndim == 4 and k.shape[2] > 0]
+
+
+def _clone_all(states):
+    """Fresh copies of a per-layer state list (None where a layer has no state)."""
+    return [None if t is None else t.clone() for t in states]
 
 
 @dataclass
 class PagedHybridCache:
-    """Paged form of Qwen3.5's hybrid cache (core/paged_cache.py:255-363).
+    """Paged form of Qwen3.5's hybrid cache (the API of core/paged_cache.py:255-363).
 
-    Full-attention K/V live in `attention` (a PagedKVCache); the linear-attention conv /
-    recurrent states are fixed-size tensors and are carried as clones.
+    The full-attention layers' K/V go into one PagedKVCache (`attention`, one pool layer
+    per full-attention layer, `layer_to_cache` mapping model layer -> pool layer) through
+    the reshape_and_cache kernel; the linear-attention conv / recurrent states have a fixed
+    size per sequence, so they are kept as copies.  Batch-1 caches only.
     """
 
     attention: PagedKVCache
@@ -701,81 +730,58 @@ class PagedHybridCache:
 
     @classmethod
     def from_qwen_cache(cls, kv, *, block_size: int = 16, seq_id: int = 0) -> "PagedHybridCache":
-        """Convert a batch=1 Qwen3.5 dynamic cache into paged attention blocks."""
-        transformer_layers = list(getattr(kv, "transformer_layers", []))
-        if not transformer_layers:
-            transformer_layers = [
-                i for i, k in enumerate(kv.key_cache)
-                if k is not None and k.ndim == 4 and k.shape[-2] > 0
-            ]
-        if not transformer_layers:
-            raise ValueError("cache contains no full-attention layers")
-
-        first = kv.key_cache[transformer_layers[0]]
-        if first.shape[0] != 1:
-            raise ValueError("PagedHybridCache currently supports batch=1 caches only")
-        _, num_kv_heads, seq_len, head_dim = first.shape
-        num_blocks = (seq_len + block_size - 1) // block_size
-        attention = PagedKVCache(
-            num_layers=len(transformer_layers),
-            num_blocks=max(num_blocks, 1),
-            block_size=block_size,
-            num_kv_heads=num_kv_heads,
-            head_dim=head_dim,
-            dtype=first.dtype,
-            device=first.device,
-        )
-        attention.create_sequence(seq_id)
-
-        layer_keys, layer_values, layer_to_cache = [], [], {}
-        for cache_layer, original_layer in enumerate(transformer_layers):
-            key = kv.key_cache[original_layer]
-            value = kv.value_cache[original_layer]
-            if key is None or value is None:
-                raise ValueError(f"missing key/value cache for layer {original_layer}")
-            if key.shape != value.shape:
-                raise ValueError(f"key/value shape mismatch at layer {original_layer}")
-            if key.shape[0] != 1:
-                raise ValueError("PagedHybridCache currently supports batch=1 caches only")
-            if key.shape[1:] != (num_kv_heads, seq_len, head_dim):
-                raise ValueError("all attention layers must share KV shape")
-            layer_to_cache[original_layer] = cache_layer
-            # [1, heads, seq, dim] -> [seq, heads, dim] as a strided view: the append
-            # kernel takes token / head strides, so no transposed copy is made.
-            layer_keys.append(key[0].transpose(0, 1))
-            layer_values.append(value[0].transpose(0, 1))
-        attention.append_tokens(seq_id, layer_keys, layer_values)
-
-        return cls(
-            attention=attention,
-            layer_to_cache=layer_to_cache,
-            conv_states=_clone_optional_tensors(kv.conv_states),
-            recurrent_states=_clone_optional_tensors(kv.recurrent_states),
-            layer_types=list(getattr(kv, "layer_types", [])) or None,
-            transformer_layers=transformer_layers,
-            seq_id=seq_id,
-        )
+        """Page a batch-1 HF Qwen3.5 cache: every full-attention layer's [1, heads, seq,
+        dim] K/V is appended to one sequence of a pool sized to hold it exactly."""
+        layers = _full_attention_layers(kv)
+        if not layers:
+            raise ValueError("the cache holds no full-attention K/V")
+        pairs = []
+        for layer in layers:
+            k, v = kv.key_cache[layer], kv.value_cache[layer]
+            if k is None or v is None:
+                raise ValueError(f"layer {layer} is listed as full attention but has no K/V")
+            if k.ndim != 4 or k.shape != v.shape:
+                raise ValueError(f"layer {layer}: K {tuple(k.shape)} and V {tuple(v.shape)} "
+                                 "are not one [batch, heads, seq, dim] shape")
+            pairs.append((k, v))
+        batch, heads, tokens, dim = pairs[0][0].shape
+        if batch != 1:
+            raise ValueError(f"only batch-1 caches can be paged (batch is {batch})")
+        for layer, (k, _) in zip(layers, pairs):
+            if tuple(k.shape) != (1, heads, tokens, dim):
+                raise ValueError(f"layer {layer} K/V is {tuple(k.shape)}, layer {layers[0]}'s "
+                                 f"is {(1, heads, tokens, dim)}")
+        first = pairs[0][0]
+        pool = PagedKVCache(num_layers=len(layers),
+                            num_blocks=max(1, -(-tokens // block_size)), block_size=block_size,
+                            num_kv_heads=heads, head_dim=dim, dtype=first.dtype,
+                            device=first.device)
+        pool.create_sequence(seq_id)
+        # [1, heads, seq, dim] -> strided [seq, heads, dim] views; the append kernel reads
+        # token and head strides, so nothing is transposed in memory first
+        pool.append_tokens(seq_id, [k[0].transpose(0, 1) for k, _ in pairs],
+                           [v[0].transpose(0, 1) for _, v in pairs])
+        types = getattr(kv, "layer_types", None)
+        return cls(attention=pool, layer_to_cache={layer: i for i, layer in enumerate(layers)},
+                   conv_states=_clone_all(kv.conv_states),
+                   recurrent_states=_clone_all(kv.recurrent_states),
+                   layer_types=list(types) if types else None, transformer_layers=layers,
+                   seq_id=seq_id)
 
     def to_qwen_cache_like(self, template):
-        """Rebuild an HF-style cache with the same class/attributes as `template`."""
+        """A shallow copy of `template` (same class, same other attributes) whose K/V come
+        back out of the pool as contiguous [1, heads, seq, dim] tensors, whose state lists
+        are fresh copies, and whose layer lists are its own."""
         out = copy.copy(template)
-        out.conv_states = _clone_optional_tensors(self.conv_states)
-        out.recurrent_states = _clone_optional_tensors(self.recurrent_states)
-        out.key_cache = [None for _ in template.key_cache]
-        out.value_cache = [None for _ in template.value_cache]
-        if hasattr(template, "layer_types"):
-            out.layer_types = list(template.layer_types)
-        if hasattr(template, "transformer_layers"):
-            out.transformer_layers = list(template.transformer_layers)
-        if hasattr(template, "last_linear_layer"):
-            out.last_linear_layer = template.last_linear_layer
-
-        for original_layer, cache_layer in self.layer_to_cache.items():
-            key, value = self.attention.gather_layer(self.seq_id, cache_layer)
-            out.key_cache[original_layer] = key.transpose(0, 1).unsqueeze(0).contiguous()
-            out.value_cache[original_layer] = value.transpose(0, 1).unsqueeze(0).contiguous()
+        for name in ("layer_types", "transformer_layers"):
+            if hasattr(template, name):
+                setattr(out, name, list(getattr(template, name)))
+        out.conv_states = _clone_all(self.conv_states)
+        out.recurrent_states = _clone_all(self.recurrent_states)
+        n = len(template.key_cache)
+        out.key_cache, out.value_cache = [None] * n, [None] * len(template.value_cache)
+        for layer, pool_layer in self.layer_to_cache.items():
+            k, v = self.attention.gather_layer(self.seq_id, pool_layer)
+            out.key_cache[layer] = k.permute(1, 0, 2).contiguous()[None]
+            out.value_cache[layer] = v.permute(1, 0, 2).contiguous()[None]
         return out
-
-
-def _clone_optional_tensors(items):
-    return [item.clone() if item is not None else None for item in items]

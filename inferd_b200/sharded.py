@@ -10,8 +10,16 @@ sequence order, after each step.  The reference runs one process on one GPU
     owners = assign_by_tokens(context_lens, world)           # balanced KV bytes, ragged counts
     full = gather_outputs(local_out, counts, group=None)     # all ranks get [sum(counts), ...]
 
+    g = OutputGather((rows, q_heads, dim), dtype, device, counts)   # a decode loop's gather
+    out = g.local()          # this step's output buffer: the attention writes it
+    g.start()                # all-gather it on the collective's own stream, asynchronously
+    full = g.result()        # the step's gathered outputs (the current stream waits for them)
+
 `gather_outputs` uses NCCL's all-gather into one tensor when the process group is NCCL and
 every shard has the same size, else a padded all-gather (also what gloo ranks on CPU use).
+`OutputGather` preallocates everything and overlaps step N's all-gather with step N + 1's
+compute: local outputs alternate between two buffers, so the collective reading step N's
+buffer never races the kernels writing step N + 1's.
 """
 
 from __future__ import annotations
@@ -83,3 +91,93 @@ def gather_outputs(local: torch.Tensor, counts: list[int] | None = None, *, grou
         out[row:row + c] = part[:c]
         row += c
     return out
+
+
+class OutputGather:
+    """Double-buffered, asynchronous all-gather of per-step outputs (decode outputs of the
+    sequences each rank owns, gathered in rank order).
+
+    Every buffer is allocated once: two local output buffers [width, *tail] (width = the
+    largest count), two gathered buffers [world * width, *tail] and, for ragged counts, the
+    row index that compacts a gathered buffer to [sum(counts), *tail].  start() issues the
+    collective with async_op=True, so it runs on the process group's own stream after the
+    work already queued on the current stream, while the current stream goes on with the
+    next step.  A local buffer is handed out again only after the collective that read it
+    two steps earlier has completed on the current stream (Work.wait orders the streams;
+    the host does not block).
+    """
+
+    def __init__(self, tail: tuple[int, ...], dtype: torch.dtype, device: torch.device,
+                 counts: list[int] | None = None, *, group=None) -> None:
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if counts is None:
+            raise ValueError("counts: rows per rank (a list of world integers)")
+        if len(counts) != self.world or any(c < 0 for c in counts):
+            raise ValueError(f"{len(counts)} counts for a world of {self.world}")
+        self.counts = [int(c) for c in counts]
+        self.width = max(max(self.counts), 1)
+        self.tail = tuple(int(t) for t in tail)
+        self.ragged = any(c != self.width for c in self.counts)
+        self._nccl = dist.get_backend(group) == "nccl"
+        shape_l = (self.width,) + self.tail
+        shape_g = (self.world * self.width,) + self.tail
+        self._local = [torch.zeros(shape_l, dtype=dtype, device=device) for _ in range(2)]
+        self._gathered = [torch.zeros(shape_g, dtype=dtype, device=device) for _ in range(2)]
+        self._compact = None
+        if self.ragged:
+            rows = [r * self.width + i for r, c in enumerate(self.counts) for i in range(c)]
+            self._index = torch.tensor(rows, dtype=torch.long, device=device)
+            self._compact = [torch.empty((sum(self.counts),) + self.tail, dtype=dtype, device=device)
+                             for _ in range(2)]
+        self._work = [None, None]
+        self._cur = 0
+        self._last = None
+        self._started = False
+
+    def local(self) -> torch.Tensor:
+        """This step's local output buffer, [counts[rank], *tail]; write it, then start()."""
+        i = self._cur
+        if self._work[i] is not None:  # the collective that read this buffer two steps ago
+            self._work[i].wait()
+            self._work[i] = None
+        self._started = False
+        return self._local[i][:self.counts[self.rank]]
+
+    def start(self) -> None:
+        """All-gather this step's local buffer, asynchronously; the next local() call hands
+        out the other buffer."""
+        if self._started:
+            raise RuntimeError("start() once per local()")
+        i = self._cur
+        src, dst = self._local[i], self._gathered[i]
+        if self._nccl:
+            self._work[i] = dist.all_gather_into_tensor(dst, src, group=self.group, async_op=True)
+        else:
+            self._work[i] = dist.all_gather(list(dst.chunk(self.world)), src, group=self.group,
+                                            async_op=True)
+        self._started = True
+        self._last = i
+        self._cur = i ^ 1
+
+    def result(self) -> torch.Tensor:
+        """The last started step's gathered outputs, [sum(counts), *tail], rank order; the
+        current stream waits for the collective (no host synchronisation)."""
+        i = self._last
+        if i is None:
+            raise RuntimeError("no all-gather has been started")
+        if self._work[i] is not None:
+            self._work[i].wait()
+            self._work[i] = None
+        if not self.ragged:
+            return self._gathered[i]
+        torch.index_select(self._gathered[i], 0, self._index, out=self._compact[i])
+        return self._compact[i]
+
+    def wait_all(self) -> None:
+        """Order every started collective before the current stream's next work."""
+        for i in range(2):
+            if self._work[i] is not None:
+                self._work[i].wait()
+                self._work[i] = None

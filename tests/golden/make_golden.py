@@ -1,8 +1,9 @@
 """Generate the golden fixtures in tests/golden/ from the reference itself.
 
-Run in a container that has the reference source tree (read-only is fine):
+Run where the reference source tree is checked out (read-only is fine), naming its root
+with --reference or the INFERD_REFERENCE environment variable:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --reference /root/reference
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --reference <reference checkout>
 
 It imports the reference's own core.paged_attn / core.paged_cache, the transformers
 eager attention the reference's speculative verify forward runs, and torch's
@@ -16,6 +17,7 @@ from __future__ import annotations
 import argparse
 import json
 import math
+import os
 import random
 import sys
 import types
@@ -318,8 +320,11 @@ def gen_fp8_dynamic(out: dict) -> None:
 
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("INFERD_REFERENCE"),
+                    help="root of the reference checkout (default: $INFERD_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or INFERD_REFERENCE")
     sys.dont_write_bytecode = True
     sys.path.insert(0, args.reference)
     import core.paged_attn as pa  # noqa: E402  (reference module)

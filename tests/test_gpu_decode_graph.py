@@ -37,12 +37,25 @@ def _twin_caches(device, lens, num_blocks=900, seed=0):
     return caches, g
 
 
-@pytest.mark.parametrize("q_len", [1, 5])
-def test_graph_steps_equal_eager_steps(cuda_device, q_len):
+@pytest.mark.parametrize("q_len,max_pairs", [(1, None), (5, None), (1, 0), (5, 2)])
+def test_graph_steps_equal_eager_steps(cuda_device, q_len, max_pairs):
+    # max_pairs caps the table changes one step may stage: past it prepare() sends every
+    # table whole before the replay (the overflow path), which a small cap forces often
     lens = [9, 40, 130, 17, 990]  # 62 pages: the table outgrows a 64-page capacity mid-run
     (a, b), g = _twin_caches(cuda_device, lens, seed=q_len)
     ids = list(range(len(lens)))
     graph = DecodeGraph(a, ids, num_q_heads=HQ, q_len=q_len, headroom_pages=2)  # small: re-captures
+    if max_pairs is not None:
+        graph._max_pairs = max_pairs
+    dense = 0
+    real_upload = graph._upload_dense
+
+    def counted_upload():
+        nonlocal dense
+        dense += 1
+        real_upload()
+
+    graph._upload_dense = counted_upload
     rng = np.random.default_rng(q_len)
     caps = set()
     for step in range(60):
@@ -77,6 +90,8 @@ def test_graph_steps_equal_eager_steps(cuda_device, q_len):
     assert [a.sequences[s].blocks for s in ids] == [b.sequences[s].blocks for s in ids]
     assert torch.equal(a.key_cache[0], b.key_cache[0]) and torch.equal(a.value_cache[0], b.value_cache[0])
     assert len(caps) > 1, "the capacity never grew: the re-capture path was not exercised"
+    if max_pairs is not None:
+        assert dense > len(caps) + 5, "the overflow path was not exercised"
 
 
 def test_rollback_argument_checks(cuda_device):

@@ -112,19 +112,29 @@ def test_dynamic_linear_matches_oracle(cuda_device, gran, m):
     assert_gemm_exact(y, ref, f"m={m} {gran}")
 
 
-@pytest.mark.parametrize("m", [1, 8, 256])
-def test_dynamic_linear_config4_shape(cuda_device, m):
+@pytest.fixture(scope="module")
+def config4_dynamic_weight(cuda_device):
     # config-4 weight: N = 17408, K = 5120, N(0, 0.02), per-tensor scales, packed tiles
     g = torch.Generator().manual_seed(4)
     n, k = 17408, 5120
     w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).to(cuda_device)
-    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(cuda_device)
     qw, sw = quantize_fp8_dynamic(w)
-    y = fp8_dynamic_linear(x, pack_fp8_weight(qw), sw, packed_shape=(n, k)).float().cpu().numpy()
+    packed = pack_fp8_weight(qw)
+    yield n, k, qw.view(torch.uint8).cpu().numpy(), sw.cpu().numpy(), packed, sw
+    del w, qw, packed
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("m", [1, 8, 32, 128, 256])
+def test_dynamic_linear_config4_all_rows(cuda_device, config4_dynamic_weight, m):
+    # every benchmarked token count over all 17408 output channels
+    n, k, qw, sw_host, packed, sw = config4_dynamic_weight
+    g = torch.Generator().manual_seed(400 + m)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(cuda_device)
+    y = fp8_dynamic_linear(x, packed, sw, packed_shape=(n, k)).float().cpu().numpy()
     qx, sx = _quant(x, "tensor")
-    cols = np.random.default_rng(m).choice(n, size=n if m <= 8 else 2048, replace=False)
-    ref = oracle.fp8_dynamic_linear(qx, sx, qw.view(torch.uint8).cpu().numpy()[cols], sw.cpu().numpy()[cols])
-    assert_gemm_exact(y[:, cols], ref, f"config 4, m={m}")
+    ref = oracle.fp8_dynamic_linear(qx, sx, qw, sw_host)
+    assert_gemm_exact(y, ref, f"config 4, m={m}")
 
 
 def test_per_tensor_scale_spans_the_batch(cuda_device):

@@ -2,8 +2,9 @@
 
 Quantisation (scales and e4m3 codes) must be bit-exact with the oracle, which is pinned to
 torch's float8_e4m3fn cast.  The linear must be within 1e-2 relative of the oracle's
-dequant-then-matmul: max |y - y_ref| <= 1e-2 * max |y_ref| and
-||y - y_ref||_F <= 1e-2 * ||y_ref||_F.
+dequant-then-matmul, read normwise (an element-wise relative bound is undefined where the
+exact output crosses zero): max |y - y_ref| <= 1e-2 * max |y_ref|, and for every token row
+||y_m - y_ref_m||_2 <= 1e-2 * ||y_ref_m||_2.
 """
 
 from __future__ import annotations
@@ -30,8 +31,11 @@ def assert_linear_close(y: np.ndarray, ref: np.ndarray, what: str) -> None:
     err = np.abs(y - ref)
     scale = float(np.abs(ref).max())
     assert float(err.max()) <= RTOL * scale, f"{what}: max err {err.max()} vs max |ref| {scale}"
-    fro = float(np.linalg.norm(y - ref) / max(np.linalg.norm(ref), 1e-30))
-    assert fro <= RTOL, f"{what}: relative Frobenius error {fro}"
+    y2, r2 = y.reshape(-1, y.shape[-1]), ref.reshape(-1, ref.shape[-1])
+    row = np.linalg.norm(y2 - r2, axis=1) / np.maximum(np.linalg.norm(r2, axis=1), 1e-30)
+    live = np.linalg.norm(r2, axis=1) > 0
+    assert float(row[live].max(initial=0.0)) <= RTOL, \
+        f"{what}: worst row relative error {row[live].max()}"
 
 
 def test_quantize_matches_golden_and_oracle(cuda_device, golden):
@@ -93,20 +97,33 @@ def test_pack_layout_and_packed_linear(cuda_device, n, k):
     assert torch.equal(y_row, y_packed)  # same MMAs in the same order
 
 
-@pytest.mark.parametrize("m", [1, 8, 256])
-def test_fp8_linear_config4_shape(cuda_device, m):
-    # config-4 weight: N = 17408, K = 5120, N(0, 0.02) quantised per channel
+@pytest.fixture(scope="module")
+def config4_weight(cuda_device):
+    # config-4 weight: N = 17408, K = 5120, N(0, 0.02) bf16, quantised per channel, packed
     g = torch.Generator().manual_seed(4)
     n, k = 17408, 5120
     w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
-    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
     q, s = quantize_fp8_per_channel(w.to(cuda_device))
-    y = fp8_linear(x.to(cuda_device), pack_fp8_weight(q), s, packed_shape=(n, k))
+    packed = pack_fp8_weight(q)
+    deq = (oracle.e4m3_decode(q.view(torch.uint8).cpu().numpy()).astype(np.float64)
+           * s.cpu().numpy().astype(np.float64)[:, None])
+    yield n, k, q, s, packed, deq
+    del q, packed
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("m", [1, 8, 32, 128, 256])
+def test_fp8_linear_config4_all_rows(cuda_device, config4_weight, m):
+    # every benchmarked token count, all 17408 output channels, packed and row-major weights
+    n, k, q, s, packed, deq = config4_weight
+    g = torch.Generator().manual_seed(40 + m)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    ref = x.double().numpy() @ deq.T
+    y = fp8_linear(x.to(cuda_device), packed, s, packed_shape=(n, k))
+    y_row = fp8_linear(x.to(cuda_device), q, s)
     torch.cuda.synchronize()
-    rows = slice(0, n) if m <= 8 else slice(0, 2048)  # keep the float64 oracle to seconds
-    ref = oracle.fp8_linear(x.float().numpy(), q.view(torch.uint8).cpu().numpy()[rows],
-                            s.cpu().numpy()[rows])
-    assert_linear_close(y.float().cpu().numpy()[:, rows], ref, f"config 4, m={m}")
+    assert torch.equal(y, y_row)
+    assert_linear_close(y.float().cpu().numpy(), ref, f"config 4, m={m}")
 
 
 def test_fp8_linear_leading_dims_bias_and_outliers(cuda_device):

@@ -444,3 +444,32 @@ def test_pack_staged_matches_pack_changes():
         assert np.all(buf[2 * n_written:] == -7)
         assert nb_a == nb_b and [t.dirty_from for t in a] == [t.dirty_from for t in b] == [_CLEAN] * len(a)
         prev_a, prev_b = (ids_a, nb_a), (ids_b, nb_b)
+
+
+def test_native_loops_reject_mistyped_buffers():
+    # the native loops read and write their buffers as int32 / int64: a view of another
+    # item size or kind is refused before anything is read or written
+    from inferd_b200.paged_cache import _CLEAN, _hostops
+    if _hostops is None:
+        pytest.skip("_hostops not built")
+    tabs = []
+    for s in range(3):
+        t = SequencePageTable(seq_id=s, block_size=4, blocks=[s, s + 3], length=7)
+        t.dirty_from = 0
+        tabs.append(t)
+    for bad in (np.zeros(3, np.int64), np.zeros(3, np.float32), np.zeros(3, np.uint32),
+                np.zeros(12, np.uint8)):
+        with pytest.raises(TypeError):
+            _hostops.scan(tabs, 0, bad)
+    ids, nblk = [0] * 3, [0] * 3
+    with pytest.raises(TypeError):
+        _hostops.pack_staged(tabs, ids, nblk, _CLEAN, np.zeros(4, np.int32), np.zeros(8, np.float32))
+    with pytest.raises(TypeError):
+        _hostops.pack_staged(tabs, ids, nblk, _CLEAN, np.zeros(4, np.int64), np.zeros(8, np.int32))
+    with pytest.raises(TypeError):
+        _hostops.plan_slots(tabs, 1, 4, [9, 10], set(range(9)), np.zeros(3, np.int32))
+    # the right types still work, and nothing above changed the tables
+    lens = np.zeros(3, np.int32)
+    nb, width, mx = _hostops.scan(tabs, 1, lens)
+    assert lens.tolist() == [8, 8, 8] and nb == [2, 2, 2] and width == 2 and mx == 8
+    assert [t.dirty_from for t in tabs] == [0, 0, 0]

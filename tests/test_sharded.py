@@ -11,7 +11,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from inferd_b200.sharded import assign_by_tokens, gather_outputs, shard_range
+from inferd_b200.sharded import OutputGather, assign_by_tokens, gather_outputs, shard_range
 
 
 @pytest.mark.parametrize("n,world", [(0, 1), (5, 1), (64, 2), (7, 2), (3, 4), (256, 8), (10, 3)])
@@ -68,6 +68,21 @@ def _worker(rank: int, world: int, port: int, q) -> None:
         ragged = torch.full((counts[rank], 3), float(rank + 1))
         out = torch.empty(3, 3)
         results["ragged"] = gather_outputs(ragged, counts, out=out).tolist()
+        # the decode loop's double-buffered gather: every step's result is that step's rows,
+        # also when the steps' collectives are in flight together
+        for counts in ([3, 3], [2, 1], [0, 4]):
+            g = OutputGather((2,), torch.float32, torch.device("cpu"), counts)
+            steps = []
+            for step in range(5):
+                buf = g.local()
+                assert buf.shape == (counts[rank], 2)
+                buf.copy_(torch.full((counts[rank], 2), float(1000 * step + 10 * rank)))
+                buf[:, 1] += torch.arange(counts[rank], dtype=torch.float32)
+                g.start()
+                if step % 2:  # read every other step, as a loop that overlaps steps would
+                    steps.append(g.result().tolist())
+            g.wait_all()
+            results[f"loop_{counts}"] = steps
         q.put((rank, results))
     finally:
         dist.destroy_process_group()
@@ -90,3 +105,7 @@ def test_gather_outputs_two_gloo_ranks():
     for r in range(2):
         assert got[r]["equal"] == expect_equal
         assert got[r]["ragged"] == expect_ragged
+        for counts in ([3, 3], [2, 1], [0, 4]):
+            want = [[[1000.0 * step + 10 * rr, 1000.0 * step + 10 * rr + i]
+                     for rr in range(2) for i in range(counts[rr])] for step in (1, 3)]
+            assert got[r][f"loop_{counts}"] == want, counts

@@ -6,7 +6,9 @@ fixed at start-up.  This entry point uses the library's own static 32 MiB scratc
 instead of a caller-provided workspace.  Its results must match inferd_paged_attention
 (called here through the Python API, which passes a workspace) within the bf16
 tolerance of the other attention tests, on two consecutive calls that reuse the shared
-scratch.  The file name keeps it last in collection order.
+scratch, and the fp32 oracle within the same tolerance.  Shapes that run on the generic
+path use no scratch and must not be refused however large the batch.  The file name keeps
+it last in collection order.
 """
 
 from __future__ import annotations
@@ -15,6 +17,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle
 from inferd_b200 import _lib, paged_attention_batched
 
 pytestmark = pytest.mark.gpu
@@ -62,7 +65,14 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls(cuda_device):
         _lib.raise_device_errors(cuda_device)
         err = float((got.float() - expect.float()).abs().max())
         assert err <= ATOL, f"call {call}: max abs difference {err}"
-        assert np.isfinite(got.float().cpu().numpy()).all()
+        out = got.float().cpu().numpy()
+        assert np.isfinite(out).all()
+        ref = oracle.batched_paged_attention(q.float().cpu().numpy(), kc.float().cpu().numpy(),
+                                             vc.float().cpu().numpy(), bt.cpu().numpy(),
+                                             cl.cpu().numpy())
+        err = float(np.abs(out - ref).max())
+        assert err <= ATOL and err <= 1e-2 * float(np.abs(ref).max()), \
+            f"call {call}: max abs error {err} against the oracle"
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch(cuda_device):
@@ -75,3 +85,29 @@ def test_noalloc_rejects_requests_beyond_its_scratch(cuda_device):
         dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(),
         4, 1, None, 4096, 4, 64, 8, 128, 16, 1, 16, 1.0, 2, None, _lib.stream_of(cuda_device))
     assert st == _lib.ERR_WORKSPACE
+
+
+def test_noalloc_generic_path_needs_no_scratch(cuda_device):
+    # head_dim 64 runs on the generic path: a batch whose tensor-core workspace would exceed
+    # 32 MiB is still served, and equals the workspace entry point bit for bit
+    b, q_len, hq, hkv, d, bs = 4096, 4, 64, 8, 64, 16
+    assert _lib.load().inferd_paged_attention_workspace_bytes(b, q_len, hq, hkv, d, 0) > 32 << 20
+    g = torch.Generator().manual_seed(7)
+    lens = torch.randint(q_len, 3 * bs, (b,), generator=g)
+    pages = (lens + bs - 1) // bs
+    nb = int(pages.sum())
+    kc = torch.randn(nb, hkv, bs, d, generator=g).to(torch.bfloat16).to(cuda_device)
+    vc = torch.randn(nb, hkv, bs, d, generator=g).to(torch.bfloat16).to(cuda_device)
+    bt = torch.zeros(b, int(pages.max()), dtype=torch.int32)
+    s = 0
+    for i, p in enumerate(pages.tolist()):
+        bt[i, :p] = torch.arange(s, s + p, dtype=torch.int32)
+        s += p
+    q = torch.randn(b, q_len, hq, d, generator=g).to(torch.bfloat16).to(cuda_device)
+    bt, cl = bt.to(cuda_device), lens.to(torch.int32).to(cuda_device)
+    mx = int(lens.max())
+    expect = paged_attention_batched(q, kc, vc, bt, cl, max_context_len=mx)
+    got = _noalloc(q, kc, vc, bt, cl, mx, cuda_device)
+    torch.cuda.synchronize()
+    _lib.raise_device_errors(cuda_device)
+    assert torch.equal(got, expect)
