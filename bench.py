@@ -244,17 +244,18 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     import torch.distributed as dist
 
     from inferd_b200 import _lib
-    from inferd_b200.sharded import OutputGather
+    from inferd_b200.sharded import OutputGather, PeerGather
 
     wl = DeviceWorkload(args.workload, rank, world, device,
                         growth_tokens=args.e2e_steps + POOL_GROWTH - E2E_STEPS)
-    gather = None
-    if world > 1:
-        # The step's kernels run on a high-priority stream and the all-gather of step N's
-        # outputs (NCCL's own stream, normal priority) overlaps step N + 1: its CTAs take
-        # the SMs the attention kernel's tail frees instead of delaying the kernel's start.
-        torch.cuda.set_stream(torch.cuda.Stream(device, priority=-1))
+    gather = peer = None
+    if world > 1 and args.gather == "nccl":
+        # NCCL all-gather of step N's outputs on NCCL's stream, overlapping step N + 1
         gather = OutputGather(tuple(wl.out.shape[1:]), wl.out.dtype, device, [wl.b] * world)
+    elif world > 1:
+        # every rank pushes its outputs into every rank's memory over NVLink and waits for
+        # the others' pushes: the gathered rows are on every GPU at the end of each step
+        peer = PeerGather(tuple(wl.out.shape[1:]), wl.out.dtype, device, wl.b)
     stream = torch.cuda.current_stream(device)
 
     def step(ev=None):
@@ -268,6 +269,9 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
             ev[1].record(stream)
         if gather is not None:
             gather.start()
+        if peer is not None:
+            peer.push(wl.out)
+            peer.wait()
 
     for _ in range(args.warmup):
         step()
@@ -320,22 +324,35 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     # output; at N = 1 the CPU leg compares every sequence's output with the oracle
     checks = {"append_bit_exact": wl.appended_bit_exact()}
     gather_us = None
-    if gather is not None:
-        mine = torch.equal(gather.result()[rank * wl.b:(rank + 1) * wl.b], wl.out)
+    if world > 1:
+        if gather is not None:
+            gathered = gather.result()
+        else:
+            gathered = peer._slots[peer._epoch & 1]
+        # every rank's rows of the gathered output equal that rank's own output, on every rank
+        ref = torch.empty_like(gathered)
+        dist.all_gather_into_tensor(ref, wl.out.contiguous())
+        mine = torch.equal(gathered, ref)
         flag = torch.tensor([int(mine and checks["append_bit_exact"])], device=device)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         checks["gathered_rows_equal_rank_outputs"] = bool(flag.item())
-        # the all-gather alone, back to back, for the record (max over ranks)
+        # the gather alone, back to back, for the record (max over ranks)
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         dist.barrier()
         torch.cuda.synchronize(device)
         g0.record(stream)
         for _ in range(k):
-            gather.local()
-            gather.start()
-        gather.wait_all()
+            if gather is not None:
+                gather.local()
+                gather.start()
+            else:
+                peer.push(wl.out)
+                peer.wait()
+        if gather is not None:
+            gather.wait_all()
         g1.record(stream)
         torch.cuda.synchronize(device)
+        _lib.raise_device_errors(device)
         t = torch.tensor([g0.elapsed_time(g1) * 1000.0 / k], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         gather_us = round(float(t.item()), 2)
@@ -345,7 +362,9 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     if not all(checks.values()) or (parity is not None and not parity["ok"]):
         raise RuntimeError(f"output check failed: {checks} {parity}")
 
-    e2e = run_e2e(args, wl, rank, world, device)
+    e2e = run_e2e(args, wl, rank, world, device, peer=peer)
+    if peer is not None:
+        peer.close()
 
     if rank != 0:
         return None
@@ -383,8 +402,12 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     }
     line["checks"] = checks
     if gather_us is not None:
-        line["allgather_us_alone"] = gather_us
-        line["allgather_bytes_per_rank"] = int(wl.out.numel() * wl.out.element_size())
+        line["gather"] = {"kind": args.gather, "us_per_step_alone": gather_us,
+                          "bytes_per_rank": int(wl.out.numel() * wl.out.element_size()),
+                          "how": "NCCL all_gather_into_tensor on NCCL's stream, overlapping the "
+                                 "next step" if args.gather == "nccl" else
+                                 "push kernel (this rank's rows into every rank's buffer over "
+                                 "NVLink, epoch flag) + bounded wait kernel, inside the step"}
     if parity is not None:
         line["parity"] = parity
     if cpu is not None and not args.no_cpu_baseline:
@@ -410,7 +433,8 @@ def config_block(workload: str, world: int) -> dict:
     }
 
 
-def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.device) -> dict:
+def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.device,
+            peer=None) -> dict:
     """Same step through the public API with pinned host inputs and a host read of the
     result every step: a DecodeGraph replay -- the host-to-device copy of the step's inputs
     (queries and new K/V from pinned memory), the page-table update, the KV append, paged
@@ -457,7 +481,10 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
 
     def one_step():
         graph.launch()
-        if world > 1:
+        if peer is not None:
+            peer.push(graph.output)
+            out_h.copy_(peer.wait(), non_blocking=True)
+        elif world > 1:
             gather_outputs(graph.output, out=gathered)
             out_h.copy_(gathered, non_blocking=True)
         if ql == 1:
@@ -812,6 +839,8 @@ def main(argv=None) -> int:
     ap.add_argument("--fp8-m", default="1,8,32,128,256", help="token counts for --workload fp8")
     ap.add_argument("--fp8-layout", choices=["packed", "rowmajor"], default="packed")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+                    help="N > 1: how each step's outputs reach every GPU")
     ap.add_argument("--e2e-steps", type=int, default=E2E_STEPS)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -848,6 +877,7 @@ def main(argv=None) -> int:
 
         dist.init_process_group("nccl", device_id=device,
                                 timeout=datetime.timedelta(seconds=120))
+    line = None
     try:
         line = run_ours(args, rank, world, device)
     finally:

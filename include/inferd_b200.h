@@ -285,6 +285,59 @@ INFERD_API int inferd_sample_probs(int64_t* tokens, const float* probs, int64_t 
                                    int32_t rows, int64_t vocab, uint64_t seed, uint64_t offset,
                                    int32_t* error_word, void* stream);
 
+/*
+ * Speculative decoding's accept / resample step for a batch (core/spec_decode.py:145-161),
+ * one launch for every draft position of every sequence.  For sequence b, draft token k
+ * (x = proposals[b * proposals_stride + k]) is accepted when u_k <= p_bk[x] / q_bk[x] (fp32
+ * division; u_k uniform on the float32 grid of [0, 1) from Philox4x32-10, key seed, counter
+ * (offset + b, 1 + k, 0)); at the first rejection one token is drawn from
+ * clamp(p_bk - q_bk, 0) -- from p_bk when that has no positive entry -- and the round ends;
+ * with all gamma drafts accepted the bonus token is drawn from p_b,gamma.  The draw follows
+ * inferd_sample_probs (Philox counter (offset + b, 0, 0)).  p: fp32 [rows][gamma + 1][vocab]
+ * at strides (p_seq_stride, p_dist_stride), q: fp32 [rows][gamma][vocab], proposals int64.
+ * Outputs: accepted[b] = accepted drafts (0 .. gamma); tokens[b * tokens_stride + 0 ..
+ * gamma] = the accepted drafts, the drawn token, then -1.  Replaces one host sync per draft
+ * token in the reference's loop.
+ */
+INFERD_API int inferd_spec_accept(int32_t* accepted, int64_t* tokens, int64_t tokens_stride,
+                                  const float* p, int64_t p_seq_stride, int64_t p_dist_stride,
+                                  const float* q, int64_t q_seq_stride, int64_t q_dist_stride,
+                                  const int64_t* proposals, int64_t proposals_stride,
+                                  int32_t rows, int32_t gamma, int64_t vocab, uint64_t seed,
+                                  uint64_t offset, int32_t* error_word, void* stream);
+
+/*
+ * Output gather over NVLink peer memory (sequence-sharded decode: every rank needs every
+ * rank's attention outputs, in rank order).  No counterpart in the reference, which runs
+ * on one GPU (core/model_runner.py:32); this replaces an all-gather collective of the
+ * per-step outputs.
+ *
+ * Each rank allocates one peer buffer of 256 + 2 * world * bytes_per_rank bytes with
+ * inferd_peer_alloc (zeroed; its CUDA IPC handle, INFERD_IPC_HANDLE_BYTES bytes, goes to
+ * every other rank, which maps it with inferd_peer_open).  Layout: uint32 flags[world] at
+ * offset 0 (the epoch each source rank last published), then slot 0 and slot 1 of
+ * world * bytes_per_rank bytes.
+ *
+ * inferd_gather_push copies bytes_per_rank bytes from src (16-byte aligned, a multiple of
+ * 16) to dst[d] + rank * bytes_per_rank for every rank d (dst: a device array of world
+ * pointers, each rank's current slot), then stores epoch into flags[d][rank] (flags: a
+ * device array of world pointers to each rank's flag words) with system-scope release.
+ * inferd_gather_wait returns, in stream order, once flags[r] >= epoch for every r
+ * (wrap-safe), i.e. once every rank's rows for this epoch are in this rank's slot; after
+ * timeout_ns (0: 2 s) it records INFERD_ERR_DEVICE_TIMEOUT in *error_word and returns.
+ * A rank pushes into a slot again only after its own wait for the following epoch.
+ */
+#define INFERD_IPC_HANDLE_BYTES 64
+INFERD_API int inferd_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+INFERD_API int inferd_peer_open(const void* ipc_handle, void** ptr);
+INFERD_API int inferd_peer_close(void* ptr);
+INFERD_API int inferd_peer_free(void* ptr);
+INFERD_API int inferd_gather_push(const void* src, int64_t bytes_per_rank, void* const* dst,
+                                  uint32_t* const* flags, int32_t rank, int32_t world,
+                                  uint32_t epoch, void* stream);
+INFERD_API int inferd_gather_wait(const uint32_t* flags, int32_t world, uint32_t epoch,
+                                  uint64_t timeout_ns, int32_t* error_word, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -84,7 +84,20 @@ _SIGNATURES = {
         _c_void_p, _f32, _u64, _u64, _c_void_p, _c_void_p]),
     "inferd_sample_probs": (ctypes.c_int, [
         _c_void_p, _c_void_p, _i64, _i32, _i64, _u64, _u64, _c_void_p, _c_void_p]),
+    "inferd_spec_accept": (ctypes.c_int, [
+        _c_void_p, _c_void_p, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64,
+        _i32, _i32, _i64, _u64, _u64, _c_void_p, _c_void_p]),
+    "inferd_peer_alloc": (ctypes.c_int, [_sz, ctypes.POINTER(_c_void_p), _c_void_p]),
+    "inferd_peer_open": (ctypes.c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "inferd_peer_close": (ctypes.c_int, [_c_void_p]),
+    "inferd_peer_free": (ctypes.c_int, [_c_void_p]),
+    "inferd_gather_push": (ctypes.c_int, [
+        _c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, ctypes.c_uint32, _c_void_p]),
+    "inferd_gather_wait": (ctypes.c_int, [
+        _c_void_p, _i32, ctypes.c_uint32, _u64, _c_void_p, _c_void_p]),
 }
+
+IPC_HANDLE_BYTES = 64
 
 
 def exported_symbols() -> list[str]:

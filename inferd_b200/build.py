@@ -26,7 +26,7 @@ LIB_PATH = LIB_DIR / "libinferd_sm100a.so"
 INCLUDE_DIR = REPO_DIR / "include"
 
 SOURCES = ["runtime.cu", "cache_ops.cu", "paged_attention.cu", "paged_attention_noalloc.cu",
-           "fp8_linear.cu", "sampling.cu"]
+           "fp8_linear.cu", "sampling.cu", "peer.cu"]
 HOSTOPS_SRC = CSRC / "host_ops.cpp"
 HOSTOPS_PATH = PKG_DIR / ("_hostops" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 

@@ -147,7 +147,8 @@ struct SampShared {
 };
 
 // max of (v, idx) with the smaller index on equal values, broadcast to every thread
-__device__ __forceinline__ void block_argmax(SampShared& sh, float& v, int& idx) {
+template <class Sh>
+__device__ __forceinline__ void block_argmax(Sh& sh, float& v, int& idx) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -181,7 +182,8 @@ __device__ __forceinline__ void block_argmax(SampShared& sh, float& v, int& idx)
 }
 
 // fp32 sum in a fixed order (xor tree within warps, then warp order), broadcast
-__device__ __forceinline__ float block_sum_f32(SampShared& sh, float v) {
+template <class Sh>
+__device__ __forceinline__ float block_sum_f32(Sh& sh, float v) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -198,7 +200,8 @@ __device__ __forceinline__ float block_sum_f32(SampShared& sh, float v) {
   return s;
 }
 
-__device__ __forceinline__ unsigned long long block_sum_u64(SampShared& sh, unsigned long long v) {
+template <class Sh>
+__device__ __forceinline__ unsigned long long block_sum_u64(Sh& sh, unsigned long long v) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -216,7 +219,8 @@ __device__ __forceinline__ unsigned long long block_sum_u64(SampShared& sh, unsi
 }
 
 // exclusive prefix of v over the block in thread order, and the block total
-__device__ __forceinline__ unsigned long long block_exscan_u64(SampShared& sh, unsigned long long v,
+template <class Sh>
+__device__ __forceinline__ unsigned long long block_exscan_u64(Sh& sh, unsigned long long v,
                                                                unsigned long long& total) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   unsigned long long inc = v;
@@ -577,6 +581,836 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
   }
 }
 
+// ---------------------------------------------------------------- 16-bit logits (bf16 / f16)
+// The same nucleus rule for 16-bit logits with far less on-chip work.  A cluster of C CTAs
+// holds a row's raw 16-bit logits in shared memory (half the bytes of fp32 probabilities, so
+// a batch of rows fits the GPU in one wave) and recomputes p(x) from them where needed:
+//     p(x) = fdiv(expf(fdiv(x, T) - ymax), z)      (the same operations as sampling_kernel)
+//
+// Candidates.  Only entries with p >= p_min can be kept, where p_min follows from top_p and
+// the vocabulary size: with q = round(p * 2^31), the last kept entry j* has every entry from
+// j* on (in descending order) at q <= q_j*, and those carry the mass Q - excl(j*) >= Q - L
+// (Q the total, L = round(top_p * 2^31)), so V * q_j* >= Q - L; the sum of the rounded p is
+// at least 1 - 2^-12 (it is 1 up to the fp32 rounding of z and of each p), so
+//     q_j* >= (2^31 (1 - 2^-12) - V / 2 - L) / V.
+// Entries below p_min come after every kept entry in the order, so they change neither the
+// cut nor any kept entry's exclusive mass: the select, the tie cut, the kept mass and the
+// draw need only the candidates.  A candidate test on x itself (x >= thr, thr from p_min
+// with a margin far above the rounding of fdiv and expf) lets the candidate pass skip every
+// other entry without computing p; each candidate's exact p goes into a per-CTA list in
+// index order.  Rows whose candidates overflow a list, and rows with top_p >= 1, take the
+// full path: the same steps over every entry, p recomputed in each pass.
+constexpr int kN16Threads = 512;
+constexpr int kN16MaxPerCta = 38912;  // 16-bit logits per CTA (76 KB)
+constexpr int kN16ListCap = 4096;     // candidates per CTA: local index (u16) + p (f32)
+constexpr int kN16Chunk = kN16Threads * 8;  // index-ordered passes: 8 consecutive per thread
+static_assert(kN16Threads / 32 == kSampWarps, "the block reductions assume 16 warps");
+
+struct N16Shared {
+  __align__(16) uint32_t hist_m[2][256];
+  __align__(16) uint32_t hist_c[2][256];
+  float wf[kSampWarps];
+  int wi[kSampWarps];
+  unsigned long long wu[kSampWarps];
+  // values published to the cluster
+  float x_f;
+  int x_i;
+  unsigned long long x_u;
+  // broadcasts
+  uint32_t b_prefix;
+  unsigned long long b_mass;
+  uint32_t b_ties;
+  unsigned long long b_u;
+  float b_f;
+  int b_i;
+  float thr;
+  int found;
+};
+
+__host__ __device__ constexpr size_t n16_list_offset(int per_cta) {
+  return (static_cast<size_t>(per_cta) * 2 + 15) / 16 * 16;
+}
+__host__ __device__ constexpr size_t n16_smem_bytes(int per_cta) {
+  return n16_list_offset(per_cta) + static_cast<size_t>(kN16ListCap) * (2 + 4);
+}
+
+template <typename In>
+__device__ __forceinline__ float h16_to_f32(uint16_t b) {
+  return to_f32<In>(*reinterpret_cast<const In*>(&b));
+}
+
+// x / d rounded to nearest even by Markstein's correction of x * RN(1/d) (P. Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990): with r = RN(1/d) and q0 = RN(x r), the fused q0 + r * (x - d q0) rounds
+// to RN(x / d) whenever nothing leaves the normal range -- guaranteed here by |x| and d in
+// [2^-60, 2^60] and [2^-30, 2^30]; other arguments take the IEEE division.  Three
+// instructions instead of the division's sequence.
+__device__ __forceinline__ float div_rn(float x, float d, float r, bool d_ok) {
+  const float ax = fabsf(x);
+  if (d_ok && ax >= 0x1p-60f && ax <= 0x1p60f) {
+    const float q0 = __fmul_rn(x, r);
+    return __fmaf_rn(__fmaf_rn(-q0, d, x), r, q0);
+  }
+  return __fdiv_rn(x, d);
+}
+__device__ __forceinline__ bool div_ok(float d) { return d >= 0x1p-30f && d <= 0x1p30f; }
+
+// p(x) = RN(expf(RN(x / T) - ymax) / z), the probability sampling_kernel computes
+struct N16Prob {
+  float temp, rt, ymax, z, rz;
+  bool t_ok, z_ok;
+  __device__ __forceinline__ float y(float x) const { return div_rn(x, temp, rt, t_ok); }
+  __device__ __forceinline__ float e(float x) const { return expf(y(x) - ymax); }
+  __device__ __forceinline__ float operator()(float x) const { return div_rn(e(x), z, rz, z_ok); }
+};
+
+// The radix select of sampling_kernel over an entry set given by `each(f)`, which calls
+// f(p) for every entry of this CTA: four 8-bit passes over the bits of p, masses in units of
+// 2^-31, histograms combined across the cluster in rank order.  Returns the threshold bits
+// and sets `above` (the mass of entries above them) and `ties` (entries equal to them).
+// Per pass: the histogram, one block barrier, the cluster barrier, then warp 0 alone reads
+// the cluster's bins (16-byte loads of its 8 bins from every CTA) and picks the digit while
+// the other warps clear the histogram buffer the pass after next will use (every CTA has
+// read it once this pass's cluster barrier is passed), and one more block barrier.
+template <int C, class Each>
+__device__ uint32_t n16_radix_select(N16Shared& sh, unsigned long long limit, Each each,
+                                     unsigned long long& above_out, uint32_t& ties_out) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  for (int b = tid; b < 2 * 256; b += kN16Threads) {
+    (&sh.hist_m[0][0])[b] = 0;
+    (&sh.hist_c[0][0])[b] = 0;
+  }
+  __syncthreads();
+  uint32_t prefix = 0;
+  unsigned long long above = 0;
+  uint32_t ties = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    const int buf = (shift >> 3) & 1;
+    uint32_t* hm = sh.hist_m[buf];
+    uint32_t* hc = sh.hist_c[buf];
+    const uint32_t hi_mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+    each([&](float v) {
+      const uint32_t bits = __float_as_uint(v);
+      if ((bits & hi_mask) == (prefix & hi_mask)) {
+        const uint32_t d = (bits >> shift) & 255u;
+        atomicAdd(&hm[d], to_q31(v));
+        atomicAdd(&hc[d], 1u);
+      }
+    });
+    __syncthreads();
+    samp_cluster_sync();  // every CTA's histogram is complete; the other buffer is free
+    if (tid < 32) {
+      // lane l owns bins 255 - 8l .. 248 - 8l (descending); the cut bin is the lowest
+      // non-empty bin whose mass above (above + all higher bins) is within the limit
+      const int b0 = 248 - 8 * lane;
+      unsigned long long m8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      uint32_t c8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int r = 0; r < C; ++r) {
+        const uint4* pm = cl_ptr(reinterpret_cast<const uint4*>(hm + b0), static_cast<uint32_t>(r));
+        const uint4* pc = cl_ptr(reinterpret_cast<const uint4*>(hc + b0), static_cast<uint32_t>(r));
+        const uint4 ma = pm[0], mb = pm[1], ca = pc[0], cb = pc[1];
+        m8[0] += ma.x; m8[1] += ma.y; m8[2] += ma.z; m8[3] += ma.w;
+        m8[4] += mb.x; m8[5] += mb.y; m8[6] += mb.z; m8[7] += mb.w;
+        c8[0] += ca.x; c8[1] += ca.y; c8[2] += ca.z; c8[3] += ca.w;
+        c8[4] += cb.x; c8[5] += cb.y; c8[6] += cb.z; c8[7] += cb.w;
+      }
+      unsigned long long mine = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mine += m8[j];
+      unsigned long long pre = mine;  // inclusive scan in lane order (descending bins)
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long t = __shfl_up_sync(0xffffffffu, pre, o);
+        if (lane >= o) pre += t;
+      }
+      unsigned long long acc = above + pre - mine;
+      int cand = 256;
+      unsigned long long cand_acc = 0;
+      uint32_t cand_cnt = 0;
+#pragma unroll
+      for (int j = 7; j >= 0; --j) {  // bins b0 + 7 .. b0, descending
+        if (c8[j] > 0 && acc <= limit) {
+          cand = b0 + j;
+          cand_acc = acc;
+          cand_cnt = c8[j];
+        }
+        acc += m8[j];
+      }
+      int best = cand;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
+      if (best == 256) best = 0;  // not reached: the largest entry always qualifies
+      const uint32_t owner = static_cast<uint32_t>((255 - best) / 8);
+      const unsigned long long best_acc = __shfl_sync(0xffffffffu, cand_acc, owner);
+      const uint32_t best_cnt = __shfl_sync(0xffffffffu, cand_cnt, owner);
+      if (lane == 0) {
+        sh.b_prefix = prefix | (static_cast<uint32_t>(best) << shift);
+        sh.b_mass = best_acc;
+        sh.b_ties = best_cnt;
+      }
+    } else if (shift > 0) {
+      uint32_t* zm = sh.hist_m[buf ^ 1];
+      uint32_t* zc = sh.hist_c[buf ^ 1];
+      for (int b = tid - 32; b < 256; b += kN16Threads - 32) {
+        zm[b] = 0;
+        zc[b] = 0;
+      }
+    }
+    __syncthreads();
+    prefix = sh.b_prefix;
+    above = sh.b_mass;
+    ties = sh.b_ties;
+  }
+  __syncthreads();  // the broadcast slots are reused by the caller
+  above_out = above;
+  ties_out = ties;
+  return prefix;
+}
+
+// Index of the k-th (0-based) entry, in index order, for which pred(i) holds among the
+// `count` entries i = 0 .. count-1 of this CTA; -1 if there are not that many.  Entries are
+// taken in chunks of 8 consecutive per thread.  Block-uniform call.
+template <class Pred>
+__device__ int n16_kth(N16Shared& sh, int count, unsigned long long k, Pred pred) {
+  const int tid = threadIdx.x;
+  if (tid == 0) sh.found = -1;
+  __syncthreads();
+  unsigned long long acc = 0;
+  for (int c0 = 0; c0 < count; c0 += kN16Chunk) {
+    const int i0 = c0 + tid * 8;
+    uint32_t bits = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (i0 + j < count && pred(i0 + j)) bits |= 1u << j;
+    unsigned long long tot;
+    const unsigned long long ex = acc + block_exscan_u64(sh, __popc(bits), tot);
+    if (k >= ex && k < ex + __popc(bits)) {
+      unsigned long long r = ex;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (bits & (1u << j)) {
+          if (r == k) sh.found = i0 + j;
+          ++r;
+        }
+    }
+    acc += tot;
+    __syncthreads();
+    if (sh.found >= 0) break;
+  }
+  const int f = sh.found;
+  __syncthreads();
+  return f;
+}
+
+// mode 0 only, In = bf16 or f16.
+template <int C, typename In>
+__global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampParams p) {
+  extern __shared__ __align__(16) uint8_t n16_dyn[];
+  __shared__ N16Shared sh;
+  uint16_t* xs = reinterpret_cast<uint16_t*>(n16_dyn);
+  uint16_t* lidx = reinterpret_cast<uint16_t*>(n16_dyn + n16_list_offset(p.per_cta));
+  float* lp = reinterpret_cast<float*>(n16_dyn + n16_list_offset(p.per_cta) + kN16ListCap * 2);
+  const int tid = threadIdx.x;
+  const uint32_t rank = samp_rank();
+  const int row = blockIdx.x / C;
+  const int64_t lo = static_cast<int64_t>(rank) * p.per_cta;
+  int n = static_cast<int>(p.vocab - lo < p.per_cta ? p.vocab - lo : p.per_cta);
+  if (n < 0) n = 0;
+  const uint16_t* src = static_cast<const uint16_t*>(p.src) + static_cast<int64_t>(row) * p.stride + lo;
+  const float temp = p.temps ? p.temps[row] : p.temp;
+  const float top_p = p.top_ps ? p.top_ps[row] : p.top_p;
+  const bool greedy = !(temp > 0.f);
+
+  // ---- phase 1: stage the raw logits, row max
+  float mx = -INFINITY;
+  {
+    int done = 0;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+      const int nv = n / 8;
+      const uint4* s4 = reinterpret_cast<const uint4*>(src);
+      uint4* x4 = reinterpret_cast<uint4*>(xs);
+#pragma unroll 4
+      for (int v = tid; v < nv; v += kN16Threads) {
+        const uint4 raw = __ldg(s4 + v);
+        x4[v] = raw;
+        const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, h16_to_f32<In>(h[j]));
+      }
+      done = nv * 8;
+    }
+    for (int i = done + tid; i < n; i += kN16Threads) {
+      const uint16_t b = src[i];
+      xs[i] = b;
+      mx = fmaxf(mx, h16_to_f32<In>(b));
+    }
+  }
+  int dummy = 0;
+  block_argmax(sh, mx, dummy);
+  if (tid == 0) sh.x_f = mx;
+  samp_cluster_sync();
+  float xmax = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < C; ++r) xmax = fmaxf(xmax, ld_cl_f32(&sh.x_f, r));
+  samp_cluster_sync();
+
+  float* out = p.probs_out ? p.probs_out + static_cast<int64_t>(row) * p.out_stride + lo : nullptr;
+  if (greedy) {
+    // T <= 0: one-hot at the first index holding the max (core/spec_decode.py:18-21)
+    int first = 0x7fffffff;
+    for (int i = tid; i < n; i += kN16Threads)
+      if (h16_to_f32<In>(xs[i]) == xmax && static_cast<int>(lo) + i < first) first = static_cast<int>(lo) + i;
+    float fv = 0.f;  // equal values: block_argmax keeps the smallest index
+    block_argmax(sh, fv, first);
+    if (tid == 0) sh.x_i = first;
+    samp_cluster_sync();
+    int gidx = 0x7fffffff;
+#pragma unroll
+    for (int r = 0; r < C; ++r) gidx = min(gidx, static_cast<int>(ld_cl_u32(&sh.x_i, r)));
+    samp_cluster_sync();
+    if (out)
+      for (int i = tid; i < n; i += kN16Threads) out[i] = (static_cast<int>(lo) + i == gidx) ? 1.f : 0.f;
+    if (p.tokens && rank == 0 && tid == 0) p.tokens[row] = gidx;
+    return;
+  }
+
+  // ---- phase 2: z = sum of expf(x / T - ymax)
+  N16Prob pr;
+  pr.temp = temp;
+  pr.rt = __frcp_rn(temp);
+  pr.t_ok = div_ok(temp);
+  pr.ymax = __fdiv_rn(xmax, temp);
+  float zs = 0.f;
+  {
+    const uint4* x4 = reinterpret_cast<const uint4*>(xs);
+    const int nv = n / 8;
+    for (int v = tid; v < nv; v += kN16Threads) {
+      const uint4 raw = x4[v];
+      const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw);
+      float part = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) part += pr.e(h16_to_f32<In>(h[j]));
+      zs += part;
+    }
+    for (int i = nv * 8 + tid; i < n; i += kN16Threads) zs += pr.e(h16_to_f32<In>(xs[i]));
+  }
+  zs = block_sum_f32(sh, zs);
+  if (tid == 0) sh.x_f = zs;
+  samp_cluster_sync();
+  float z = 0.f;
+#pragma unroll
+  for (int r = 0; r < C; ++r) z += ld_cl_f32(&sh.x_f, r);
+  samp_cluster_sync();
+  pr.z = z;
+  pr.rz = __frcp_rn(z);
+  pr.z_ok = div_ok(z);
+  auto prob = [&](int i) { return pr(h16_to_f32<In>(xs[i])); };
+
+  // ---- phase 3: candidates (only with a cut)
+  const bool cut = top_p < 1.f;
+  const unsigned long long limit = __double2ull_rn(static_cast<double>(top_p) * 2147483648.0);
+  bool fast = false;
+  int count = 0;
+  if (cut) {
+    if (tid == 0) {
+      const double v = static_cast<double>(p.vocab);
+      const double qmin = (2147483648.0 * (1.0 - 1.0 / 4096.0) - 0.5 * v - static_cast<double>(limit)) / v - 1.0;
+      float thr = -INFINITY;
+      if (qmin > 0.0) {
+        // p >= p_min needs x / T >= ymax + ln(p_min z) up to the rounding of the division,
+        // expf, the subtraction and logf (relative 2^-20 or less); the margin is orders of
+        // magnitude wider
+        const float lq = logf(__double2float_rd(qmin / 2147483648.0));
+        float t = pr.ymax + lq + logf(z);
+        t -= 1e-3f + 1e-5f * fabsf(t);
+        const float xt = t * temp;
+        thr = xt - 1e-5f * fabsf(xt);
+      }
+      sh.thr = thr;
+    }
+    __syncthreads();
+    const float thr = sh.thr;
+    // The candidate indices in index order: warp w owns the contiguous entries
+    // [w * per_w, (w + 1) * per_w), lanes take 8 consecutive entries per 256-entry chunk.
+    // One pass counts (per warp), one block barrier gives every warp its offset, a second
+    // pass writes; then the candidates' p in one dense pass over the list.
+    const int warp = tid >> 5, lane = tid & 31;
+    const int per_w = ((n + kSampWarps - 1) / kSampWarps + 7) / 8 * 8;
+    const int w0 = min(n, warp * per_w), w1 = min(n, w0 + per_w);
+    auto lane_bits = [&](int i0) -> uint32_t {
+      uint32_t bits = 0;
+      if (i0 + 8 <= w1) {
+        const uint4 raw = reinterpret_cast<const uint4*>(xs)[i0 / 8];
+        const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (h16_to_f32<In>(h[j]) >= thr) bits |= 1u << j;
+      } else {
+        for (int j = 0; j < 8; ++j)
+          if (i0 + j < w1 && h16_to_f32<In>(xs[i0 + j]) >= thr) bits |= 1u << j;
+      }
+      return bits;
+    };
+    int wc = 0;
+    for (int c = w0; c < w1; c += 256) wc += __popc(lane_bits(c + 8 * lane));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wc += __shfl_xor_sync(0xffffffffu, wc, o);
+    if (lane == 0) sh.wi[warp] = wc;
+    __syncthreads();
+    int pos = 0;
+    count = 0;
+    for (int w = 0; w < kSampWarps; ++w) {
+      if (w < warp) pos += sh.wi[w];
+      count += sh.wi[w];
+    }
+    for (int c = w0; c < w1; c += 256) {
+      uint32_t bits = lane_bits(c + 8 * lane);
+      const int mine = __popc(bits);
+      int incl = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      int at = pos + incl - mine;
+      while (bits) {
+        const int j = __ffs(bits) - 1;
+        bits &= bits - 1;
+        if (at < kN16ListCap) lidx[at] = static_cast<uint16_t>(c + 8 * lane + j);
+        ++at;
+      }
+      pos += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    __syncthreads();
+    for (int j = tid; j < count && j < kN16ListCap; j += kN16Threads) lp[j] = prob(lidx[j]);
+    if (tid == 0) sh.x_i = count;
+    __syncthreads();
+    samp_cluster_sync();
+    int worst = 0;
+#pragma unroll
+    for (int r = 0; r < C; ++r) worst = max(worst, static_cast<int>(ld_cl_u32(&sh.x_i, r)));
+    samp_cluster_sync();
+    fast = worst <= kN16ListCap;
+  }
+  // every entry of this CTA's set, as f(p) (list entries, or every logit)
+  auto each = [&](auto&& f) {
+    if (fast) {
+      for (int j = tid; j < count; j += kN16Threads) f(lp[j]);
+    } else {
+      for (int i = tid; i < n; i += kN16Threads) f(prob(i));
+    }
+  };
+
+  // ---- phase 4: top-p threshold, then the index at which a tied group is cut
+  uint32_t tbits = 0;
+  int i_cut = 0x7fffffff;  // ties at tbits are kept below this global index
+  if (cut) {
+    unsigned long long above;
+    uint32_t ties;
+    tbits = n16_radix_select<C>(sh, limit, each, above, ties);
+    const unsigned long long tq = to_q31(__uint_as_float(tbits));
+    uint32_t keep_ties = ties;
+    if (tq > 0) {
+      const unsigned long long room = (limit - above) / tq + 1;  // above <= limit
+      if (room < keep_ties) keep_ties = static_cast<uint32_t>(room);
+    }
+    if (keep_ties < ties) {
+      // the first dropped tie is the keep_ties-th tie in index order
+      unsigned long long mine = 0;
+      each([&](float v) { mine += __float_as_uint(v) == tbits ? 1u : 0u; });
+      mine = block_sum_u64(sh, mine);
+      if (tid == 0) sh.x_u = mine;
+      samp_cluster_sync();
+      unsigned long long before = 0;
+      for (uint32_t r = 0; r < rank; ++r) before += ld_cl_u64(&sh.x_u, r);
+      samp_cluster_sync();
+      int local_cut = -1;
+      if (keep_ties >= before && keep_ties < before + mine) {
+        const unsigned long long k = keep_ties - before;
+        local_cut = fast ? n16_kth(sh, count, k, [&](int j) { return __float_as_uint(lp[j]) == tbits; })
+                         : n16_kth(sh, n, k, [&](int i) { return __float_as_uint(prob(i)) == tbits; });
+        if (fast && local_cut >= 0) local_cut = lidx[local_cut];
+      }
+      if (tid == 0) sh.x_i = local_cut >= 0 ? static_cast<int>(lo) + local_cut : 0x7fffffff;
+      samp_cluster_sync();
+#pragma unroll
+      for (int r = 0; r < C; ++r) i_cut = min(i_cut, static_cast<int>(ld_cl_u32(&sh.x_i, r)));
+      samp_cluster_sync();
+    }
+  }
+  auto kept = [&](float v, int gi) {
+    const uint32_t b = __float_as_uint(v);
+    return !cut || b > tbits || (b == tbits && gi < i_cut);
+  };
+
+  // ---- kept mass in units of 2^-52: this CTA's share, the shares before it, the total
+  constexpr float kFx = 4503599627370496.0f;
+  unsigned long long local = 0;
+  if (fast) {
+    for (int j = tid; j < count; j += kN16Threads) {
+      const float v = lp[j];
+      if (kept(v, static_cast<int>(lo) + lidx[j])) local += to_fixed(v, kFx);
+    }
+  } else {
+    for (int i = tid; i < n; i += kN16Threads) {
+      const float v = prob(i);
+      if (kept(v, static_cast<int>(lo) + i)) local += to_fixed(v, kFx);
+    }
+  }
+  local = block_sum_u64(sh, local);
+  if (tid == 0) sh.x_u = local;
+  samp_cluster_sync();
+  unsigned long long base = 0, total = 0;
+#pragma unroll
+  for (int r = 0; r < C; ++r) {
+    const unsigned long long v = ld_cl_u64(&sh.x_u, r);
+    if (r < static_cast<int>(rank)) base += v;
+    total += v;
+  }
+  samp_cluster_sync();
+
+  // ---- phase 5: renormalised probabilities
+  if (out) {
+    const float s = static_cast<float>(static_cast<double>(total) / kFixedOne);
+    if (fast) {
+      // zeros everywhere, then the kept candidates (the barrier orders the two stores)
+      int done = 0;
+      if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+        const int nv = n / 4;
+        float4* out4 = reinterpret_cast<float4*>(out);
+        for (int v = tid; v < nv; v += kN16Threads) out4[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+        done = nv * 4;
+      }
+      for (int i = done + tid; i < n; i += kN16Threads) out[i] = 0.f;
+      __syncthreads();
+      for (int j = tid; j < count; j += kN16Threads) {
+        const float v = lp[j];
+        if (v > 0.f && kept(v, static_cast<int>(lo) + lidx[j])) out[lidx[j]] = __fdiv_rn(v, s);
+      }
+    } else {
+      for (int i = tid; i < n; i += kN16Threads) {
+        const float v = prob(i);
+        out[i] = (v > 0.f && kept(v, static_cast<int>(lo) + i)) ? __fdiv_rn(v, s) : 0.f;
+      }
+    }
+  }
+
+  // ---- phase 6: one draw, inverse CDF in index order over the kept masses
+  if (p.tokens) {
+    if (total == 0) {
+      if (rank == 0 && tid == 0) {
+        p.tokens[row] = -1;
+        report_error(p.error_word, INFERD_ERR_INVALID_ARGUMENT);
+      }
+      return;
+    }
+    const unsigned long long target = __umul64hi(philox_u64(p.seed, p.offset + static_cast<uint64_t>(row)), total);
+    if (target >= base && target < base + local) {
+      // weights of the entries of this CTA in index order (candidates or every logit)
+      const int m = fast ? count : n;
+      if (tid == 0) sh.found = 0;
+      __syncthreads();
+      unsigned long long acc0 = base;
+      for (int c0 = 0; c0 < m; c0 += kN16Chunk) {
+        const int i0 = c0 + tid * 8;
+        unsigned long long q[8];
+        unsigned long long mine = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          q[j] = 0;
+          if (i0 + j < m) {
+            const int li = fast ? lidx[i0 + j] : i0 + j;
+            const float v = fast ? lp[i0 + j] : prob(i0 + j);
+            if (kept(v, static_cast<int>(lo) + li)) q[j] = to_fixed(v, kFx);
+          }
+          mine += q[j];
+        }
+        unsigned long long tot_chunk;
+        const unsigned long long ex = acc0 + block_exscan_u64(sh, mine, tot_chunk);
+        if (target >= ex && target < ex + mine) {
+          unsigned long long acc = ex;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            acc += q[j];
+            if (acc > target) {
+              p.tokens[row] = lo + (fast ? lidx[i0 + j] : i0 + j);
+              sh.found = 1;
+              break;
+            }
+          }
+        }
+        acc0 += tot_chunk;
+        __syncthreads();
+        if (sh.found) break;
+      }
+    }
+  }
+}
+
+template <int C, typename In>
+int launch_nucleus16(const SampParams& p, cudaStream_t s) {
+  const size_t smem = n16_smem_bytes(p.per_cta);
+  static bool configured[64] = {false};
+  const int dev = current_device();
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(nucleus16_kernel<C, In>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(n16_smem_bytes(kN16MaxPerCta)));
+    if (e != cudaSuccess) return cuda_status(e);
+    e = cudaFuncSetAttribute(nucleus16_kernel<C, In>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return cuda_status(e);
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.rows) * C);
+  cfg.blockDim = dim3(kN16Threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, nucleus16_kernel<C, In>, p));
+}
+
+// 16-bit logits: the candidate kernel when a row fits 8 CTAs' shared memory; false otherwise
+template <typename In>
+bool dispatch_nucleus16(SampParams& p, cudaStream_t s, int* status) {
+  int c = 1;
+  while (c < 8 && (p.vocab + c - 1) / c > kN16MaxPerCta) c <<= 1;
+  const int64_t per = ((p.vocab + c - 1) / c + 7) / 8 * 8;  // 16-byte aligned CTA slices
+  if (per > kN16MaxPerCta) return false;
+  p.per_cta = static_cast<int32_t>(per);
+  switch (c) {
+    case 1: *status = launch_nucleus16<1, In>(p, s); break;
+    case 2: *status = launch_nucleus16<2, In>(p, s); break;
+    case 4: *status = launch_nucleus16<4, In>(p, s); break;
+    default: *status = launch_nucleus16<8, In>(p, s); break;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- speculative accept / resample
+// core/spec_decode.py:145-161 for a batch of sequences in one launch.  For sequence b, draft
+// token k (x = proposals[b][k]) is accepted when u_k <= p[b][k][x] / q[b][k][x] (fp32
+// division; u_k uniform on the float32 grid of [0, 1), Philox stream 1 + k).  At the first
+// rejection one token is drawn from clamp(p[b][k] - q[b][k], 0) -- from p[b][k] when that is
+// all zero -- and the round ends; when all gamma drafts are accepted the bonus token is drawn
+// from p[b][gamma].  The draw is sample_from's rule (power-of-two fixed point, inverse CDF in
+// index order, Philox stream 0), so the reference's loop of host syncs (one .item() per draft
+// token) becomes one launch.  One cluster of C CTAs per sequence; CTA r scans entries
+// [r * per_cta, (r + 1) * per_cta) of the chosen distribution straight from global memory.
+constexpr int kSpecThreads = 512;
+
+struct SpecParams {
+  const float* p;            // [rows][gamma + 1][vocab] at strides p_row, p_dist
+  const float* q;            // [rows][gamma][vocab]     at strides q_row, q_dist
+  int64_t p_row, p_dist, q_row, q_dist;
+  const int64_t* proposals;  // [rows][prop_row]
+  int64_t prop_row;
+  int32_t rows, gamma;
+  int64_t vocab;
+  int32_t per_cta;
+  int32_t* accepted;         // [rows]
+  int64_t* tokens;           // [rows][tok_row], gamma + 1 used: accepted drafts, the draw, -1
+  int64_t tok_row;
+  uint64_t seed, offset;
+  int32_t* error_word;
+};
+
+struct SpecShared {
+  float wf[kSampWarps];
+  int wi[kSampWarps];
+  unsigned long long wu[kSampWarps];
+  float b_f;
+  int b_i;
+  unsigned long long b_u;
+  float x_f;
+  unsigned long long x_u;
+  int kstar;
+  int found;
+};
+
+__device__ __forceinline__ float spec_uniform(uint64_t seed, uint64_t n, uint32_t stream) {
+  uint32_t c[4] = {static_cast<uint32_t>(n), static_cast<uint32_t>(n >> 32), stream, 0u};
+  uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    philox_round(c, k0, k1);
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return static_cast<float>(c[0] >> 8) * 0x1p-24f;
+}
+
+template <int C>
+__global__ void __launch_bounds__(kSpecThreads) spec_accept_kernel(const SpecParams p) {
+  __shared__ SpecShared sh;
+  const int tid = threadIdx.x;
+  const uint32_t rank = samp_rank();
+  const int row = blockIdx.x / C;
+  const int64_t lo = static_cast<int64_t>(rank) * p.per_cta;
+  int n = static_cast<int>(p.vocab - lo < p.per_cta ? p.vocab - lo : p.per_cta);
+  if (n < 0) n = 0;
+  const uint64_t ctr = p.offset + static_cast<uint64_t>(row);
+  const float* prow = p.p + static_cast<int64_t>(row) * p.p_row;
+  const float* qrow = p.q + static_cast<int64_t>(row) * p.q_row;
+  const int64_t* props = p.proposals + static_cast<int64_t>(row) * p.prop_row;
+
+  // ---- the accept decisions (cheap: gamma ratios), the same in every CTA of the cluster
+  if (tid == 0) {
+    int kstar = p.gamma;
+    for (int k = 0; k < p.gamma; ++k) {
+      const int64_t x = props[k];
+      if (x < 0 || x >= p.vocab) {  // not a token: rejected (and reported)
+        report_error(p.error_word, INFERD_ERR_INVALID_ARGUMENT);
+        kstar = k;
+        break;
+      }
+      const float ratio = __fdiv_rn(prow[k * p.p_dist + x], qrow[k * p.q_dist + x]);
+      if (!(spec_uniform(p.seed, ctr, 1u + static_cast<uint32_t>(k)) <= ratio)) {
+        kstar = k;
+        break;
+      }
+    }
+    sh.kstar = kstar;
+  }
+  __syncthreads();
+  const int kstar = sh.kstar;
+  const bool resid = kstar < p.gamma;
+  const float* pd = prow + static_cast<int64_t>(kstar) * p.p_dist + lo;
+  const float* qd = resid ? qrow + static_cast<int64_t>(kstar) * p.q_dist + lo : nullptr;
+
+  // ---- weights: the residual clamp(p - q, 0), else the bonus distribution; a residual with
+  // no positive entry falls back to p (the reference's `total > 0` test)
+  bool use_q = resid;
+  float fxs = 0.f;
+  unsigned long long local = 0, base = 0, total = 0;
+  for (int attempt = 0; attempt < 2; ++attempt) {
+    auto weight = [&](int i) {
+      const float a = __ldg(pd + i);
+      return use_q ? fmaxf(a - __ldg(qd + i), 0.f) : a;
+    };
+    float wmax = 0.f;
+    bool bad = false;
+    for (int i = tid; i < n; i += kSpecThreads) {
+      const float w = weight(i);
+      if (!(w >= 0.f) || w == INFINITY) bad = true;
+      else wmax = fmaxf(wmax, w);
+    }
+    if (bad) report_error(p.error_word, INFERD_ERR_INVALID_ARGUMENT);
+    int dummy = 0;
+    block_argmax(sh, wmax, dummy);
+    if (tid == 0) sh.x_f = wmax;
+    samp_cluster_sync();
+    float gmax = 0.f;
+#pragma unroll
+    for (int r = 0; r < C; ++r) gmax = fmaxf(gmax, ld_cl_f32(&sh.x_f, r));
+    samp_cluster_sync();
+    // 2^(52 - k) with 2^k >= vocab * max weight (sample_from's scale)
+    int ex = 0;
+    frexpf(gmax, &ex);
+    const int lv = p.vocab > 1 ? 64 - __clzll(static_cast<unsigned long long>(p.vocab - 1)) : 0;
+    int kk = ex + lv;
+    if (kk < 0) kk = 0;
+    fxs = ldexpf(1.f, 52 - kk);
+    local = 0;
+    for (int i = tid; i < n; i += kSpecThreads) {
+      const float w = weight(i);
+      if (w >= 0.f && w != INFINITY) local += to_fixed(w, fxs);
+    }
+    local = block_sum_u64(sh, local);
+    if (tid == 0) sh.x_u = local;
+    samp_cluster_sync();
+    base = 0;
+    total = 0;
+#pragma unroll
+    for (int r = 0; r < C; ++r) {
+      const unsigned long long v = ld_cl_u64(&sh.x_u, r);
+      if (r < static_cast<int>(rank)) base += v;
+      total += v;
+    }
+    samp_cluster_sync();
+    if (total > 0 || !use_q) break;
+    use_q = false;  // all-zero residual: draw from p[kstar] itself
+  }
+
+  // ---- outputs: the accepted drafts and the count (CTA 0), then the draw
+  int64_t* tok = p.tokens + static_cast<int64_t>(row) * p.tok_row;
+  if (rank == 0) {
+    for (int k = tid; k <= p.gamma; k += kSpecThreads) {
+      if (k < kstar) tok[k] = props[k];
+      else if (k > kstar) tok[k] = -1;
+    }
+    if (tid == 0) p.accepted[row] = kstar;
+  }
+  if (total == 0) {
+    if (rank == 0 && tid == 0) {
+      tok[kstar] = -1;
+      report_error(p.error_word, INFERD_ERR_INVALID_ARGUMENT);
+    }
+    return;
+  }
+  const unsigned long long target = __umul64hi(philox_u64(p.seed, ctr), total);
+  if (target >= base && target < base + local) {
+    if (tid == 0) sh.found = 0;
+    __syncthreads();
+    unsigned long long acc0 = base;
+    for (int c0 = 0; c0 < n; c0 += kSpecThreads * 8) {
+      const int i0 = c0 + tid * 8;
+      unsigned long long qv[8];
+      unsigned long long mine = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        qv[j] = 0;
+        if (i0 + j < n) {
+          const float a = __ldg(pd + i0 + j);
+          const float w = use_q ? fmaxf(a - __ldg(qd + i0 + j), 0.f) : a;
+          if (w >= 0.f && w != INFINITY) qv[j] = to_fixed(w, fxs);
+        }
+        mine += qv[j];
+      }
+      unsigned long long tot_chunk;
+      const unsigned long long ex = acc0 + block_exscan_u64(sh, mine, tot_chunk);
+      if (target >= ex && target < ex + mine) {
+        unsigned long long acc = ex;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          acc += qv[j];
+          if (acc > target) {
+            tok[kstar] = lo + i0 + j;
+            sh.found = 1;
+            break;
+          }
+        }
+      }
+      acc0 += tot_chunk;
+      __syncthreads();
+      if (sh.found) break;
+    }
+  }
+}
+
+template <int C>
+int launch_spec(const SpecParams& p, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.rows) * C);
+  cfg.blockDim = dim3(kSpecThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, spec_accept_kernel<C>, p));
+}
+
 template <int C, typename In>
 int launch_sampling(const SampParams& p, cudaStream_t s) {
   const size_t smem = static_cast<size_t>(p.per_cta) * sizeof(float);
@@ -652,9 +1486,10 @@ extern "C" INFERD_API int inferd_nucleus_sample(float* probs_out, int64_t out_st
   p.offset = offset;
   p.error_word = error_word;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = INFERD_OK;
   if (dtype == INFERD_F32) return dispatch_cluster<float>(p, s);
-  if (dtype == INFERD_BF16) return dispatch_cluster<__nv_bfloat16>(p, s);
-  if (dtype == INFERD_F16) return dispatch_cluster<__half>(p, s);
+  if (dtype == INFERD_BF16) return dispatch_nucleus16<__nv_bfloat16>(p, s, &st) ? st : dispatch_cluster<__nv_bfloat16>(p, s);
+  if (dtype == INFERD_F16) return dispatch_nucleus16<__half>(p, s, &st) ? st : dispatch_cluster<__half>(p, s);
   return INFERD_ERR_UNSUPPORTED;
 }
 
@@ -678,4 +1513,49 @@ extern "C" INFERD_API int inferd_sample_probs(int64_t* tokens, const float* prob
   p.offset = offset;
   p.error_word = error_word;
   return dispatch_cluster<float>(p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" INFERD_API int inferd_spec_accept(int32_t* accepted, int64_t* tokens, int64_t tokens_stride,
+                                             const float* p, int64_t p_seq_stride, int64_t p_dist_stride,
+                                             const float* q, int64_t q_seq_stride, int64_t q_dist_stride,
+                                             const int64_t* proposals, int64_t proposals_stride,
+                                             int32_t rows, int32_t gamma, int64_t vocab, uint64_t seed,
+                                             uint64_t offset, int32_t* error_word, void* stream) {
+  if (rows < 0 || gamma < 0 || vocab <= 0) return INFERD_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return INFERD_OK;
+  if (!accepted || !tokens || !p || (gamma > 0 && (!q || !proposals))) return INFERD_ERR_INVALID_ARGUMENT;
+  if (tokens_stride < gamma + 1 || p_dist_stride < vocab || p_seq_stride < (gamma + 1) * p_dist_stride ||
+      (gamma > 0 && (q_dist_stride < vocab || q_seq_stride < gamma * q_dist_stride ||
+                     proposals_stride < gamma)))
+    return INFERD_ERR_INVALID_ARGUMENT;
+  if (vocab > 0x7fffffff) return INFERD_ERR_UNSUPPORTED;
+  SpecParams sp = {};
+  sp.p = p;
+  sp.q = gamma > 0 ? q : p;
+  sp.p_row = p_seq_stride;
+  sp.p_dist = p_dist_stride;
+  sp.q_row = q_seq_stride;
+  sp.q_dist = q_dist_stride;
+  sp.proposals = gamma > 0 ? proposals : reinterpret_cast<const int64_t*>(tokens);
+  sp.prop_row = proposals_stride;
+  sp.rows = rows;
+  sp.gamma = gamma;
+  sp.vocab = vocab;
+  sp.accepted = accepted;
+  sp.tokens = tokens;
+  sp.tok_row = tokens_stride;
+  sp.seed = seed;
+  sp.offset = offset;
+  sp.error_word = error_word;
+  // CTAs per sequence: enough to spread a batch over the SMs, each scanning >= 8192 entries
+  int c = 1;
+  while (c < 8 && static_cast<int64_t>(rows) * c * 2 <= current_sm_count() && vocab / (2 * c) >= 8192) c <<= 1;
+  sp.per_cta = static_cast<int32_t>(((vocab + c - 1) / c + 7) / 8 * 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (c) {
+    case 1: return launch_spec<1>(sp, s);
+    case 2: return launch_spec<2>(sp, s);
+    case 4: return launch_spec<4>(sp, s);
+    default: return launch_spec<8>(sp, s);
+  }
 }

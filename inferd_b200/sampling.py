@@ -124,3 +124,45 @@ def sample_nucleus(logits: torch.Tensor, temperature, top_p, *,
                             want_tokens=True, generator=generator)
     tokens = tokens.view(-1, 1)
     return (tokens, probs.view(logits.shape)) if return_probs else tokens
+
+
+def accept_resample(p: torch.Tensor, q: torch.Tensor, proposals: torch.Tensor, *,
+                    generator: torch.Generator | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """The accept / resample step of a speculative round (core/spec_decode.py:145-161) for a
+    batch, in one launch and without host synchronisation.
+
+    p [B, gamma + 1, V] fp32: the target's probabilities (p[:, k] verifies draft token k,
+    p[:, gamma] is the bonus distribution); q [B, gamma, V] fp32: the draft's; proposals
+    [B, gamma] int64.  Returns (accepted [B] int32, tokens [B, gamma + 1] int64): sequence b
+    emits tokens[b, :accepted[b] + 1] (the accepted drafts, then the token drawn from the
+    residual clamp(p - q, 0) at the first rejection, or from p[:, gamma] when all were
+    accepted); the remaining entries are -1.  Random draws follow the kernels' Philox
+    streams under a seed taken from `generator` (torch's default generator when None), so
+    they are reproducible under torch.manual_seed but are not torch.rand / torch.multinomial's.
+    """
+    dev = _lib.require_cuda(p, q, proposals)
+    if p.ndim != 3 or q.ndim != 3 or proposals.ndim != 2:
+        raise ValueError("expected p [B, gamma + 1, V], q [B, gamma, V], proposals [B, gamma]")
+    b, g1, vocab = p.shape
+    gamma = g1 - 1
+    if tuple(q.shape) != (b, gamma, vocab) or tuple(proposals.shape) != (b, gamma):
+        raise ValueError(f"q must be [{b}, {gamma}, {vocab}] and proposals [{b}, {gamma}]")
+    if vocab > _MAX_VOCAB:
+        raise ValueError(f"vocab {vocab} exceeds {_MAX_VOCAB}")
+    p = p.float().contiguous()
+    q = q.float().contiguous()
+    props = proposals.to(torch.int64).contiguous()
+    accepted = torch.empty((b,), dtype=torch.int32, device=dev)
+    tokens = torch.empty((b, gamma + 1), dtype=torch.int64, device=dev)
+    if b == 0:
+        return accepted, tokens
+    lib = _lib.load()
+    st = lib.inferd_spec_accept(
+        accepted.data_ptr(), tokens.data_ptr(), gamma + 1, p.data_ptr(), (gamma + 1) * vocab, vocab,
+        q.data_ptr() if gamma else None, gamma * vocab, vocab, props.data_ptr() if gamma else None,
+        max(gamma, 1), b, gamma, vocab, _seed(generator), 0, _lib.error_word(dev).data_ptr(),
+        _lib.stream_of(dev))
+    _lib.check(st, "spec_accept")
+    if _SYNC_CHECKS:
+        _lib.raise_device_errors(dev)
+    return accepted, tokens

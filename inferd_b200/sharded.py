@@ -181,3 +181,132 @@ class OutputGather:
             if self._work[i] is not None:
                 self._work[i].wait()
                 self._work[i] = None
+
+
+class _DeviceBytes:
+    """A raw device allocation seen by torch through the CUDA array interface (no copy, no
+    ownership)."""
+
+    def __init__(self, ptr: int, nbytes: int) -> None:
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+class PeerGather:
+    """Per-step gather of equal-sized per-rank outputs through NVLink peer memory, without
+    a collective call on the data path (the kernels of csrc/peer.cu).
+
+    Every rank allocates one buffer in its own HBM (flags, then two slots of world x rows
+    outputs) and maps every other rank's buffer through CUDA IPC; the process group is
+    used once, to exchange the IPC handles.  push(local) copies this rank's rows into the
+    current slot of every rank's buffer and publishes the step's epoch; wait() orders the
+    current stream after every rank's push of that epoch (a bounded device-side wait: a
+    rank that stops publishing leaves INFERD_ERR_DEVICE_TIMEOUT in the error word instead
+    of a hung GPU) and returns this rank's slot, [world * rows, *tail] in rank order.  Each
+    push must be followed by its wait before the next push: that is what keeps a rank
+    from overwriting a slot a peer may still read (the slot is rewritten two steps later,
+    after every rank has pushed the step in between).
+    """
+
+    FLAG_BYTES = 256
+
+    def __init__(self, tail: tuple[int, ...], dtype: torch.dtype, device: torch.device,
+                 rows_per_rank: int, *, group=None, timeout_s: float = 2.0) -> None:
+        import ctypes
+
+        from . import _lib
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 64:
+            raise ValueError("at most 64 ranks")
+        self.device = torch.device(device)
+        self.tail = tuple(int(t) for t in tail)
+        self.rows = int(rows_per_rank)
+        self.dtype = dtype
+        elems = self.rows
+        for t in self.tail:
+            elems *= t
+        self.bytes_per_rank = elems * torch.empty(0, dtype=dtype).element_size()
+        if self.bytes_per_rank % 16 != 0:
+            raise ValueError("one rank's rows must be a multiple of 16 bytes")
+        self.timeout_ns = int(timeout_s * 1e9)
+        slot_bytes = self.world * self.bytes_per_rank
+        total = self.FLAG_BYTES + 2 * slot_bytes
+        self._lib = lib = _lib.load()
+        self._opened: list[int] = []
+        self._own = None
+        with torch.cuda.device(self.device):
+            ptr = ctypes.c_void_p()
+            handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+            _lib.check(lib.inferd_peer_alloc(total, ctypes.byref(ptr), handle), "peer_alloc")
+            self._own = ptr.value
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle.raw), group=group)
+            bases = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                _lib.check(lib.inferd_peer_open(ctypes.create_string_buffer(h, _lib.IPC_HANDLE_BYTES),
+                                                ctypes.byref(p)), "peer_open")
+                self._opened.append(p.value)
+                bases.append(p.value)
+            self._dst = [torch.tensor([b + self.FLAG_BYTES + s * slot_bytes for b in bases],
+                                      dtype=torch.int64, device=self.device) for s in range(2)]
+            self._flags = torch.tensor(bases, dtype=torch.int64, device=self.device)
+            own = torch.as_tensor(_DeviceBytes(self._own, total), device=self.device)
+            self._slots = [own[self.FLAG_BYTES + s * slot_bytes:self.FLAG_BYTES + (s + 1) * slot_bytes]
+                           .view(dtype).view((self.world * self.rows,) + self.tail) for s in range(2)]
+        self._epoch = 0
+        self._pending = False
+        dist.barrier(group=group)  # every buffer is mapped everywhere before the first push
+
+    def push(self, local: torch.Tensor) -> None:
+        """Copy this rank's rows ([rows, *tail], contiguous, on this device) into every rank's
+        current slot and publish the step; enqueued on the current stream."""
+        from . import _lib
+
+        if self._pending:
+            raise RuntimeError("wait() for the previous push before the next one")
+        if tuple(local.shape) != (self.rows,) + self.tail or local.dtype != self.dtype \
+                or local.device != self.device or not local.is_contiguous():
+            raise ValueError("local must be a contiguous [rows, *tail] tensor of this gather's "
+                             "dtype on its device")
+        self._epoch += 1
+        st = self._lib.inferd_gather_push(
+            local.data_ptr(), self.bytes_per_rank, self._dst[self._epoch & 1].data_ptr(),
+            self._flags.data_ptr(), self.rank, self.world, self._epoch & 0xFFFFFFFF,
+            _lib.stream_of(self.device))
+        _lib.check(st, "gather_push")
+        self._pending = True
+
+    def wait(self) -> torch.Tensor:
+        """Order the current stream after every rank's push of this step; returns this rank's
+        slot, [world * rows, *tail] in rank order, valid until the push after next."""
+        from . import _lib
+
+        if not self._pending:
+            raise RuntimeError("no push to wait for")
+        st = self._lib.inferd_gather_wait(self._own, self.world, self._epoch & 0xFFFFFFFF,
+                                          self.timeout_ns, _lib.error_word(self.device).data_ptr(),
+                                          _lib.stream_of(self.device))
+        _lib.check(st, "gather_wait")
+        self._pending = False
+        return self._slots[self._epoch & 1]
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective: every rank calls it)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no rank still writes into a buffer being released
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                self._lib.inferd_peer_close(p)
+            self._opened = []
+            self._slots = []
+            self._lib.inferd_peer_free(self._own)
+        self._own = None

@@ -42,10 +42,12 @@ from .fp8 import (  # noqa: F401
     quantize_per_channel,
 )
 from .sampling import (  # noqa: F401
+    accept_resample,
     kept_mask_fixed,
     nucleus_probs,
     philox4x32_10,
     row_random64,
+    row_uniform,
     sample_fixed,
     to_fixed,
     weight_scale,

@@ -131,3 +131,42 @@ def row_random64(seed: int, offset: int, row: int) -> int:
     n = int(offset) + int(row)
     out = philox4x32_10([n & _MASK, (n >> 32) & _MASK, 0, 0], [seed & _MASK, (seed >> 32) & _MASK])
     return (out[0] << 32) | out[1]
+
+
+def row_uniform(seed: int, offset: int, row: int, stream: int) -> np.float32:
+    """The uniform in [0, 1) the accept step draws for `row` on `stream` (1 + draft index):
+    Philox4x32-10, key = seed, counter = (offset + row (low, high words), stream, 0); the
+    top 24 bits of output word 0 times 2^-24 (the float32 grid torch.rand draws from)."""
+    n = int(offset) + int(row)
+    out = philox4x32_10([n & _MASK, (n >> 32) & _MASK, int(stream) & _MASK, 0],
+                        [seed & _MASK, (seed >> 32) & _MASK])
+    return np.float32((out[0] >> 8) * 2.0 ** -24)
+
+
+def accept_resample(p, q, proposals, seed: int, offset: int, row: int):
+    """core/spec_decode.py:145-161 for one sequence.  p [gamma + 1, V] are the target's
+    probabilities (p[k] verifies draft token k, p[gamma] is the bonus distribution), q
+    [gamma, V] the draft's, proposals [gamma] the drafted tokens.  Draft token k is accepted
+    when u_k <= p[k][x_k] / q[k][x_k] (float32 division, u_k = row_uniform(.., 1 + k)); at the
+    first rejection one token is drawn from clamp(p[k] - q[k], 0) (from p[k] when that is all
+    zero) and the round ends; if every draft is accepted the bonus token is drawn from
+    p[gamma].  Draws use sample_fixed with row_random64(seed, offset, row).  Returns
+    (number accepted, emitted tokens), the tokens being the accepted drafts then the draw."""
+    p = np.asarray(p, dtype=np.float32)
+    q = np.asarray(q, dtype=np.float32)
+    gamma = q.shape[0]
+    emitted = []
+    for k in range(gamma):
+        x = int(proposals[k])
+        with np.errstate(divide="ignore", invalid="ignore"):
+            ratio = np.float32(p[k, x]) / np.float32(q[k, x])
+        if row_uniform(seed, offset, row, 1 + k) <= ratio:
+            emitted.append(x)
+            continue
+        w = np.maximum(p[k] - q[k], np.float32(0.0)).astype(np.float32)
+        if not np.any(w > 0):
+            w = p[k]
+        emitted.append(sample_fixed(w, row_random64(seed, offset, row)))
+        return k, emitted
+    emitted.append(sample_fixed(p[gamma], row_random64(seed, offset, row)))
+    return gamma, emitted

@@ -53,8 +53,11 @@ def _boundary_ok(got: np.ndarray, logits: np.ndarray, t: float, p: float) -> Non
             pos = np.empty_like(order)
             pos[order] = np.arange(order.size)
             assert np.all(np.abs(excl[pos[diff]] - p) < 5e-4), f"row {r}: {diff.size} entries differ"
+        # an entry the two rules decide differently changes the renormalisation; compare the
+        # distributions renormalised over the entries both keep
         keep = (got[r] > 0) & (ref[r] > 0)
-        np.testing.assert_allclose(got[r][keep], ref[r][keep], rtol=1e-4)
+        a, b = got[r][keep].astype(np.float64), ref[r][keep].astype(np.float64)
+        np.testing.assert_allclose(a / a.sum(), b / b.sum(), rtol=1e-4)
 
 
 @pytest.mark.parametrize("vocab", [7, 5000, 32768 + 17, 100000, 151936, 262144])
@@ -171,3 +174,85 @@ def test_zero_row_is_an_error(cuda_device):
     p[0, 3] = 1.0
     with pytest.raises(ValueError):
         sample_from(p)
+
+
+# ------------------------------------------------------------------ 16-bit logits
+# bf16 / f16 logits take the candidate kernel: the top-p select runs over the entries whose
+# p can reach the cut (a bound from top_p and the vocabulary size), or over every entry when
+# the candidates overflow the per-CTA lists.  Both must follow the same rule.
+
+@pytest.mark.parametrize("scale,t,top_p", [(3.0, 0.7, 0.9), (5.0, 1.0, 0.8), (3.0, 1.3, 0.5),
+                                           (8.0, 0.5, 0.99), (2.0, 0.7, 0.95)])
+def test_nucleus_probs_bf16_rows(cuda_device, scale, t, top_p):
+    # (3.0, 0.7, 0.9) is the sampling benchmark's row; (2.0, 0.7, 0.95) overflows the lists
+    g = torch.Generator().manual_seed(int(scale * 100 + t * 10))
+    logits = (torch.randn(6, 151936, generator=g) * scale).to(torch.bfloat16)
+    got = nucleus_probs(logits.to(cuda_device), t, top_p).cpu().numpy()
+    _boundary_ok(got, logits.float().numpy(), t, top_p)
+    np.testing.assert_allclose(got.sum(axis=1), 1.0, rtol=1e-5)
+    # the fp32 kernel on the same values: the same kept entries (its z is summed in another
+    # order, which may move an entry sitting exactly on the cut) and the same values
+    ref32 = nucleus_probs(logits.float().to(cuda_device), t, top_p).cpu().numpy()
+    for r in range(got.shape[0]):
+        assert np.count_nonzero((got[r] > 0) != (ref32[r] > 0)) <= 2
+        both = (got[r] > 0) & (ref32[r] > 0)
+        a, b = got[r][both].astype(np.float64), ref32[r][both].astype(np.float64)
+        np.testing.assert_allclose(a / a.sum(), b / b.sum(), rtol=1e-5)
+
+
+def test_bf16_tied_group_cut_across_ctas_in_index_order(cuda_device):
+    # 256 equal logits scattered over a 151936 vocabulary (four CTAs), everything else so far
+    # below that z rounds to 256 exactly: each tied p is 2^-8, q = 2^23 units of 2^-31, so
+    # top_p = 0.3 keeps floor(0.3 * 2^31 / 2^23) + 1 = 77 of them, the first 77 in index order
+    vocab = 151936
+    logits = torch.full((2, vocab), -40.0)
+    g = torch.Generator().manual_seed(11)
+    pos = torch.randperm(vocab, generator=g)[:256].sort().values
+    logits[:, pos] = 10.0
+    logits = logits.to(torch.bfloat16)
+    got = nucleus_probs(logits.to(cuda_device), 1.0, 0.3).cpu().numpy()
+    p = oracle.nucleus_probs(logits[0].float().numpy(), 1.0, 1.0)
+    assert np.all(p[pos.numpy()] == np.float32(2.0 ** -8))
+    n_keep = int(oracle.kept_mask_fixed(p, 0.3).sum())
+    assert n_keep == 77
+    for r in range(2):
+        kept = np.nonzero(got[r])[0]
+        assert kept.tolist() == pos[:n_keep].tolist()
+        np.testing.assert_allclose(got[r][kept], 1.0 / n_keep, rtol=1e-6)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_greedy_rows_half_logits(cuda_device, dtype):
+    logits = torch.randn(4, 151936, device=cuda_device).to(dtype)
+    logits[1, 1000] = logits[1, 120000] = 60.0  # a tie at the max across CTAs: the first wins
+    got = nucleus_probs(logits, 0.0, 0.9)
+    idx = logits.float().argmax(dim=-1)
+    idx[1] = 1000
+    assert torch.equal(got.argmax(dim=-1), idx) and torch.all(got.sum(dim=-1) == 1)
+    tok = sample_nucleus(logits, 0.0, 0.5)
+    assert tok.view(-1).tolist() == idx.tolist()
+
+
+def test_sample_nucleus_bf16_distribution_and_support(cuda_device):
+    logits = torch.tensor([3.0, 2.5, 0.0, -1.0, 2.0, 1.0, -3.0, 0.5])
+    ref = torch.from_numpy(oracle.nucleus_probs(logits.numpy(), 0.9, 0.8)).double()
+    n = 200_000
+    tok, probs = sample_nucleus(logits.to(torch.bfloat16).to(cuda_device).expand(n, 8).contiguous(),
+                                0.9, 0.8, return_probs=True)
+    np.testing.assert_allclose(probs[0].cpu().numpy(), ref.numpy(), rtol=1e-5)
+    freq = torch.bincount(tok.view(-1).cpu(), minlength=8).double() / n
+    assert torch.all(freq[ref == 0] == 0), "drew a token outside the nucleus"
+    assert torch.all((freq - ref).abs() < 5 * torch.sqrt(ref * (1 - ref) / n) + 1e-9)
+
+
+def test_sample_nucleus_bf16_large_vocab_draws_from_the_kept_set(cuda_device):
+    # draws over a full vocabulary land on kept entries, with the row's kept probabilities
+    g = torch.Generator().manual_seed(21)
+    logits = (torch.randn(64, 151936, generator=g) * 3.0).to(torch.bfloat16).to(cuda_device)
+    torch.manual_seed(5)
+    tok, probs = sample_nucleus(logits, 0.7, 0.9, return_probs=True)
+    picked = probs.gather(1, tok.view(-1, 1)).view(-1)
+    assert torch.all(picked > 0)
+    torch.manual_seed(5)
+    tok2 = sample_nucleus(logits, 0.7, 0.9)
+    assert torch.equal(tok.view(-1), tok2.view(-1))  # same draws with or without probs
