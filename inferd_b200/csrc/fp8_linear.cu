@@ -673,10 +673,12 @@ __global__ void __launch_bounds__(kSplitThreads) split_activations_kernel(const 
                                                                          float* __restrict__ x_scale) {
   __shared__ float red[kSplitThreads / 32];
   // Launched early (programmatic dependent launch): x and the workspace planes may belong
-  // to the previous grid until it completes.  Only then may the GEMM launch, so its early
-  // weight loads also see every write made before this call.
-  grid_dependency_wait();
+  // to the previous grid until it completes, so nothing is read or written before the
+  // wait.  The GEMM may launch at once: before its own wait it only loads weights, which no
+  // grid of this library writes (weights are written by load-time kernels that never
+  // trigger early), so its prologue and first weight ring overlap the previous call's tail.
   grid_launch_dependents();
+  grid_dependency_wait();
   const int m = blockIdx.x;
   const __nv_bfloat16* row = x + static_cast<int64_t>(m) * k;
   const int groups = k / 8;  // k % 16 == 0
@@ -815,8 +817,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) row_absmax_kernel(const T* __restrict__ x, int64_t k,
                                                          float* __restrict__ row_amax) {
   __shared__ float red[8];
-  grid_dependency_wait();  // first kernel of a call: as split_activations_kernel
-  grid_launch_dependents();
+  grid_launch_dependents();  // first kernel of a call: as split_activations_kernel
+  grid_dependency_wait();
   const float a = row_absmax(x + static_cast<int64_t>(blockIdx.x) * k, k, red);
   if (threadIdx.x == 0) row_amax[blockIdx.x] = a;
 }
@@ -830,9 +832,10 @@ __global__ void __launch_bounds__(256) quantize_dynamic_kernel(const T* __restri
                                                                uint8_t* __restrict__ q, float* __restrict__ scale) {
   __shared__ float red[8];
   // per tensor: second kernel, its primary is row_absmax_kernel; per row: the call's first
-  // kernel, so it waits for the previous grid before letting the GEMM launch
-  if (!kPerTensor) grid_dependency_wait();
+  // kernel, which (as split_activations_kernel) lets the GEMM launch before it waits for the
+  // previous grid and reads x
   grid_launch_dependents();
+  if (!kPerTensor) grid_dependency_wait();
   const int64_t r = blockIdx.x;
   const T* row = x + r * k;
   float amax = 0.f;

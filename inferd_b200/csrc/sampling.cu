@@ -661,6 +661,11 @@ struct N16Prob {
   bool t_ok, z_ok;
   __device__ __forceinline__ float y(float x) const { return div_rn(x, temp, rt, t_ok); }
   __device__ __forceinline__ float e(float x) const { return expf(y(x) - ymax); }
+  // the same term for the sum z only, as 2^((y - ymax) log2 e) on the ex2 unit: it differs
+  // from expf by a few parts in 10^7 at most, and z is a sum of such terms
+  __device__ __forceinline__ float e_sum(float x) const {
+    return ex2(__fmul_rn(y(x) - ymax, 1.4426950408889634f));
+  }
   __device__ __forceinline__ float operator()(float x) const { return div_rn(e(x), z, rz, z_ok); }
 };
 
@@ -672,9 +677,10 @@ struct N16Prob {
 // the cluster's bins (16-byte loads of its 8 bins from every CTA) and picks the digit while
 // the other warps clear the histogram buffer the pass after next will use (every CTA has
 // read it once this pass's cluster barrier is passed), and one more block barrier.
-template <int C, class Each>
+template <int C, bool kCluster, class Each>
 __device__ uint32_t n16_radix_select(N16Shared& sh, unsigned long long limit, Each each,
                                      unsigned long long& above_out, uint32_t& ties_out) {
+  constexpr int R = kCluster ? C : 1;  // CTAs whose histograms are summed
   const int tid = threadIdx.x, lane = tid & 31;
   for (int b = tid; b < 2 * 256; b += kN16Threads) {
     (&sh.hist_m[0][0])[b] = 0;
@@ -698,18 +704,28 @@ __device__ uint32_t n16_radix_select(N16Shared& sh, unsigned long long limit, Ea
       }
     });
     __syncthreads();
-    samp_cluster_sync();  // every CTA's histogram is complete; the other buffer is free
+    if (kCluster) samp_cluster_sync();  // every CTA's histogram is complete; the other buffer is free
     if (tid < 32) {
       // lane l owns bins 255 - 8l .. 248 - 8l (descending); the cut bin is the lowest
       // non-empty bin whose mass above (above + all higher bins) is within the limit
       const int b0 = 248 - 8 * lane;
       unsigned long long m8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       uint32_t c8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      uint4 vm[R][2], vc[R][2];  // every CTA's bins first, so the loads are in flight together
 #pragma unroll
-      for (int r = 0; r < C; ++r) {
-        const uint4* pm = cl_ptr(reinterpret_cast<const uint4*>(hm + b0), static_cast<uint32_t>(r));
-        const uint4* pc = cl_ptr(reinterpret_cast<const uint4*>(hc + b0), static_cast<uint32_t>(r));
-        const uint4 ma = pm[0], mb = pm[1], ca = pc[0], cb = pc[1];
+      for (int r = 0; r < R; ++r) {
+        const uint4* pm = kCluster ? cl_ptr(reinterpret_cast<const uint4*>(hm + b0), static_cast<uint32_t>(r))
+                                   : reinterpret_cast<const uint4*>(hm + b0);
+        const uint4* pc = kCluster ? cl_ptr(reinterpret_cast<const uint4*>(hc + b0), static_cast<uint32_t>(r))
+                                   : reinterpret_cast<const uint4*>(hc + b0);
+        vm[r][0] = pm[0];
+        vm[r][1] = pm[1];
+        vc[r][0] = pc[0];
+        vc[r][1] = pc[1];
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint4 ma = vm[r][0], mb = vm[r][1], ca = vc[r][0], cb = vc[r][1];
         m8[0] += ma.x; m8[1] += ma.y; m8[2] += ma.z; m8[3] += ma.w;
         m8[4] += mb.x; m8[5] += mb.y; m8[6] += mb.z; m8[7] += mb.w;
         c8[0] += ca.x; c8[1] += ca.y; c8[2] += ca.z; c8[3] += ca.w;
@@ -875,7 +891,7 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
     return;
   }
 
-  // ---- phase 2: z = sum of expf(x / T - ymax)
+  // ---- phase 2: z = sum of exp(x / T - ymax)
   N16Prob pr;
   pr.temp = temp;
   pr.rt = __frcp_rn(temp);
@@ -890,10 +906,10 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
       const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw);
       float part = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) part += pr.e(h16_to_f32<In>(h[j]));
+      for (int j = 0; j < 8; ++j) part += pr.e_sum(h16_to_f32<In>(h[j]));
       zs += part;
     }
-    for (int i = nv * 8 + tid; i < n; i += kN16Threads) zs += pr.e(h16_to_f32<In>(xs[i]));
+    for (int i = nv * 8 + tid; i < n; i += kN16Threads) zs += pr.e_sum(h16_to_f32<In>(xs[i]));
   }
   zs = block_sum_f32(sh, zs);
   if (tid == 0) sh.x_f = zs;
@@ -974,11 +990,12 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
         if (lane >= o) incl += t;
       }
       int at = pos + incl - mine;
-      while (bits) {
-        const int j = __ffs(bits) - 1;
-        bits &= bits - 1;
-        if (at < kN16ListCap) lidx[at] = static_cast<uint16_t>(c + 8 * lane + j);
-        ++at;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if ((bits >> j) & 1u) {
+          if (at < kN16ListCap) lidx[at] = static_cast<uint16_t>(c + 8 * lane + j);
+          ++at;
+        }
       }
       pos += __shfl_sync(0xffffffffu, incl, 31);
     }
@@ -1003,12 +1020,13 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
   };
 
   // ---- phase 4: top-p threshold, then the index at which a tied group is cut
+  constexpr float kFx = 4503599627370496.0f;
   uint32_t tbits = 0;
   int i_cut = 0x7fffffff;  // ties at tbits are kept below this global index
   if (cut) {
     unsigned long long above;
     uint32_t ties;
-    tbits = n16_radix_select<C>(sh, limit, each, above, ties);
+    tbits = n16_radix_select<C, true>(sh, limit, each, above, ties);
     const unsigned long long tq = to_q31(__uint_as_float(tbits));
     uint32_t keep_ties = ties;
     if (tq > 0) {
@@ -1045,7 +1063,6 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
   };
 
   // ---- kept mass in units of 2^-52: this CTA's share, the shares before it, the total
-  constexpr float kFx = 4503599627370496.0f;
   unsigned long long local = 0;
   if (fast) {
     for (int j = tid; j < count; j += kN16Threads) {
