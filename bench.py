@@ -250,7 +250,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
                         growth_tokens=args.e2e_steps + POOL_GROWTH - E2E_STEPS)
     gather = peer = None
     if world > 1 and args.gather == "nccl":
-        # NCCL all-gather of step N's outputs on NCCL's stream, overlapping step N + 1
+        # NCCL all-gather of step N's outputs on NCCL's stream, overlapping step N + 1 (the
+        # faster of the two on measurement)
         gather = OutputGather(tuple(wl.out.shape[1:]), wl.out.dtype, device, [wl.b] * world)
     elif world > 1:
         # every rank pushes its outputs into every rank's memory over NVLink and waits for
@@ -839,7 +840,7 @@ def main(argv=None) -> int:
     ap.add_argument("--fp8-m", default="1,8,32,128,256", help="token counts for --workload fp8")
     ap.add_argument("--fp8-layout", choices=["packed", "rowmajor"], default="packed")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="nccl",
                     help="N > 1: how each step's outputs reach every GPU")
     ap.add_argument("--e2e-steps", type=int, default=E2E_STEPS)
     ap.add_argument("--cpu-budget", type=float, default=15.0)

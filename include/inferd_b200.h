@@ -312,16 +312,18 @@ INFERD_API int inferd_spec_accept(int32_t* accepted, int64_t* tokens, int64_t to
  * on one GPU (core/model_runner.py:32); this replaces an all-gather collective of the
  * per-step outputs.
  *
- * Each rank allocates one peer buffer of 256 + 2 * world * bytes_per_rank bytes with
+ * Each rank allocates one peer buffer of 512 + 2 * world * bytes_per_rank bytes with
  * inferd_peer_alloc (zeroed; its CUDA IPC handle, INFERD_IPC_HANDLE_BYTES bytes, goes to
  * every other rank, which maps it with inferd_peer_open).  Layout: uint32 flags[world] at
- * offset 0 (the epoch each source rank last published), then slot 0 and slot 1 of
- * world * bytes_per_rank bytes.
+ * offset 0 (the epoch each source rank last published), uint32 push counters[world] at
+ * offset 256 (this rank's own bookkeeping), then slot 0 and slot 1 of world *
+ * bytes_per_rank bytes from offset 512.
  *
  * inferd_gather_push copies bytes_per_rank bytes from src (16-byte aligned, a multiple of
  * 16) to dst[d] + rank * bytes_per_rank for every rank d (dst: a device array of world
  * pointers, each rank's current slot), then stores epoch into flags[d][rank] (flags: a
- * device array of world pointers to each rank's flag words) with system-scope release.
+ * device array of world pointers to each rank's flag words) with system-scope release;
+ * counters is this rank's own counter array (offset 256 of its buffer).
  * inferd_gather_wait returns, in stream order, once flags[r] >= epoch for every r
  * (wrap-safe), i.e. once every rank's rows for this epoch are in this rank's slot; after
  * timeout_ns (0: 2 s) it records INFERD_ERR_DEVICE_TIMEOUT in *error_word and returns.
@@ -333,8 +335,8 @@ INFERD_API int inferd_peer_open(const void* ipc_handle, void** ptr);
 INFERD_API int inferd_peer_close(void* ptr);
 INFERD_API int inferd_peer_free(void* ptr);
 INFERD_API int inferd_gather_push(const void* src, int64_t bytes_per_rank, void* const* dst,
-                                  uint32_t* const* flags, int32_t rank, int32_t world,
-                                  uint32_t epoch, void* stream);
+                                  uint32_t* const* flags, uint32_t* counters, int32_t rank,
+                                  int32_t world, uint32_t epoch, void* stream);
 INFERD_API int inferd_gather_wait(const uint32_t* flags, int32_t world, uint32_t epoch,
                                   uint64_t timeout_ns, int32_t* error_word, void* stream);
 

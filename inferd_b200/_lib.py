@@ -92,7 +92,7 @@ _SIGNATURES = {
     "inferd_peer_close": (ctypes.c_int, [_c_void_p]),
     "inferd_peer_free": (ctypes.c_int, [_c_void_p]),
     "inferd_gather_push": (ctypes.c_int, [
-        _c_void_p, _i64, _c_void_p, _c_void_p, _i32, _i32, ctypes.c_uint32, _c_void_p]),
+        _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _i32, _i32, ctypes.c_uint32, _c_void_p]),
     "inferd_gather_wait": (ctypes.c_int, [
         _c_void_p, _i32, ctypes.c_uint32, _u64, _c_void_p, _c_void_p]),
 }

@@ -6,12 +6,14 @@
 // own HBM, mapped into every other rank's address space through CUDA IPC:
 //
 //     [0, 256)            flags: uint32 per source rank, the last epoch it published
-//     [256, ...)          slot 0, then slot 1: world x bytes_per_rank each
+//     [256, 512)          this rank's push counters: uint32 per destination rank
+//     [512, ...)          slot 0, then slot 1: world x bytes_per_rank each
 //
 // A step's push kernel copies this rank's output (bytes_per_rank) into slot s of every
 // rank's buffer at offset rank * bytes_per_rank with plain 16-byte stores (through NVLink
-// for peers; one CTA per destination), then publishes the step's epoch in every rank's
-// flag for this rank (system-scope release).  The wait kernel spins, bounded, until this
+// for peers), kPushCtas CTAs per destination so that enough SMs feed each link.  The CTA
+// that finishes a destination last (a counter in this rank's own header) publishes the
+// step's epoch in that rank's flag for this rank (system-scope release).  The wait kernel spins, bounded, until this
 // rank's flags all carry the epoch (system-scope acquire); once it completes, slot s holds
 // every rank's rows.  Slots alternate by step: a rank pushes step N + 2 into slot s only
 // after its own wait for step N + 1, i.e. after every rank pushed step N + 1, which each
@@ -28,8 +30,10 @@
 namespace inferd {
 namespace {
 
-constexpr int kPushThreads = 512;
+constexpr int kPushThreads = 256;
+constexpr int kPushCtas = 16;  // CTAs per destination
 constexpr int kMaxWorld = 64;
+constexpr int kCounterOffset = 256;  // bytes: the push counters in this rank's own header
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -40,29 +44,37 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// CTA d copies src into dst[d] + rank * bytes, then publishes epoch in flags[d][rank].
+// CTA (d, c) copies part c of src into dst[d] + rank * bytes; the last of destination d's
+// CTAs to finish publishes epoch in flags[d][rank].  counters: this rank's own header.
 __global__ void __launch_bounds__(kPushThreads) gather_push_kernel(
     const uint8_t* __restrict__ src, int64_t bytes, uint8_t* const* __restrict__ dst,
-    uint32_t* const* __restrict__ flags, int32_t rank, uint32_t epoch) {
-  const int d = blockIdx.x;
+    uint32_t* const* __restrict__ flags, uint32_t* __restrict__ counters, int32_t rank,
+    uint32_t epoch) {
+  __shared__ int last;
+  const int d = blockIdx.x / kPushCtas, part = blockIdx.x % kPushCtas;
   uint8_t* out = dst[d] + static_cast<int64_t>(rank) * bytes;
-  const int64_t n16 = bytes / 16;
+  const int64_t n16 = bytes / 16;  // bytes is a multiple of 16
+  const int64_t lo = n16 * part / kPushCtas, hi = n16 * (part + 1) / kPushCtas;
   const uint4* s4 = reinterpret_cast<const uint4*>(src);
   uint4* o4 = reinterpret_cast<uint4*>(out);
-  int64_t i = threadIdx.x;
-  for (; i + 3 * kPushThreads < n16; i += 4 * kPushThreads) {  // four 16-byte loads in flight
-    const uint4 a = __ldg(s4 + i), b = __ldg(s4 + i + kPushThreads),
-                c = __ldg(s4 + i + 2 * kPushThreads), e = __ldg(s4 + i + 3 * kPushThreads);
+  int64_t i = lo + threadIdx.x;
+  for (; i + kPushThreads < hi; i += 2 * kPushThreads) {  // two 16-byte loads in flight
+    const uint4 a = __ldg(s4 + i), b = __ldg(s4 + i + kPushThreads);
     o4[i] = a;
     o4[i + kPushThreads] = b;
-    o4[i + 2 * kPushThreads] = c;
-    o4[i + 3 * kPushThreads] = e;
   }
-  for (; i < n16; i += kPushThreads) o4[i] = __ldg(s4 + i);
-  for (int64_t j = n16 * 16 + threadIdx.x; j < bytes; j += kPushThreads) out[j] = src[j];
-  __threadfence_system();  // this thread's stores before the flag, at system scope
+  for (; i < hi; i += kPushThreads) o4[i] = __ldg(s4 + i);
+  __threadfence_system();  // this thread's stores before the counter, at system scope
   __syncthreads();
-  if (threadIdx.x == 0) st_release_sys(flags[d] + rank, epoch);
+  if (threadIdx.x == 0) {
+    // counters only grow: every push adds kPushCtas per destination
+    last = (atomicAdd(counters + d, 1u) + 1u) % kPushCtas == 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && last) {
+    __threadfence_system();  // the other CTAs' stores, seen through their counter updates
+    st_release_sys(flags[d] + rank, epoch);
+  }
 }
 
 // Lane r < world waits until flags[r] has reached epoch (wrap-safe compare).
@@ -127,14 +139,16 @@ extern "C" INFERD_API int inferd_peer_free(void* ptr) {
 }
 
 extern "C" INFERD_API int inferd_gather_push(const void* src, int64_t bytes, void* const* dst,
-                                             uint32_t* const* flags, int32_t rank, int32_t world,
-                                             uint32_t epoch, void* stream) {
+                                             uint32_t* const* flags, uint32_t* counters, int32_t rank,
+                                             int32_t world, uint32_t epoch, void* stream) {
   if (bytes < 0 || world <= 0 || world > kMaxWorld || rank < 0 || rank >= world)
     return INFERD_ERR_INVALID_ARGUMENT;
   if (dst == nullptr || flags == nullptr || (bytes > 0 && src == nullptr)) return INFERD_ERR_INVALID_ARGUMENT;
   if (!aligned16(src) || bytes % 16 != 0) return INFERD_ERR_INVALID_ARGUMENT;  // rows are 16-byte multiples
-  gather_push_kernel<<<world, kPushThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(src), bytes, reinterpret_cast<uint8_t* const*>(dst), flags, rank, epoch);
+  if (counters == nullptr) return INFERD_ERR_INVALID_ARGUMENT;
+  gather_push_kernel<<<world * kPushCtas, kPushThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), bytes, reinterpret_cast<uint8_t* const*>(dst), flags, counters, rank,
+      epoch);
   return launch_status();
 }
 

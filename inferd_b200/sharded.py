@@ -196,8 +196,8 @@ class PeerGather:
     """Per-step gather of equal-sized per-rank outputs through NVLink peer memory, without
     a collective call on the data path (the kernels of csrc/peer.cu).
 
-    Every rank allocates one buffer in its own HBM (flags, then two slots of world x rows
-    outputs) and maps every other rank's buffer through CUDA IPC; the process group is
+    Every rank allocates one buffer in its own HBM (flags, push counters, then two slots of
+    world x rows outputs) and maps every other rank's buffer through CUDA IPC; the process group is
     used once, to exchange the IPC handles.  push(local) copies this rank's rows into the
     current slot of every rank's buffer and publishes the step's epoch; wait() orders the
     current stream after every rank's push of that epoch (a bounded device-side wait: a
@@ -208,7 +208,7 @@ class PeerGather:
     after every rank has pushed the step in between).
     """
 
-    FLAG_BYTES = 256
+    HEADER_BYTES = 512  # epoch flags [0, 256), this rank's push counters [256, 512)
 
     def __init__(self, tail: tuple[int, ...], dtype: torch.dtype, device: torch.device,
                  rows_per_rank: int, *, group=None, timeout_s: float = 2.0) -> None:
@@ -233,7 +233,7 @@ class PeerGather:
             raise ValueError("one rank's rows must be a multiple of 16 bytes")
         self.timeout_ns = int(timeout_s * 1e9)
         slot_bytes = self.world * self.bytes_per_rank
-        total = self.FLAG_BYTES + 2 * slot_bytes
+        total = self.HEADER_BYTES + 2 * slot_bytes
         self._lib = lib = _lib.load()
         self._opened: list[int] = []
         self._own = None
@@ -254,11 +254,11 @@ class PeerGather:
                                                 ctypes.byref(p)), "peer_open")
                 self._opened.append(p.value)
                 bases.append(p.value)
-            self._dst = [torch.tensor([b + self.FLAG_BYTES + s * slot_bytes for b in bases],
+            self._dst = [torch.tensor([b + self.HEADER_BYTES + s * slot_bytes for b in bases],
                                       dtype=torch.int64, device=self.device) for s in range(2)]
             self._flags = torch.tensor(bases, dtype=torch.int64, device=self.device)
             own = torch.as_tensor(_DeviceBytes(self._own, total), device=self.device)
-            self._slots = [own[self.FLAG_BYTES + s * slot_bytes:self.FLAG_BYTES + (s + 1) * slot_bytes]
+            self._slots = [own[self.HEADER_BYTES + s * slot_bytes:self.HEADER_BYTES + (s + 1) * slot_bytes]
                            .view(dtype).view((self.world * self.rows,) + self.tail) for s in range(2)]
         self._epoch = 0
         self._pending = False
@@ -278,8 +278,8 @@ class PeerGather:
         self._epoch += 1
         st = self._lib.inferd_gather_push(
             local.data_ptr(), self.bytes_per_rank, self._dst[self._epoch & 1].data_ptr(),
-            self._flags.data_ptr(), self.rank, self.world, self._epoch & 0xFFFFFFFF,
-            _lib.stream_of(self.device))
+            self._flags.data_ptr(), self._own + 256, self.rank, self.world,
+            self._epoch & 0xFFFFFFFF, _lib.stream_of(self.device))
         _lib.check(st, "gather_push")
         self._pending = True
 

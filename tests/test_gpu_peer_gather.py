@@ -35,7 +35,7 @@ def test_push_and_wait_one_rank_through_c_abi(cuda_device):
     lib = _lib.load()
     rows, width = 8, 256  # 8 rows x 256 bf16 = 4 KiB per rank
     nbytes = rows * width * 2
-    total = 256 + 2 * nbytes
+    total = 512 + 2 * nbytes
     ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
     _lib.check(lib.inferd_peer_alloc(total, ctypes.byref(ptr), handle), "peer_alloc")
     try:
@@ -47,20 +47,20 @@ def test_push_and_wait_one_rank_through_c_abi(cuda_device):
         for epoch in range(1, 6):
             src = torch.randn(rows, width, device=cuda_device).to(torch.bfloat16)
             slot = epoch & 1
-            dst = torch.tensor([base + 256 + slot * nbytes], dtype=torch.int64, device=cuda_device)
+            dst = torch.tensor([base + 512 + slot * nbytes], dtype=torch.int64, device=cuda_device)
             _lib.check(lib.inferd_gather_push(src.data_ptr(), nbytes, dst.data_ptr(), flags.data_ptr(),
-                                              0, 1, epoch, stream), "gather_push")
+                                              base + 256, 0, 1, epoch, stream), "gather_push")
             _lib.check(lib.inferd_gather_wait(base, 1, epoch, 0, err.data_ptr(), stream), "gather_wait")
             torch.cuda.synchronize()
             _lib.raise_device_errors(cuda_device)
-            got = own[256 + slot * nbytes:256 + (slot + 1) * nbytes].view(torch.bfloat16).view(rows, width)
+            got = own[512 + slot * nbytes:512 + (slot + 1) * nbytes].view(torch.bfloat16).view(rows, width)
             assert torch.equal(got, src)
             assert int(own[:4].view(torch.int32)[0]) == epoch
         # bad arguments are refused before anything is launched
         assert lib.inferd_gather_push(src.data_ptr(), nbytes + 2, dst.data_ptr(), flags.data_ptr(),
-                                      0, 1, 9, stream) == _lib.ERR_INVALID_ARGUMENT
+                                      base + 256, 0, 1, 9, stream) == _lib.ERR_INVALID_ARGUMENT
         assert lib.inferd_gather_push(src.data_ptr(), nbytes, dst.data_ptr(), flags.data_ptr(),
-                                      1, 1, 9, stream) == _lib.ERR_INVALID_ARGUMENT
+                                      base + 256, 1, 1, 9, stream) == _lib.ERR_INVALID_ARGUMENT
     finally:
         torch.cuda.synchronize()
         lib.inferd_peer_free(ptr.value)
@@ -71,7 +71,7 @@ def test_wait_for_a_flag_nothing_sets_times_out(cuda_device):
     # up after 1 ms, records the timeout, and the GPU keeps working.
     lib = _lib.load()
     ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
-    _lib.check(lib.inferd_peer_alloc(256 + 32, ctypes.byref(ptr), handle), "peer_alloc")
+    _lib.check(lib.inferd_peer_alloc(512 + 32, ctypes.byref(ptr), handle), "peer_alloc")
     try:
         err = _lib.error_word(cuda_device)
         st = lib.inferd_gather_wait(ptr.value, 2, 5, 1_000_000, err.data_ptr(), _lib.stream_of(cuda_device))
