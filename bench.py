@@ -218,12 +218,13 @@ class DeviceWorkload:
             torch.cuda.current_stream(self.device).cuda_stream)
         _lib.check(st, "reshape_and_cache")
 
-    def attend(self) -> None:
-        """The step's paged attention over every sequence, into self.out."""
+    def attend(self, gather=None) -> None:
+        """The step's paged attention over every sequence, into self.out (and, with a
+        PeerGather, into every rank's gather slot from the kernel's epilogue)."""
         from inferd_b200.paged_attn import paged_attention_batched
 
         paged_attention_batched(self.q, self.kc, self.vc, self.bt, self.cl,
-                                max_context_len=self.max_ctx, out=self.out)
+                                max_context_len=self.max_ctx, out=self.out, gather=gather)
 
     def sequence_pages(self, i: int) -> tuple[np.ndarray, np.ndarray]:
         """Sequence i's K and V pages, read back from the pool in table order as float32
@@ -254,9 +255,12 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         # faster of the two on measurement)
         gather = OutputGather(tuple(wl.out.shape[1:]), wl.out.dtype, device, [wl.b] * world)
     elif world > 1:
-        # every rank pushes its outputs into every rank's memory over NVLink and waits for
-        # the others' pushes: the gathered rows are on every GPU at the end of each step
+        # p2p: every rank pushes its outputs into every rank's memory over NVLink and waits
+        # for the others' pushes.  fused: the attention kernel's epilogue stores them there
+        # itself and a one-CTA kernel publishes the step; the wait for step N - 1 comes at
+        # the start of step N, where every rank has long published it.
         peer = PeerGather(tuple(wl.out.shape[1:]), wl.out.dtype, device, wl.b)
+    fused = peer is not None and args.gather == "fused"
     stream = torch.cuda.current_stream(device)
 
     def step(ev=None):
@@ -265,12 +269,14 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
             ev[0].record(stream)
         if gather is not None:
             wl.out = gather.local()  # double-buffered: the gather of step N - 1 may still read
-        wl.attend()
+        if fused and peer._pending:
+            peer.wait()
+        wl.attend(gather=peer if fused else None)
         if ev is not None:
             ev[1].record(stream)
         if gather is not None:
             gather.start()
-        if peer is not None:
+        if peer is not None and not fused:
             peer.push(wl.out)
             peer.wait()
 
@@ -295,6 +301,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         step(attn_ev[i])
     if gather is not None:
         gather.wait_all()  # the last steps' all-gathers belong to the timed region
+    if fused:
+        peer.wait()  # so does the last step's gather
     t1.record(stream)
     torch.cuda.synchronize(device)
     clocks = sampler.stop()
@@ -329,6 +337,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
         if gather is not None:
             gathered = gather.result()
         else:
+            if fused and peer._pending:
+                peer.wait()
             gathered = peer._slots[peer._epoch & 1]
         # every rank's rows of the gathered output equal that rank's own output, on every rank
         ref = torch.empty_like(gathered)
@@ -346,7 +356,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
             if gather is not None:
                 gather.local()
                 gather.start()
-            else:
+            else:  # (fused: the push kernel stands in for the epilogue's extra stores)
                 peer.push(wl.out)
                 peer.wait()
         if gather is not None:
@@ -405,10 +415,15 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     if gather_us is not None:
         line["gather"] = {"kind": args.gather, "us_per_step_alone": gather_us,
                           "bytes_per_rank": int(wl.out.numel() * wl.out.element_size()),
-                          "how": "NCCL all_gather_into_tensor on NCCL's stream, overlapping the "
-                                 "next step" if args.gather == "nccl" else
-                                 "push kernel (this rank's rows into every rank's buffer over "
-                                 "NVLink, epoch flag) + bounded wait kernel, inside the step"}
+                          "how": {"nccl": "NCCL all_gather_into_tensor on NCCL's stream, "
+                                          "overlapping the next step",
+                                  "p2p": "push kernel (this rank's rows into every rank's buffer "
+                                         "over NVLink, epoch flag) + bounded wait kernel, inside "
+                                         "the step",
+                                  "fused": "the attention epilogue stores the rows into every "
+                                           "rank's buffer over NVLink; a one-CTA kernel publishes "
+                                           "the epoch; the bounded wait for step N - 1 opens step N"
+                                  }[args.gather]}
     if parity is not None:
         line["parity"] = parity
     if cpu is not None and not args.no_cpu_baseline:
@@ -840,7 +855,7 @@ def main(argv=None) -> int:
     ap.add_argument("--fp8-m", default="1,8,32,128,256", help="token counts for --workload fp8")
     ap.add_argument("--fp8-layout", choices=["packed", "rowmajor"], default="packed")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--gather", choices=["p2p", "nccl"], default="nccl",
+    ap.add_argument("--gather", choices=["p2p", "nccl", "fused"], default="nccl",
                     help="N > 1: how each step's outputs reach every GPU")
     ap.add_argument("--e2e-steps", type=int, default=E2E_STEPS)
     ap.add_argument("--cpu-budget", type=float, default=15.0)

@@ -340,6 +340,28 @@ INFERD_API int inferd_gather_push(const void* src, int64_t bytes_per_rank, void*
 INFERD_API int inferd_gather_wait(const uint32_t* flags, int32_t world, uint32_t epoch,
                                   uint64_t timeout_ns, int32_t* error_word, void* stream);
 
+/*
+ * The same gather fused into the attention: inferd_paged_attention_gather is
+ * inferd_paged_attention (tensor-core path only; other shapes return
+ * INFERD_ERR_UNSUPPORTED) whose epilogue also copies every finished (sequence, kv head)
+ * block of output rows, as 16-byte vectors, to peer_out[i] + peer_offset + (its index in
+ * out) for i < num_peers, each rank's current slot (peer_out: a device array of 16-byte
+ * aligned pointers); peer_offset = rank * bytes_per_rank / element size, a multiple of 8
+ * elements (INFERD_ERR_INVALID_ARGUMENT otherwise).  inferd_gather_publish then
+ * stores epoch into flags[d][rank] for every rank d (system-scope release, after the
+ * attention grids on the stream), and inferd_gather_wait orders the consumer as above.
+ */
+INFERD_API int inferd_paged_attention_gather(
+    void* out, const void* query, const void* key_cache, const void* value_cache,
+    const void* block_tables, int32_t block_table_bytes, int64_t block_table_stride,
+    const int32_t* context_lens, int32_t num_seqs, int32_t q_len, int32_t num_q_heads,
+    int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int64_t num_blocks,
+    int32_t max_context_len, float scale, int32_t dtype, void* workspace, size_t workspace_bytes,
+    void* const* peer_out, int32_t num_peers, int64_t peer_offset, int32_t* error_word,
+    void* stream);
+INFERD_API int inferd_gather_publish(uint32_t* const* flags, int32_t rank, int32_t world,
+                                     uint32_t epoch, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

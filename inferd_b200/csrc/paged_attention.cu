@@ -55,6 +55,13 @@ constexpr float kLog2e = 1.4426950408889634f;
 #define INFERD_STAGES_PER_WARP 3  // pages in flight per warp (3 x 8 KiB)
 #endif
 constexpr int kStagesPerWarp = INFERD_STAGES_PER_WARP;
+#ifndef INFERD_NT3_CTAS
+#define INFERD_NT3_CTAS 2
+#endif
+// CTAs per SM and pages in flight per warp for NT n-tiles: three CTAs of 4 warps need
+// <= 170 registers a thread and 2-page rings (3 x 4 x 2 x 8 KiB of shared memory).
+constexpr int ctas_per_sm(int nt) { return nt == 3 ? INFERD_NT3_CTAS : kCtasPerSm; }
+constexpr int stages_for(int nt) { return ctas_per_sm(nt) >= 3 ? 2 : kStagesPerWarp; }
 
 struct FastParams {
   void* out;
@@ -67,12 +74,36 @@ struct FastParams {
   int32_t num_seqs, q_len, num_q_heads, num_kv_heads, group, nq;
   int64_t num_blocks;
   float scale_log2;
-  int32_t defer_merge;  // cut segments: partials only, merged by merge_cut_segments_kernel
   int32_t* counters;  // per (sequence, kv head) ticket counters / cut markers, 0 between launches
   float* part_ml;     // [slot][NQP][2]    (m, l) per query row
   float* part_o;      // [slot][128][NQP]  unnormalised O, query row fastest
   int32_t* error_word;
+  // Output gather fused into the epilogue: once a (sequence, kv head) segment's output rows
+  // are in out, they are copied to peer_out[i] + peer_offset + (their index in out) for
+  // i < num_peers -- each rank's gather slot, through NVLink for peers -- as 16-byte
+  // vectors.  num_peers == 0: out only.
+  void* const* peer_out;
+  int32_t num_peers;
+  int64_t peer_offset;
 };
+
+// Copy the output rows of segment (b, h) -- q_len runs of group * 128 contiguous elements --
+// from out to every gather destination; thread t of nthreads.  The caller makes the rows'
+// stores visible to these threads first (__syncwarp / __syncthreads).
+template <typename T>
+__device__ __forceinline__ void copy_segment_to_peers(const FastParams& p, const T* optr, int b,
+                                                      int h, int t, int nthreads) {
+  constexpr int kVec = 16 / sizeof(T);
+  const int per = p.group * (kHeadDim / kVec);  // vectors per query position
+  for (int i = t; i < per * p.q_len; i += nthreads) {
+    const int qi = i / per, k = i - qi * per;
+    const int64_t base =
+        ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + static_cast<int64_t>(h) * p.group) * kHeadDim;
+    const uint4 v = reinterpret_cast<const uint4*>(optr + base)[k];
+    for (int r = 0; r < p.num_peers; ++r)
+      reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[r]) + p.peer_offset + base)[k] = v;
+  }
+}
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
@@ -134,7 +165,7 @@ __device__ __forceinline__ void load_q_frags(uint32_t (&qf)[8][NT][2], const T* 
 }
 
 template <bool kBf16, int NT, int STAGES>
-__global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
+__global__ void __launch_bounds__(kWarps * 32, ctas_per_sm(NT))
     paged_attn_tc_kernel(const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap, const FastParams p) {
   using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
@@ -192,6 +223,11 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
     uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.out) +
                                           static_cast<int64_t>(b) * p.q_len * p.num_q_heads * kHeadDim);
     for (int64_t i = lane; i < n16; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
+    for (int i = 0; i < p.num_peers; ++i) {
+      uint4* pd = reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[i]) + p.peer_offset +
+                                           static_cast<int64_t>(b) * p.q_len * p.num_q_heads * kHeadDim);
+      for (int64_t j = lane; j < n16; j += 32) pd[j] = make_uint4(0, 0, 0, 0);
+    }
   }
   if (T_pages == 0) return;
 
@@ -311,11 +347,15 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
           const float lv = l[nt][e & 1];
           const float inv = lv > 0.f ? 1.f / lv : 0.f;
           const int qi = c / p.group, gi = c - qi * p.group;
-          T* dst = optr + ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) * kHeadDim;
+          const int64_t row = ((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) * kHeadDim;
 #pragma unroll
           for (int mt = 0; mt < 8; ++mt)
-            dst[mt * 16 + (lane >> 2) + ((e >> 1) << 3)] = from_f32<T>(o[mt][nt][e] * inv);
+            optr[row + mt * 16 + (lane >> 2) + ((e >> 1) << 3)] = from_f32<T>(o[mt][nt][e] * inv);
         }
+      if (p.num_peers > 0) {
+        __syncwarp();
+        copy_segment_to_peers<T>(p, optr, b, h, lane, 32);
+      }
       return;
     }
     // partial: slot = unit + segment id is unique (units and segments are both monotone
@@ -343,7 +383,7 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
     }
     const int u_first = unit_of(seg_start, T_pages, U);
     const int u_last = unit_of(seg_end - 1, T_pages, U);
-    if (p.defer_merge) {
+    if constexpr (NT > 1) {
       // partials only: merge_cut_segments_kernel merges every cut segment after this grid.
       // Every piece of the segment stores the same marker (piece count, first unit); both
       // fit (the host keeps the grid below 2048 warps).
@@ -468,11 +508,15 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
         const int c = nt * 8 + cp + j;
         if (c >= p.nq) continue;
         const int qi = c / p.group, gi = c - qi * p.group;
-        T* dst = optr + ((static_cast<int64_t>(mb) * p.q_len + qi) * p.num_q_heads + mh * p.group + gi) * kHeadDim;
+        const int64_t row = ((static_cast<int64_t>(mb) * p.q_len + qi) * p.num_q_heads + mh * p.group + gi) * kHeadDim;
 #pragma unroll
         for (int k = 0; k < 16; ++k)
-          dst[k * 8 + (lane >> 2)] = from_f32<T>(j == 0 ? acc[k].x * i0 : acc[k].y * i1);
+          optr[row + k * 8 + (lane >> 2)] = from_f32<T>(j == 0 ? acc[k].x * i0 : acc[k].y * i1);
       }
+    }
+    if (p.num_peers > 0) {
+      __syncwarp();
+      copy_segment_to_peers<T>(p, optr, mb, mh, lane, 32);
     }
     if (lane == 0) p.counters[seg_id] = 0;
   };
@@ -611,8 +655,10 @@ __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
   }
   // (also after an abort, so the ticket counters return to zero)
   end_piece(g1);
-  if (n_merge > 0) merge_segment(merge_b0, merge_h0);
-  if (n_merge > 1) merge_segment(merge_b1, merge_h1);
+  if constexpr (NT == 1) {
+    if (n_merge > 0) merge_segment(merge_b0, merge_h0);
+    if (n_merge > 1) merge_segment(merge_b1, merge_h1);
+  }
   // the merge kernel that follows (deferred merging) may be scheduled once every CTA has a
   // warp past this point; it waits for the whole grid before it reads anything
   grid_launch_dependents();
@@ -712,6 +758,10 @@ __global__ void __launch_bounds__(kHeadDim) merge_cut_segments_kernel(const Fast
     const int qi = c / p.group, gi = c - qi * p.group;
     optr[((static_cast<int64_t>(b) * p.q_len + qi) * p.num_q_heads + h * p.group + gi) * kHeadDim + d] =
         from_f32<T>(acc[c] * Linv[c]);
+  }
+  if (p.num_peers > 0) {
+    __syncthreads();
+    copy_segment_to_peers<T>(p, optr, b, h, d, kHeadDim);
   }
   if (d == 0) p.counters[seg_id] = 0;
 }
@@ -877,10 +927,10 @@ inline WorkspaceLayout workspace_layout(int num_seqs, int num_kv_heads, int nqp,
   return w;
 }
 
-inline int fast_grid(int sm_count) { return sm_count * kCtasPerSm; }
+inline int fast_grid(int sm_count, int nqp) { return sm_count * ctas_per_sm(nqp / 8); }
 
-inline size_t fast_smem_bytes(int num_seqs) {
-  return 1024 + static_cast<size_t>(kWarps) * kStagesPerWarp * (kStageBytes + 8) +
+inline size_t fast_smem_bytes(int num_seqs, int nqp) {
+  return 1024 + static_cast<size_t>(kWarps) * stages_for(nqp / 8) * (kStageBytes + 8) +
          (static_cast<size_t>(num_seqs) + 1) * 4;
 }
 
@@ -931,7 +981,7 @@ int pool_map(const void* pool, int64_t rows, CUtensorMap* out) {
   return INFERD_OK;
 }
 
-template <bool kBf16, int NT, int STAGES = kStagesPerWarp>
+template <bool kBf16, int NT, int STAGES = stages_for(NT)>
 int launch_fast_t(const CUtensorMap& km, const CUtensorMap& vm, const FastParams& fp, int grid,
                   size_t smem, cudaStream_t s) {
   static bool configured[64] = {false};
@@ -1025,18 +1075,18 @@ extern "C" size_t inferd_paged_attention_workspace_bytes(int32_t num_seqs, int32
   const int group = num_q_heads / (num_kv_heads > 0 ? num_kv_heads : 1);
   const int nqp = nq_pad(q_len * (group > 0 ? group : 1));
   const int chunk = num_seqs < kMaxSeqsFast ? num_seqs : kMaxSeqsFast;
-  return workspace_layout(chunk, num_kv_heads, nqp, fast_grid(sms)).total;
+  return workspace_layout(chunk, num_kv_heads, nqp, fast_grid(sms, nqp)).total;
 }
 
-extern "C" int inferd_paged_attention(void* out, const void* query, const void* key_cache,
-                                      const void* value_cache, const void* block_tables,
-                                      int32_t block_table_bytes, int64_t block_table_stride,
-                                      const int32_t* context_lens, int32_t num_seqs,
-                                      int32_t q_len, int32_t num_q_heads, int32_t num_kv_heads,
-                                      int32_t head_dim, int32_t block_size, int64_t num_blocks,
-                                      int32_t max_context_len, float scale, int32_t dtype,
-                                      void* workspace, size_t workspace_bytes,
-                                      int32_t* error_word, void* stream) {
+static int paged_attention_impl(void* out, const void* query, const void* key_cache,
+                                const void* value_cache, const void* block_tables,
+                                int32_t block_table_bytes, int64_t block_table_stride,
+                                const int32_t* context_lens, int32_t num_seqs, int32_t q_len,
+                                int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                int32_t block_size, int64_t num_blocks, int32_t max_context_len,
+                                float scale, int32_t dtype, void* workspace,
+                                size_t workspace_bytes, int32_t* error_word, void* stream,
+                                void* const* peer_out, int32_t num_peers, int64_t peer_offset) {
   if (num_seqs < 0 || q_len <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
       block_size <= 0 || num_blocks <= 0 || max_context_len < 0 || block_table_stride < 0)
     return INFERD_ERR_INVALID_ARGUMENT;
@@ -1055,6 +1105,7 @@ extern "C" int inferd_paged_attention(void* out, const void* query, const void* 
   const bool fast = paged_attention_fast_path(dtype, head_dim, block_size, nq, num_blocks,
                                               num_kv_heads, key_cache, value_cache, query, out);
   if (!fast) {
+    if (num_peers > 0) return INFERD_ERR_UNSUPPORTED;  // the gathered form is the fast path's
     if (head_dim > kGenMaxDim) return INFERD_ERR_UNSUPPORTED;
     if (static_cast<int64_t>(q_len) * num_q_heads > 65535 * 1024) return INFERD_ERR_UNSUPPORTED;
     GenericParams gp;
@@ -1094,7 +1145,7 @@ extern "C" int inferd_paged_attention(void* out, const void* query, const void* 
   }
 
   const int nqp = nq_pad(nq);
-  const int grid = fast_grid(current_sm_count());
+  const int grid = fast_grid(current_sm_count(), nqp);
   // the cut-segment marker of the merge kernel packs a piece count below 2^11
   if (nqp > 8 && grid * kWarps >= (1 << 11)) return INFERD_ERR_UNSUPPORTED;
   const int chunk_max = kMaxSeqsFast;
@@ -1132,25 +1183,63 @@ extern "C" int inferd_paged_attention(void* out, const void* query, const void* 
     fp.part_ml = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + wl.ml);
     fp.part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + wl.o);
     fp.error_word = error_word;
-    // Several n-tiles: merge the cut segments in a second, fully parallel kernel
-    fp.defer_merge = nqp > 8 ? 1 : 0;
+    fp.peer_out = peer_out;
+    fp.num_peers = num_peers;
+    fp.peer_offset = peer_offset + static_cast<int64_t>(b0) * q_len * num_q_heads * kHeadDim;
+    // Several n-tiles: the kernel leaves the partials of cut segments to a second, fully
+    // parallel kernel (merge_cut_segments_kernel)
+    const bool defer_merge = nqp > 8;
     // grid: persistent, but no more CTAs than pages can feed (upper bound from the host)
     const int64_t pages_ub = static_cast<int64_t>(nb) * num_kv_heads *
                              ((static_cast<int64_t>(max_context_len) + kPage - 1) / kPage);
     int g = grid;
     const int64_t ctas_ub = (pages_ub + kWarps - 1) / kWarps;  // one warp per page at most
     if (ctas_ub < g) g = ctas_ub > 0 ? static_cast<int>(ctas_ub) : 1;
-    const size_t smem = fast_smem_bytes(nb);
+    const size_t smem = fast_smem_bytes(nb, nqp);
     st = dtype == INFERD_BF16 ? launch_fast<true>(km, vm, fp, nqp / 8, g, smem, s)
                               : launch_fast<false>(km, vm, fp, nqp / 8, g, smem, s);
     if (st != INFERD_OK) return st;
-    if (fp.defer_merge) {
+    if (defer_merge) {
       st = dtype == INFERD_BF16 ? launch_merge<true>(fp, nqp / 8, nb * num_kv_heads, s)
                                 : launch_merge<false>(fp, nqp / 8, nb * num_kv_heads, s);
       if (st != INFERD_OK) return st;
     }
   }
   return INFERD_OK;
+}
+
+extern "C" int inferd_paged_attention(void* out, const void* query, const void* key_cache,
+                                      const void* value_cache, const void* block_tables,
+                                      int32_t block_table_bytes, int64_t block_table_stride,
+                                      const int32_t* context_lens, int32_t num_seqs,
+                                      int32_t q_len, int32_t num_q_heads, int32_t num_kv_heads,
+                                      int32_t head_dim, int32_t block_size, int64_t num_blocks,
+                                      int32_t max_context_len, float scale, int32_t dtype,
+                                      void* workspace, size_t workspace_bytes,
+                                      int32_t* error_word, void* stream) {
+  return paged_attention_impl(out, query, key_cache, value_cache, block_tables, block_table_bytes,
+                              block_table_stride, context_lens, num_seqs, q_len, num_q_heads,
+                              num_kv_heads, head_dim, block_size, num_blocks, max_context_len,
+                              scale, dtype, workspace, workspace_bytes, error_word, stream,
+                              nullptr, 0, 0);
+}
+
+extern "C" int inferd_paged_attention_gather(
+    void* out, const void* query, const void* key_cache, const void* value_cache,
+    const void* block_tables, int32_t block_table_bytes, int64_t block_table_stride,
+    const int32_t* context_lens, int32_t num_seqs, int32_t q_len, int32_t num_q_heads,
+    int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int64_t num_blocks,
+    int32_t max_context_len, float scale, int32_t dtype, void* workspace, size_t workspace_bytes,
+    void* const* peer_out, int32_t num_peers, int64_t peer_offset, int32_t* error_word,
+    void* stream) {
+  if (num_peers < 1 || num_peers > 64 || peer_out == nullptr || peer_offset < 0 ||
+      peer_offset % 8 != 0)
+    return INFERD_ERR_INVALID_ARGUMENT;
+  return paged_attention_impl(out, query, key_cache, value_cache, block_tables, block_table_bytes,
+                              block_table_stride, context_lens, num_seqs, q_len, num_q_heads,
+                              num_kv_heads, head_dim, block_size, num_blocks, max_context_len,
+                              scale, dtype, workspace, workspace_bytes, error_word, stream,
+                              peer_out, num_peers, peer_offset);
 }
 
 extern "C" int inferd_dense_attention(void* out, const void* query, const void* key,

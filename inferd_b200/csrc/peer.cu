@@ -77,6 +77,18 @@ __global__ void __launch_bounds__(kPushThreads) gather_push_kernel(
   }
 }
 
+// Thread d < world publishes epoch in flags[d][rank]: the rows of this epoch were stored
+// into every rank's slot by the grids before this one on the stream (the attention kernel's
+// fused epilogue), which completed before this grid started.
+__global__ void __launch_bounds__(kMaxWorld) gather_publish_kernel(uint32_t* const* flags, int32_t rank,
+                                                                   int32_t world, uint32_t epoch) {
+  const int d = threadIdx.x;
+  if (d < world) {
+    __threadfence_system();
+    st_release_sys(flags[d] + rank, epoch);
+  }
+}
+
 // Lane r < world waits until flags[r] has reached epoch (wrap-safe compare).
 __global__ void __launch_bounds__(kMaxWorld) gather_wait_kernel(const uint32_t* flags, int32_t world,
                                                                 uint32_t epoch, uint64_t timeout_ns,
@@ -158,5 +170,13 @@ extern "C" INFERD_API int inferd_gather_wait(const uint32_t* flags, int32_t worl
   if (timeout_ns == 0 || timeout_ns > kWaitTimeoutNs) timeout_ns = kWaitTimeoutNs;
   gather_wait_kernel<<<1, kMaxWorld, 0, static_cast<cudaStream_t>(stream)>>>(flags, world, epoch,
                                                                             timeout_ns, error_word);
+  return launch_status();
+}
+
+extern "C" INFERD_API int inferd_gather_publish(uint32_t* const* flags, int32_t rank, int32_t world,
+                                                uint32_t epoch, void* stream) {
+  if (flags == nullptr || world <= 0 || world > kMaxWorld || rank < 0 || rank >= world)
+    return INFERD_ERR_INVALID_ARGUMENT;
+  gather_publish_kernel<<<1, kMaxWorld, 0, static_cast<cudaStream_t>(stream)>>>(flags, rank, world, epoch);
   return launch_status();
 }

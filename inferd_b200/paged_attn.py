@@ -225,6 +225,7 @@ def paged_attention_batched(
     scale: float | None = None,
     max_context_len: int | None = None,
     out: torch.Tensor | None = None,
+    gather=None,
 ) -> torch.Tensor:
     """Batched paged attention, one launch for all sequences.
 
@@ -234,6 +235,10 @@ def paged_attention_batched(
     context_lens None means every sequence has max_context_len keys.  max_context_len is
     a host-side upper bound used only to size the launch; it defaults to the block-table
     capacity, so nothing here synchronises with the device.
+
+    gather: an inferd_b200.sharded.PeerGather whose rows are this call's output; the kernel
+    also stores them into every rank's gather slot and the step is published (call
+    gather.wait() before the next gathered call, and to read the gathered rows).
     """
     if query.ndim != 4:
         raise ValueError("query must be [num_seqs, q_len, q_heads, head_dim]")
@@ -279,6 +284,20 @@ def paged_attention_batched(
             _WS_BYTES.clear()
         _WS_BYTES[ws_key] = ws_bytes
     ws = _lib.workspace(dev, ws_bytes)
+    if gather is not None:
+        if gather.device != dev or gather.rows != b or gather.tail != (q_len, q_heads, head_dim) \
+                or gather.dtype != query.dtype:
+            raise ValueError("gather was built for other rows, shapes, dtype or device")
+        dst, n_dst, offset = gather.begin()
+        st = lib.inferd_paged_attention_gather(
+            out.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(),
+            bt.element_size(), bt.stride(0), _lib.ptr(context_lens), b, q_len, q_heads, kv_heads,
+            head_dim, block_size, num_blocks, int(max_context_len), float(scale),
+            _lib.dtype_code(query.dtype), ws.data_ptr(), ws.numel(), dst, n_dst, offset,
+            _lib.error_word(dev).data_ptr(), _lib.stream_of(dev))
+        _lib.check(st, "paged_attention_gather")
+        gather.publish()
+        return out
     st = lib.inferd_paged_attention(
         out.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(),
         bt.element_size(), bt.stride(0), _lib.ptr(context_lens), b, q_len, q_heads, kv_heads,

@@ -283,6 +283,27 @@ class PeerGather:
         _lib.check(st, "gather_push")
         self._pending = True
 
+    def begin(self) -> tuple[int, int, int]:
+        """Open the next step for a kernel that stores its outputs into every rank's slot
+        itself (inferd_paged_attention_gather): returns (device array of the destinations,
+        number of destinations, this rank's element offset in each).  publish() follows the
+        kernel, then wait()."""
+        if self._pending:
+            raise RuntimeError("wait() for the previous push before the next one")
+        self._epoch += 1
+        elems = self.bytes_per_rank // torch.empty(0, dtype=self.dtype).element_size()
+        return self._dst[self._epoch & 1].data_ptr(), self.world, self.rank * elems
+
+    def publish(self) -> None:
+        """Publish the step opened by begin() once the kernels that stored its rows are
+        enqueued (a one-CTA kernel: system-scope release of this rank's flag everywhere)."""
+        from . import _lib
+
+        st = self._lib.inferd_gather_publish(self._flags.data_ptr(), self.rank, self.world,
+                                             self._epoch & 0xFFFFFFFF, _lib.stream_of(self.device))
+        _lib.check(st, "gather_publish")
+        self._pending = True
+
     def wait(self) -> torch.Tensor:
         """Order the current stream after every rank's push of this step; returns this rank's
         slot, [world * rows, *tail] in rank order, valid until the push after next."""

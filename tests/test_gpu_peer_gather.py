@@ -147,3 +147,90 @@ def test_peer_gather_two_ranks_match_nccl_all_gather():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert got == {0: True, 1: True}, got
+
+
+def _attn_inputs(device, seed, b=6, hq=32, hkv=8, d=128, q_len=1):
+    g = torch.Generator(device=device).manual_seed(seed)
+    lens = torch.randint(20, 700, (b,), generator=g, device=device).to(torch.int32)
+    pages = (lens + 15) // 16
+    nb = int(pages.sum()) + 4
+    kc = torch.randn(nb, hkv, 16, d, generator=g, device=device).to(torch.bfloat16)
+    vc = torch.randn(nb, hkv, 16, d, generator=g, device=device).to(torch.bfloat16)
+    perm = torch.randperm(nb, generator=g, device=device).to(torch.int32)
+    bt = torch.zeros(b, int(pages.max()), dtype=torch.int32, device=device)
+    s = 0
+    for i, p in enumerate(pages.tolist()):
+        bt[i, :p] = perm[s:s + p]
+        s += p
+    q = torch.randn(b, q_len, hq, d, generator=g, device=device).to(torch.bfloat16)
+    return q, kc, vc, bt, lens
+
+
+@pytest.mark.parametrize("q_len", [1, 5])
+def test_attention_epilogue_gather_one_rank(cuda_device, q_len):
+    # the gathered slot holds exactly what the attention wrote to `out`, step after step
+    from inferd_b200 import paged_attention_batched
+
+    port = _free_port()
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    try:
+        g = PeerGather((q_len, 32, 128), torch.bfloat16, cuda_device, 6)
+        for step in range(4):
+            q, kc, vc, bt, cl = _attn_inputs(cuda_device, 10 * step + q_len, q_len=q_len)
+            if g._pending:
+                g.wait()
+            out = paged_attention_batched(q, kc, vc, bt, cl, gather=g)
+            ref = paged_attention_batched(q, kc, vc, bt, cl)
+            slot = g.wait()
+            torch.cuda.synchronize()
+            assert torch.equal(out, ref) and torch.equal(slot, out)
+        g.close()
+        _lib.raise_device_errors(cuda_device)
+    finally:
+        dist.destroy_process_group()
+
+
+def _fused_worker(rank: int, port: int, results) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    ok = True
+    try:
+        from inferd_b200 import paged_attention_batched
+
+        g = PeerGather((1, 32, 128), torch.bfloat16, dev, 6, timeout_s=1.0)
+        ref = torch.empty(12, 1, 32, 128, dtype=torch.bfloat16, device=dev)
+        for step in range(5):
+            q, kc, vc, bt, cl = _attn_inputs(dev, 100 * step + rank)
+            if g._pending:
+                g.wait()
+            out = paged_attention_batched(q, kc, vc, bt, cl, gather=g)
+            full = g.wait()
+            dist.all_gather_into_tensor(ref, out)
+            torch.cuda.synchronize(dev)
+            ok &= bool(torch.equal(full, ref))
+        _lib.raise_device_errors(dev)
+        g.close()
+    except Exception as e:  # reported to the parent, which fails the test
+        ok = repr(e)
+    finally:
+        dist.destroy_process_group()
+    results.put((rank, ok))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_attention_epilogue_gather_two_ranks_match_nccl():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert got == {0: True, 1: True}, got
