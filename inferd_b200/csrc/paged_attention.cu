@@ -63,6 +63,9 @@ constexpr int kStagesPerWarp = INFERD_STAGES_PER_WARP;
 constexpr int ctas_per_sm(int nt) { return nt == 3 ? INFERD_NT3_CTAS : kCtasPerSm; }
 constexpr int stages_for(int nt) { return ctas_per_sm(nt) >= 3 ? 2 : kStagesPerWarp; }
 
+// query rows per (sequence, kv head), rounded up to whole 8-column MMA tiles
+__host__ __device__ constexpr int nq_pad(int nq) { return ((nq + 7) / 8) * 8; }
+
 struct FastParams {
   void* out;
   const void* query;
@@ -144,6 +147,40 @@ __device__ __forceinline__ int unit_of(int64_t g, int64_t T, int U) {
   return static_cast<int>(u);
 }
 
+// Pages per sequence and their exclusive prefix over the launch's sequences, by a block
+// scan over NTHREADS threads: prefix[b] = pages of sequences [0, b), prefix[B] = total.
+// Ends with a block barrier.
+template <int NTHREADS>
+__device__ __forceinline__ void page_prefix(const FastParams& p, int* prefix, int* warp_tot) {
+  constexpr int kW = NTHREADS / 32;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int B = p.num_seqs;
+  const int chunk = (B + NTHREADS - 1) / NTHREADS;
+  const int b0 = min(B, tid * chunk), b1 = min(B, b0 + chunk);
+  int local = 0;
+  for (int b = b0; b < b1; ++b) local += (seq_len_of(p, b, true) + kPage - 1) / kPage;
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  int run = incl - local;
+  int total = 0;
+  for (int w = 0; w < kW; ++w) {
+    if (w < warp) run += warp_tot[w];
+    total += warp_tot[w];
+  }
+  for (int b = b0; b < b1; ++b) {
+    prefix[b] = run;
+    run += (seq_len_of(p, b, false) + kPage - 1) / kPage;
+  }
+  if (tid == 0) prefix[B] = total;
+  __syncthreads();
+}
+
 // Query-row fragments (MMA B operand, d x rows) of one segment, read from global memory:
 // b0 = rows n = nt*8 + lane/4, d = kk*16 + 2*(lane%4) + {0,1}; b1 = the same at d + 8.
 template <typename T, int NT>
@@ -182,33 +219,7 @@ __global__ void __launch_bounds__(kWarps * 32, ctas_per_sm(NT))
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int B = p.num_seqs, Hkv = p.num_kv_heads;
 
-  // ---- pages per sequence, exclusive prefix over sequences (block scan)
-  {
-    const int chunk = (B + kThreads - 1) / kThreads;
-    const int b0 = min(B, tid * chunk), b1 = min(B, b0 + chunk);
-    int local = 0;
-    for (int b = b0; b < b1; ++b) local += (seq_len_of(p, b, true) + kPage - 1) / kPage;
-    int incl = local;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    if (lane == 31) warp_tot[warp] = incl;
-    __syncthreads();
-    int run = incl - local;
-    int total = 0;
-    for (int w = 0; w < kWarps; ++w) {
-      if (w < warp) run += warp_tot[w];
-      total += warp_tot[w];
-    }
-    for (int b = b0; b < b1; ++b) {
-      prefix[b] = run;
-      run += (seq_len_of(p, b, false) + kPage - 1) / kPage;
-    }
-    if (tid == 0) prefix[B] = total;
-    __syncthreads();
-  }
+  page_prefix<kThreads>(p, prefix, warp_tot);
   // No block-level synchronisation below this point: every warp runs on its own.
 
   const int64_t T_pages = static_cast<int64_t>(Hkv) * prefix[B];
@@ -766,6 +777,504 @@ __global__ void __launch_bounds__(kHeadDim) merge_cut_segments_kernel(const Fast
   if (d == 0) p.counters[seg_id] = 0;
 }
 
+// ------------------------------------------------------------------ tensor-memory path
+// Windows of several query rows per kv head (speculative verify: q_len x group rows, 9 to
+// 32 of them).  One persistent CTA per SM streams the balanced page range of its unit
+// (CTA) in chunks of up to four pages of one segment:
+//   warp 0      lane 0 issues the TMA loads of a chunk (K and V, 128-byte swizzle) into a
+//               4-stage ring; each stage holds K lo | K hi | V lo | V hi, 64 rows x 128 B
+//               each, so the chunk's keys form one K-major (and one MN-major) operand;
+//   warp 1      lane 0 issues tcgen05.mma: S = Q K^T (M = 128 rows, N = 64 keys, K = 128,
+//               into one of two 64-column tensor-memory buffers), and O += P V (M = 128,
+//               N = 128, one K = 16 step per page, V as an MN-major operand) into 128
+//               columns that hold O for the whole segment;
+//   warps 2-5   one thread per query row (row r in tensor-memory lane 32 (r % 4) + r / 4):
+//               read the row's 64 scores, mask, online softmax in base 2 with a lazy
+//               rescale (O and l are rescaled only when the running maximum grows by more
+//               than 2^8), write P (16-bit, K-major, swizzled) for the P V MMA, and at the
+//               end of a segment piece read O, normalise and store (or leave a partial for
+//               merge_cut_segments_kernel).
+// The Q tile of the next segment is written as soon as the last S of the current one has
+// been read, so the MMA warp runs one chunk ahead of the softmax warps (S(i+1) is computed
+// while softmax(i) runs) and the ring keeps four chunks of loads in flight.
+constexpr int kVPages = 4;                       // pages per chunk
+constexpr int kVKeys = kVPages * kPage;          // 64 keys: N of S, K of P V
+constexpr int kVStages = 4;
+constexpr int kVRegion = kVPages * kHalfBytes;   // 8 KiB: 64 rows x 128 B
+constexpr int kVStageBytes = 4 * kVRegion;       // K lo | K hi | V lo | V hi
+constexpr int kVQBytes = 2 * 128 * 128;          // Q tile, 128 rows x 256 B (lo | hi halves)
+constexpr int kVPBytes = 128 * 128;              // P tile, 128 rows x 64 keys x 2 B
+constexpr int kVThreads = 192;
+constexpr int kVTmemCols = 256;                  // S0 [0, 64) | S1 [64, 128) | O [128, 256)
+constexpr float kVRescale = 8.f;                 // lazy rescale threshold (log2 units)
+constexpr int kVBarOffset = kVStages * kVStageBytes + kVQBytes + 2 * kVPBytes;
+constexpr int kVPrefixOffset = kVBarOffset + 512;
+
+// Instruction descriptor, kind::f16: A and B 16-bit (bf16 or f16), D f32, A K-major, B
+// K-major or MN-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t f16_idesc(bool bf16, bool b_mn_major, int n) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(128 >> 4) << 24);
+}
+
+// tensor-memory lane (= MMA row) of query row r
+__device__ __forceinline__ int vrow_lane(int r) { return 32 * (r & 3) + (r >> 2); }
+
+// The unit's page range [g0, g1) walked in chunks: at most kVPages pages, never across a
+// segment or past the range.  Every role walks the same sequence.
+struct ChunkWalk {
+  int64_t g, g0, g1, seg_start, seg_end;
+  int b, h, pb, L;
+  __device__ void init(const FastParams& p, const int* prefix, int64_t a, int64_t e) {
+    g0 = g = a;
+    g1 = e;
+    const int Hkv = p.num_kv_heads;
+    b = find_seq(prefix, p.num_seqs, a / Hkv);
+    pb = prefix[b + 1] - prefix[b];
+    seg_start = static_cast<int64_t>(Hkv) * prefix[b];
+    h = static_cast<int>((a - seg_start) / pb);
+    seg_start += static_cast<int64_t>(h) * pb;
+    seg_end = seg_start + pb;
+    L = seq_len_of(p, b, false);
+  }
+  __device__ bool done() const { return g >= g1; }
+  __device__ int pages() const { return static_cast<int>(min64(kVPages, min64(seg_end, g1) - g)); }
+  __device__ bool first() const { return g == g0 || g == seg_start; }
+  __device__ bool last(int np) const { return g + np == seg_end || g + np == g1; }
+  __device__ void advance(const FastParams& p, const int* prefix, int np) {
+    g += np;
+    if (g == seg_end && g < g1) {
+      if (++h == p.num_kv_heads) {
+        h = 0;
+        do { ++b; } while (prefix[b + 1] == prefix[b]);
+        L = seq_len_of(p, b, false);
+      }
+      pb = prefix[b + 1] - prefix[b];
+      seg_start = g;
+      seg_end = g + pb;
+    }
+  }
+};
+
+template <bool kBf16>
+__global__ void __launch_bounds__(kVThreads, 1)
+    paged_verify_tmem_kernel(const __grid_constant__ CUtensorMap kmap,
+                             const __grid_constant__ CUtensorMap vmap, const FastParams p) {
+  using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int warp_tot[kVThreads / 32];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* ring = smem;
+  uint8_t* qtile = smem + kVStages * kVStageBytes;
+  uint8_t* ptile = qtile + kVQBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kVBarOffset);
+  uint64_t* full = bars;        // [4] TMA bytes of a stage landed
+  uint64_t* empty = bars + 4;   // [4] the P V MMAs of a stage are done
+  uint64_t* s_full = bars + 8;  // [2] S of a chunk is in tensor memory
+  uint64_t* s_free = bars + 10; // [2] the softmax threads have read it
+  uint64_t* p_full = bars + 12; // [2] P written (and O rescaled)
+  uint64_t* o_done = bars + 14; // [2] the P V MMAs of a chunk are done
+  uint64_t* q_full = bars + 16; // Q tile of the next segment piece written
+  uint64_t* m_done = bars + 17; // every MMA of the CTA is done
+  int* prefix = reinterpret_cast<int*>(smem + kVPrefixOffset);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int B = p.num_seqs, Hkv = p.num_kv_heads;
+
+  if (tid == 0) {
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);  // one arrival per softmax warp
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(q_full, 4);
+    mbar_init(m_done, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  if (warp == 1) {
+    tmem_alloc1(&tmem_slot, kVTmemCols);
+    tmem_relinquish1();
+  }
+  page_prefix<kVThreads>(p, prefix, warp_tot);  // ends with __syncthreads
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  const int64_t T_pages = static_cast<int64_t>(Hkv) * prefix[B];
+  const int U = static_cast<int>(min64(gridDim.x, max64(T_pages, 1)));
+  const int u = blockIdx.x;
+  const bool active = u < U && T_pages > 0;
+  const int64_t g0 = static_cast<int64_t>(u) * T_pages / U;
+  const int64_t g1 = static_cast<int64_t>(u + 1) * T_pages / U;
+  volatile int* vabort = &abort_flag;
+  int fills = 0;  // chunks whose loads the producer issued (warp 0)
+
+  if (warp == 0) {
+    // ---------------- producer
+    if (active) {
+      if (lane == 0) {
+        prefetch_tensormap(&kmap);
+        prefetch_tensormap(&vmap);
+      }
+      const uint64_t policy = l2_policy_evict_first();
+      // pool row (block * Hkv + head) * 16 of global page g
+      auto row_of = [&](int64_t g) -> int32_t {
+        const int b = find_seq(prefix, B, g / Hkv);
+        const int pb = prefix[b + 1] - prefix[b];
+        const int64_t off = g - static_cast<int64_t>(Hkv) * prefix[b];
+        const int h = static_cast<int>(off / pb);
+        int64_t blk = block_id(p, b, static_cast<int>(off - static_cast<int64_t>(h) * pb));
+        if (blk < 0 || blk >= p.num_blocks) {
+          report_error(p.error_word, INFERD_ERR_DEVICE_INDEX);
+          blk = 0;
+        }
+        return static_cast<int32_t>((blk * Hkv + h) * kPage);
+      };
+      // rows of the unit's pages 32 at a time: lane l of rows_cur holds page batch0 + l, and
+      // rows_next the batch after, loaded one batch ahead of its use
+      int64_t batch0 = g0;
+      int32_t rows_cur = g0 + lane < g1 ? row_of(g0 + lane) : 0;
+      int32_t rows_next = g0 + 32 + lane < g1 ? row_of(g0 + 32 + lane) : 0;
+      ChunkWalk cw;
+      cw.init(p, prefix, g0, g1);
+      for (int i = 0; !cw.done(); ++i) {
+        const int np = cw.pages();
+        const int s = i % kVStages, round = i / kVStages;
+        bool ok = *vabort == 0;
+        if (ok && round > 0 && lane == 0) ok = mbar_wait(&empty[s], (round - 1) & 1);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) {
+          if (lane == 0) { report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT); *vabort = 1; }
+          break;
+        }
+        uint8_t* st = ring + s * kVStageBytes;
+        if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(np) * kStageBytes);
+        for (int q = 0; q < np; ++q) {
+          const int64_t gq = cw.g + q;
+          if (gq >= batch0 + 32) {  // rotate the batches (warp-uniform)
+            batch0 += 32;
+            rows_cur = rows_next;
+            rows_next = batch0 + 32 + lane < g1 ? row_of(batch0 + 32 + lane) : 0;
+          }
+          const int32_t r = __shfl_sync(0xffffffffu, rows_cur, static_cast<int>(gq - batch0));
+          if (lane == 0) {
+            tma_load_2d(st + q * kHalfBytes, &kmap, 0, r, &full[s], policy);
+            tma_load_2d(st + kVRegion + q * kHalfBytes, &kmap, 64, r, &full[s], policy);
+            tma_load_2d(st + 2 * kVRegion + q * kHalfBytes, &vmap, 0, r, &full[s], policy);
+            tma_load_2d(st + 3 * kVRegion + q * kHalfBytes, &vmap, 64, r, &full[s], policy);
+          }
+        }
+        ++fills;
+        cw.advance(p, prefix, np);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (one thread)
+    if (active && lane == 0) {
+      const uint32_t idesc_s = f16_idesc(kBf16, false, kVKeys);
+      const uint32_t idesc_o = f16_idesc(kBf16, true, kHeadDim);
+      const uint32_t q_base = smem_u32(qtile), p_base = smem_u32(ptile), r_base = smem_u32(ring);
+      ChunkWalk cw;
+      cw.init(p, prefix, g0, g1);
+      int piece = 0;
+      int prev_np = 0, prev_first = 0;
+      bool ok = true;
+      // O += P(j) V(j), one K = 16 step per page of chunk j
+      auto issue_pv = [&](int j, int np, bool first) -> bool {
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1)) return false;
+        tc_fence_after();
+        const uint32_t pa = p_base + (j & 1) * kVPBytes;
+        const uint32_t va = r_base + (j % kVStages) * kVStageBytes + 2 * kVRegion;
+        for (int q = 0; q < np; ++q)
+          mma_f16_1(tmem + 128, sw128_desc(pa + q * 32), sw128_mn_desc(va + q * kHalfBytes, kVRegion, 1024),
+                    idesc_o, (first && q == 0) ? 0u : 1u);
+        mma_commit1(&o_done[j & 1]);
+        mma_commit1(&empty[j % kVStages]);
+        return true;
+      };
+      int i = 0;
+      for (; !cw.done() && ok; ++i) {
+        const int np = cw.pages();
+        const bool first = cw.first();
+        if (*vabort) { ok = false; break; }
+        if (first) {
+          ok = mbar_wait(q_full, piece & 1);
+          ++piece;
+        }
+        if (ok) ok = mbar_wait(&full[i % kVStages], (i / kVStages) & 1);
+        if (ok && i >= 2) ok = mbar_wait(&s_free[i & 1], ((i >> 1) - 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        // S(i) = Q K^T over the 128 dims: 8 K-steps of 16 (lo half, then hi half)
+        const uint32_t ka = r_base + (i % kVStages) * kVStageBytes;
+        const uint32_t sc = tmem + (i & 1) * kVKeys;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_1(sc, sw128_desc(q_base + (kk >> 2) * (kVQBytes / 2) + (kk & 3) * 32),
+                    sw128_desc(ka + (kk >> 2) * kVRegion + (kk & 3) * 32), idesc_s, kk > 0 ? 1u : 0u);
+        mma_commit1(&s_full[i & 1]);
+        if (i > 0) ok = issue_pv(i - 1, prev_np, prev_first != 0);
+        prev_np = np;
+        prev_first = first ? 1 : 0;
+        cw.advance(p, prefix, np);
+      }
+      if (ok && i > 0) ok = issue_pv(i - 1, prev_np, prev_first != 0);
+      if (!ok) {
+        report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+        *vabort = 1;
+      }
+      // every MMA issued by this thread is complete before tensor memory is released
+      mma_commit1(m_done);
+      mbar_wait(m_done, 0);
+    }
+  } else {
+    // ---------------- softmax / epilogue: one thread per query row
+    const int t = tid - 64;                  // 0..127
+    const int qd = warp & 3;                 // tensor-memory lane quarter of this warp
+    const int r = 4 * lane + qd;             // query row of this thread
+    const int m_lane = 32 * qd + lane;       // its MMA row
+    const bool live = r < p.nq;
+    const int qi = live ? r / p.group : 0, gi = live ? r - qi * p.group : 0;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * qd) << 16);
+    const T* qptr = static_cast<const T*>(p.query);
+    T* optr = static_cast<T*>(p.out);
+    const int nqp = nq_pad(p.nq);            // column count of the partial layout
+
+    // Q rows of segment (b, h) into the Q tile (K-major, 128-byte swizzle, lo | hi halves)
+    auto write_q = [&](int b, int h) {
+      for (int it = t; it < p.nq * 16; it += 128) {
+        const int rr = it >> 4, c = it & 15;
+        const int q2 = rr / p.group, g2 = rr - q2 * p.group;
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(
+            qptr + ((static_cast<int64_t>(b) * p.q_len + q2) * p.num_q_heads + h * p.group + g2) * kHeadDim) + c);
+        const int ml = vrow_lane(rr);
+        *reinterpret_cast<uint4*>(qtile + (c >> 3) * (kVQBytes / 2) + ml * 128 + (((c & 7) ^ (ml & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_full);
+    };
+
+    if (active) {
+      ChunkWalk cw;
+      cw.init(p, prefix, g0, g1);
+      write_q(cw.b, cw.h);
+      float m_run = -INFINITY, l_run = 0.f;
+      int lim = 0;
+      bool ok = true;
+      for (int j = 0; !cw.done(); ++j) {
+        const int np = cw.pages();
+        const bool first = cw.first(), last = cw.last(np);
+        if (first) {
+          m_run = -INFINITY;
+          l_run = 0.f;
+          lim = live ? cw.L - p.q_len + qi : -1;
+        }
+        if (ok && *vabort) ok = false;
+        if (ok) ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1);
+        if (!__all_sync(0xffffffffu, ok)) ok = false;
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t sv[kVKeys];
+        tmem_ld32(lane_addr + (j & 1) * kVKeys, sv);
+        tmem_ld32(lane_addr + (j & 1) * kVKeys + 32, sv + 32);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[j & 1]);
+        // the next piece's Q: every S of this piece has completed
+        if (last && cw.g + np < cw.g1) {
+          ChunkWalk nx = cw;
+          nx.advance(p, prefix, np);
+          write_q(nx.b, nx.h);
+        }
+        // masked scores in base 2; keys past the piece's pages, the sequence end or the
+        // causal limit of this row are -inf
+        const int key0 = static_cast<int>(cw.g - cw.seg_start) * kPage;
+        const int kmax = min(np * kPage - 1, lim - key0);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < kVKeys; ++k) {
+          const float x = k <= kmax ? __uint_as_float(sv[k]) * p.scale_log2 : -INFINITY;
+          sv[k] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+        // lazy rescale: O and l keep the old reference unless the maximum grew by > 2^8
+        bool need = false;
+        float factor = 1.f;
+        if (first) {
+          m_run = mx;
+        } else if (mx > m_run + kVRescale) {
+          factor = ex2(m_run - mx);
+          need = true;
+          m_run = mx;
+          l_run *= factor;
+        }
+        if (j >= 1 && !first && __any_sync(0xffffffffu, need)) {
+          // O holds P(j-1) V(j-1) only once those MMAs are done
+          if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) ok = false;
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c0 = 0; c0 < kHeadDim; c0 += 32) {
+            uint32_t ov[32];
+            tmem_ld32(lane_addr + 128 + c0, ov);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * factor);
+            tmem_st32(lane_addr + 128 + c0, ov);
+          }
+          tmem_st_wait();
+        }
+        const float mref = m_run == -INFINITY ? 0.f : m_run;
+        // P(j) into its buffer once P(j-2) V(j-2) is done reading it
+        if (j >= 2) {
+          if (!mbar_wait(&o_done[j & 1], ((j - 2) >> 1) & 1)) ok = false;
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        }
+        uint8_t* prow = ptile + (j & 1) * kVPBytes + m_lane * 128;
+        float lsum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float e8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            e8[e] = live ? ex2(__uint_as_float(sv[8 * c + e]) - mref) : 0.f;
+            lsum += e8[e];
+          }
+          uint4 v;
+          v.x = pack2<kBf16>(e8[0], e8[1]);
+          v.y = pack2<kBf16>(e8[2], e8[3]);
+          v.z = pack2<kBf16>(e8[4], e8[5]);
+          v.w = pack2<kBf16>(e8[6], e8[7]);
+          *reinterpret_cast<uint4*>(prow + ((c ^ (m_lane & 7)) << 4)) = v;
+        }
+        l_run += lsum;
+        // V rows past the sequence end hold stale pool bytes: zero them (P is 0 there,
+        // but 0 * NaN would not be)
+        const int tail = cw.L - key0;  // valid keys of this chunk
+        if (tail < np * kPage) {
+          uint8_t* vb = ring + (j % kVStages) * kVStageBytes + 2 * kVRegion;
+          const int zr = np * kPage - tail;  // rows tail .. np*16-1, all in the last page
+          for (int it = t; it < zr * 16; it += 128) {
+            const int rowi = tail + (it >> 4), c = it & 15;
+            *reinterpret_cast<uint4*>(vb + (c >> 3) * kVRegion + rowi * 128 + ((c & 7) << 4)) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[j & 1]);
+
+        if (last) {
+          // ---- end of a segment piece: O after the piece's last P V
+          if (!mbar_wait(&o_done[j & 1], (j >> 1) & 1)) ok = false;
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          tc_fence_after();
+          const bool whole_seg = (cw.g + np == cw.seg_end) && (cw.seg_start >= cw.g0);
+          const int seg_id = cw.b * Hkv + cw.h;
+          if (whole_seg) {
+            const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+            T* orow = optr + ((static_cast<int64_t>(cw.b) * p.q_len + qi) * p.num_q_heads + cw.h * p.group + gi) * kHeadDim;
+#pragma unroll 1
+            for (int c0 = 0; c0 < kHeadDim; c0 += 32) {
+              uint32_t ov[32];
+              tmem_ld32(lane_addr + 128 + c0, ov);
+              tmem_ld_wait();
+              if (live) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  uint4 v;
+                  v.x = pack2<kBf16>(__uint_as_float(ov[8 * c + 0]) * inv, __uint_as_float(ov[8 * c + 1]) * inv);
+                  v.y = pack2<kBf16>(__uint_as_float(ov[8 * c + 2]) * inv, __uint_as_float(ov[8 * c + 3]) * inv);
+                  v.z = pack2<kBf16>(__uint_as_float(ov[8 * c + 4]) * inv, __uint_as_float(ov[8 * c + 5]) * inv);
+                  v.w = pack2<kBf16>(__uint_as_float(ov[8 * c + 6]) * inv, __uint_as_float(ov[8 * c + 7]) * inv);
+                  reinterpret_cast<uint4*>(orow + c0)[c] = v;
+                  for (int i2 = 0; i2 < p.num_peers; ++i2)  // the gather slots
+                    reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[i2]) + p.peer_offset +
+                                             (orow - optr) + c0)[c] = v;
+                }
+              }
+            }
+          } else {
+            // partial: unnormalised O and (m, l) in the merge kernel's layout, slot = unit +
+            // segment id; rows nq .. nqp-1 are padding with (m, l) = (-inf, 0) and O = 0
+            const int64_t slot = static_cast<int64_t>(u) + seg_id;
+            float* po = p.part_o + slot * kHeadDim * nqp;
+#pragma unroll 1
+            for (int c0 = 0; c0 < kHeadDim; c0 += 32) {
+              uint32_t ov[32];
+              tmem_ld32(lane_addr + 128 + c0, ov);
+              tmem_ld_wait();
+              if (r < nqp) {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) po[(c0 + e) * nqp + r] = live ? __uint_as_float(ov[e]) : 0.f;
+              }
+            }
+            if (r < nqp)
+              *reinterpret_cast<float2*>(p.part_ml + (slot * nqp + r) * 2) =
+                  live ? make_float2(m_run, l_run) : make_float2(-INFINITY, 0.f);
+            if (t == 0) {
+              const int64_t ss = cw.seg_start, se = cw.seg_end;
+              const int u_first = unit_of(ss, T_pages, U), u_last = unit_of(se - 1, T_pages, U);
+              p.counters[seg_id] = ((u_last - u_first + 1) << 20) | u_first;
+            }
+          }
+          tc_fence_before();
+        }
+        cw.advance(p, prefix, np);
+      }
+      if (!ok) {
+        if (t == 0) report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+        *vabort = 1;
+      }
+    }
+    // sequences without keys: zero output rows
+    if (u < U || T_pages == 0) {
+      const int U0 = T_pages == 0 ? static_cast<int>(gridDim.x) : U;
+      for (int b = u; b < B; b += U0) {
+        if (prefix[b + 1] != prefix[b]) continue;
+        const int64_t n16 = static_cast<int64_t>(p.q_len) * p.num_q_heads * kHeadDim * sizeof(T) / 16;
+        const int64_t base = static_cast<int64_t>(b) * p.q_len * p.num_q_heads * kHeadDim;
+        uint4* dst = reinterpret_cast<uint4*>(optr + base);
+        for (int64_t i = t; i < n16; i += 128) dst[i] = make_uint4(0, 0, 0, 0);
+        for (int i2 = 0; i2 < p.num_peers; ++i2) {
+          uint4* pd = reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[i2]) + p.peer_offset + base);
+          for (int64_t i = t; i < n16; i += 128) pd[i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+    }
+  }
+
+  // ---- teardown: no TMA write may still be in flight into this CTA's ring, and every
+  // tensor-memory access is complete before the columns are released
+  tc_fence_before();
+  __syncthreads();
+  grid_launch_dependents();
+  if (warp == 0 && lane == 0) {
+    // drain (after an abort the MMA warp may not have consumed every stage): wait, bounded,
+    // for the last phase of every stage the producer filled
+    for (int s = 0; s < kVStages && s < fills; ++s) {
+      const int rounds = (fills - s + kVStages - 1) / kVStages;
+      mbar_wait(&full[s], static_cast<uint32_t>((rounds - 1) & 1));
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc1(tmem, kVTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------ generic path
 struct GenericParams {
   void* out;
@@ -902,7 +1411,6 @@ int launch_generic(const GenericParams& gp, int32_t dtype, int32_t num_seqs, cud
 // ------------------------------------------------------------------ fast-path host side
 inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-inline int nq_pad(int nq) { return ((nq + 7) / 8) * 8; }
 
 struct WorkspaceLayout {
   size_t counters, ml, o, total;
@@ -1009,6 +1517,30 @@ int launch_fast(const CUtensorMap& km, const CUtensorMap& vm, const FastParams& 
     case 3: return launch_fast_t<kBf16, 3>(km, vm, fp, grid, smem, s);
     default: return launch_fast_t<kBf16, 4>(km, vm, fp, grid, smem, s);
   }
+}
+
+#ifndef INFERD_VERIFY_TMEM
+#define INFERD_VERIFY_TMEM 0
+#endif
+
+inline size_t verify_smem_bytes(int num_seqs) {
+  return 1024 + kVPrefixOffset + (static_cast<size_t>(num_seqs) + 1) * 4;
+}
+
+template <bool kBf16>
+int launch_verify_tmem(const CUtensorMap& km, const CUtensorMap& vm, const FastParams& fp, int grid,
+                       size_t smem, cudaStream_t s) {
+  static bool configured[64] = {false};
+  const int dev = current_device();
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(paged_verify_tmem_kernel<kBf16>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(verify_smem_bytes(kMaxSeqsFast)));
+    if (e != cudaSuccess) return cuda_status(e);
+    configured[dev] = true;
+  }
+  paged_verify_tmem_kernel<kBf16><<<grid, kVThreads, smem, s>>>(km, vm, fp);
+  return launch_status();
 }
 
 template <bool kBf16, int NQP>
@@ -1192,12 +1724,21 @@ static int paged_attention_impl(void* out, const void* query, const void* key_ca
     // grid: persistent, but no more CTAs than pages can feed (upper bound from the host)
     const int64_t pages_ub = static_cast<int64_t>(nb) * num_kv_heads *
                              ((static_cast<int64_t>(max_context_len) + kPage - 1) / kPage);
-    int g = grid;
-    const int64_t ctas_ub = (pages_ub + kWarps - 1) / kWarps;  // one warp per page at most
-    if (ctas_ub < g) g = ctas_ub > 0 ? static_cast<int>(ctas_ub) : 1;
-    const size_t smem = fast_smem_bytes(nb, nqp);
-    st = dtype == INFERD_BF16 ? launch_fast<true>(km, vm, fp, nqp / 8, g, smem, s)
-                              : launch_fast<false>(km, vm, fp, nqp / 8, g, smem, s);
+    if (INFERD_VERIFY_TMEM && nqp > 8) {
+      // several query rows per kv head: the tensor-memory kernel, one CTA per SM
+      int g = current_sm_count();
+      if (pages_ub < g) g = pages_ub > 0 ? static_cast<int>(pages_ub) : 1;
+      const size_t smem = verify_smem_bytes(nb);
+      st = dtype == INFERD_BF16 ? launch_verify_tmem<true>(km, vm, fp, g, smem, s)
+                                : launch_verify_tmem<false>(km, vm, fp, g, smem, s);
+    } else {
+      int g = grid;
+      const int64_t ctas_ub = (pages_ub + kWarps - 1) / kWarps;  // one warp per page at most
+      if (ctas_ub < g) g = ctas_ub > 0 ? static_cast<int>(ctas_ub) : 1;
+      const size_t smem = fast_smem_bytes(nb, nqp);
+      st = dtype == INFERD_BF16 ? launch_fast<true>(km, vm, fp, nqp / 8, g, smem, s)
+                                : launch_fast<false>(km, vm, fp, nqp / 8, g, smem, s);
+    }
     if (st != INFERD_OK) return st;
     if (defer_merge) {
       st = dtype == INFERD_BF16 ? launch_merge<true>(fp, nqp / 8, nb * num_kv_heads, s)

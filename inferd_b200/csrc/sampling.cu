@@ -28,6 +28,7 @@
 #include <cuda_fp16.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "common.cuh"
 #include "runtime.cuh"
@@ -600,9 +601,15 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
 // other entry without computing p; each candidate's exact p goes into a per-CTA list in
 // index order.  Rows whose candidates overflow a list, and rows with top_p >= 1, take the
 // full path: the same steps over every entry, p recomputed in each pass.
+#ifndef INFERD_N16_CTAS_PER_SM
+#define INFERD_N16_CTAS_PER_SM 2
+#endif
 constexpr int kN16Threads = 512;
-constexpr int kN16MaxPerCta = 38912;  // 16-bit logits per CTA (76 KB)
-constexpr int kN16ListCap = 4096;     // candidates per CTA: local index (u16) + p (f32)
+constexpr int kN16CtasPerSm = INFERD_N16_CTAS_PER_SM;
+constexpr int kN16MaxPerCta = 38912 * 2 / kN16CtasPerSm;  // 16-bit logits per CTA (76 KB at 2 / SM)
+constexpr int kN16ListCap = 4096 * 2 / kN16CtasPerSm;  // candidates per CTA: local index + p (f32)
+// local index of a candidate: 16 bits while a CTA's slice fits them
+using N16Idx = std::conditional<(kN16MaxPerCta > 65536), uint32_t, uint16_t>::type;
 constexpr int kN16Chunk = kN16Threads * 8;  // index-ordered passes: 8 consecutive per thread
 static_assert(kN16Threads / 32 == kSampWarps, "the block reductions assume 16 warps");
 
@@ -612,14 +619,20 @@ struct N16Shared {
   float wf[kSampWarps];
   int wi[kSampWarps];
   unsigned long long wu[kSampWarps];
-  // values published to the cluster
+  // values published to the cluster (an exchange with a slot of its own, written once,
+  // needs one cluster barrier; the kernel's last barrier keeps every CTA alive until the
+  // others have read its slots)
   float x_f;
   int x_i;
   unsigned long long x_u;
+  float x_mz[2];              // block max of the logits, block sum z relative to it
+  unsigned long long x_kept;  // kept mass of the CTA
   // broadcasts
   uint32_t b_prefix;
   unsigned long long b_mass;
   uint32_t b_ties;
+  uint32_t b_ties_before;  // entries equal to the threshold in lower-ranked CTAs
+  uint32_t b_ties_mine;    // and in this CTA
   unsigned long long b_u;
   float b_f;
   int b_i;
@@ -631,7 +644,7 @@ __host__ __device__ constexpr size_t n16_list_offset(int per_cta) {
   return (static_cast<size_t>(per_cta) * 2 + 15) / 16 * 16;
 }
 __host__ __device__ constexpr size_t n16_smem_bytes(int per_cta) {
-  return n16_list_offset(per_cta) + static_cast<size_t>(kN16ListCap) * (2 + 4);
+  return n16_list_offset(per_cta) + static_cast<size_t>(kN16ListCap) * (sizeof(N16Idx) + 4);
 }
 
 template <typename In>
@@ -661,11 +674,6 @@ struct N16Prob {
   bool t_ok, z_ok;
   __device__ __forceinline__ float y(float x) const { return div_rn(x, temp, rt, t_ok); }
   __device__ __forceinline__ float e(float x) const { return expf(y(x) - ymax); }
-  // the same term for the sum z only, as 2^((y - ymax) log2 e) on the ex2 unit: it differs
-  // from expf by a few parts in 10^7 at most, and z is a sum of such terms
-  __device__ __forceinline__ float e_sum(float x) const {
-    return ex2(__fmul_rn(y(x) - ymax, 1.4426950408889634f));
-  }
   __device__ __forceinline__ float operator()(float x) const { return div_rn(e(x), z, rz, z_ok); }
 };
 
@@ -679,7 +687,8 @@ struct N16Prob {
 // read it once this pass's cluster barrier is passed), and one more block barrier.
 template <int C, bool kCluster, class Each>
 __device__ uint32_t n16_radix_select(N16Shared& sh, unsigned long long limit, Each each,
-                                     unsigned long long& above_out, uint32_t& ties_out) {
+                                     unsigned long long& above_out, uint32_t& ties_out,
+                                     uint32_t& ties_before_out, uint32_t& ties_mine_out) {
   constexpr int R = kCluster ? C : 1;  // CTAs whose histograms are summed
   const int tid = threadIdx.x, lane = tid & 31;
   for (int b = tid; b < 2 * 256; b += kN16Threads) {
@@ -765,6 +774,24 @@ __device__ uint32_t n16_radix_select(N16Shared& sh, unsigned long long limit, Ea
         sh.b_mass = best_acc;
         sh.b_ties = best_cnt;
       }
+      if (shift == 0) {
+        // the final bin holds exactly the entries equal to the threshold: its count in each
+        // CTA (lane r reads CTA r's), split into the CTAs ranked below this one and this CTA
+        const uint32_t me = kCluster ? samp_rank() : 0u;
+        uint32_t cnt = 0;
+        if (lane < R) cnt = kCluster ? *cl_ptr(hc + best, static_cast<uint32_t>(lane)) : hc[best];
+        uint32_t before = static_cast<uint32_t>(lane) < me ? cnt : 0u;
+        uint32_t mine = static_cast<uint32_t>(lane) == me ? cnt : 0u;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          before += __shfl_xor_sync(0xffffffffu, before, o);
+          mine += __shfl_xor_sync(0xffffffffu, mine, o);
+        }
+        if (lane == 0) {
+          sh.b_ties_before = before;
+          sh.b_ties_mine = mine;
+        }
+      }
     } else if (shift > 0) {
       uint32_t* zm = sh.hist_m[buf ^ 1];
       uint32_t* zc = sh.hist_c[buf ^ 1];
@@ -778,9 +805,12 @@ __device__ uint32_t n16_radix_select(N16Shared& sh, unsigned long long limit, Ea
     above = sh.b_mass;
     ties = sh.b_ties;
   }
+  const uint32_t tb = sh.b_ties_before, tm = sh.b_ties_mine;
   __syncthreads();  // the broadcast slots are reused by the caller
   above_out = above;
   ties_out = ties;
+  ties_before_out = tb;
+  ties_mine_out = tm;
   return prefix;
 }
 
@@ -821,12 +851,12 @@ __device__ int n16_kth(N16Shared& sh, int count, unsigned long long k, Pred pred
 
 // mode 0 only, In = bf16 or f16.
 template <int C, typename In>
-__global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampParams p) {
+__global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(const SampParams p) {
   extern __shared__ __align__(16) uint8_t n16_dyn[];
   __shared__ N16Shared sh;
   uint16_t* xs = reinterpret_cast<uint16_t*>(n16_dyn);
-  uint16_t* lidx = reinterpret_cast<uint16_t*>(n16_dyn + n16_list_offset(p.per_cta));
-  float* lp = reinterpret_cast<float*>(n16_dyn + n16_list_offset(p.per_cta) + kN16ListCap * 2);
+  N16Idx* lidx = reinterpret_cast<N16Idx*>(n16_dyn + n16_list_offset(p.per_cta));
+  float* lp = reinterpret_cast<float*>(n16_dyn + n16_list_offset(p.per_cta) + kN16ListCap * sizeof(N16Idx));
   const int tid = threadIdx.x;
   const uint32_t rank = samp_rank();
   const int row = blockIdx.x / C;
@@ -838,38 +868,75 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
   const float top_p = p.top_ps ? p.top_ps[row] : p.top_p;
   const bool greedy = !(temp > 0.f);
 
-  // ---- phase 1: stage the raw logits, row max
-  float mx = -INFINITY;
+  // ---- phase 1: stage the raw logits; per thread the running max of x and the sum z of
+  // 2^((x/T - y(max)) log2 e) relative to it (rescaled when the max grows), so one pass
+  // and one cluster exchange give the row max and z.  The terms of z come from the ex2
+  // unit: each differs from expf by a few parts in 10^7 at most.
+  N16Prob pr;
+  pr.temp = temp;
+  pr.rt = greedy ? 0.f : __frcp_rn(temp);
+  pr.t_ok = !greedy && div_ok(temp);
+  constexpr float kLog2e = 1.4426950408889634f;
+  float mx = -INFINITY, zs = 0.f;
+  // fold cnt values whose max is cm into (mx, zs)
+  auto absorb = [&](const float* f, int cnt, float cm) {
+    if (greedy) {
+      mx = fmaxf(mx, cm);
+      return;
+    }
+    if (cm > mx) {
+      if (zs != 0.f) zs *= ex2(__fmul_rn(pr.y(mx) - pr.y(cm), kLog2e));
+      mx = cm;
+    }
+    if (mx == -INFINITY) return;
+    const float ym = pr.y(mx);
+    for (int j = 0; j < cnt; ++j) zs += ex2(__fmul_rn(pr.y(f[j]) - ym, kLog2e));
+  };
   {
     int done = 0;
     if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
       const int nv = n / 8;
       const uint4* s4 = reinterpret_cast<const uint4*>(src);
       uint4* x4 = reinterpret_cast<uint4*>(xs);
-#pragma unroll 4
+#pragma unroll 2
       for (int v = tid; v < nv; v += kN16Threads) {
         const uint4 raw = __ldg(s4 + v);
         x4[v] = raw;
         const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw);
+        float f[8];
+        float cm = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, h16_to_f32<In>(h[j]));
+        for (int j = 0; j < 8; ++j) {
+          f[j] = h16_to_f32<In>(h[j]);
+          cm = fmaxf(cm, f[j]);
+        }
+        absorb(f, 8, cm);
       }
       done = nv * 8;
     }
     for (int i = done + tid; i < n; i += kN16Threads) {
       const uint16_t b = src[i];
       xs[i] = b;
-      mx = fmaxf(mx, h16_to_f32<In>(b));
+      const float f = h16_to_f32<In>(b);
+      absorb(&f, 1, f);
     }
   }
-  int dummy = 0;
-  block_argmax(sh, mx, dummy);
-  if (tid == 0) sh.x_f = mx;
+  float bmax = mx;
+  {
+    int dummy = 0;
+    block_argmax(sh, bmax, dummy);
+  }
+  float bz = 0.f;
+  if (!greedy && zs != 0.f) bz = zs * ex2(__fmul_rn(pr.y(mx) - pr.y(bmax), kLog2e));
+  bz = block_sum_f32(sh, bz);
+  if (tid == 0) {
+    sh.x_mz[0] = bmax;
+    sh.x_mz[1] = bz;
+  }
   samp_cluster_sync();
   float xmax = -INFINITY;
 #pragma unroll
-  for (int r = 0; r < C; ++r) xmax = fmaxf(xmax, ld_cl_f32(&sh.x_f, r));
-  samp_cluster_sync();
+  for (int r = 0; r < C; ++r) xmax = fmaxf(xmax, ld_cl_f32(&sh.x_mz[0], r));
 
   float* out = p.probs_out ? p.probs_out + static_cast<int64_t>(row) * p.out_stride + lo : nullptr;
   if (greedy) {
@@ -891,33 +958,14 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
     return;
   }
 
-  // ---- phase 2: z = sum of exp(x / T - ymax)
-  N16Prob pr;
-  pr.temp = temp;
-  pr.rt = __frcp_rn(temp);
-  pr.t_ok = div_ok(temp);
+  // ---- phase 2: z = sum of exp(x / T - ymax), the CTAs' sums moved to the row max
   pr.ymax = __fdiv_rn(xmax, temp);
-  float zs = 0.f;
-  {
-    const uint4* x4 = reinterpret_cast<const uint4*>(xs);
-    const int nv = n / 8;
-    for (int v = tid; v < nv; v += kN16Threads) {
-      const uint4 raw = x4[v];
-      const uint16_t* h = reinterpret_cast<const uint16_t*>(&raw);
-      float part = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) part += pr.e_sum(h16_to_f32<In>(h[j]));
-      zs += part;
-    }
-    for (int i = nv * 8 + tid; i < n; i += kN16Threads) zs += pr.e_sum(h16_to_f32<In>(xs[i]));
-  }
-  zs = block_sum_f32(sh, zs);
-  if (tid == 0) sh.x_f = zs;
-  samp_cluster_sync();
   float z = 0.f;
 #pragma unroll
-  for (int r = 0; r < C; ++r) z += ld_cl_f32(&sh.x_f, r);
-  samp_cluster_sync();
+  for (int r = 0; r < C; ++r) {
+    const float cz = ld_cl_f32(&sh.x_mz[1], r);
+    if (cz != 0.f) z += cz * ex2(__fmul_rn(pr.y(ld_cl_f32(&sh.x_mz[0], r)) - pr.ymax, kLog2e));
+  }
   pr.z = z;
   pr.rz = __frcp_rn(z);
   pr.z_ok = div_ok(z);
@@ -993,7 +1041,7 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         if ((bits >> j) & 1u) {
-          if (at < kN16ListCap) lidx[at] = static_cast<uint16_t>(c + 8 * lane + j);
+          if (at < kN16ListCap) lidx[at] = static_cast<N16Idx>(c + 8 * lane + j);
           ++at;
         }
       }
@@ -1001,14 +1049,11 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
     }
     __syncthreads();
     for (int j = tid; j < count && j < kN16ListCap; j += kN16Threads) lp[j] = prob(lidx[j]);
-    if (tid == 0) sh.x_i = count;
     __syncthreads();
-    samp_cluster_sync();
-    int worst = 0;
-#pragma unroll
-    for (int r = 0; r < C; ++r) worst = max(worst, static_cast<int>(ld_cl_u32(&sh.x_i, r)));
-    samp_cluster_sync();
-    fast = worst <= kN16ListCap;
+    // A CTA whose list overflowed takes the full path alone: every entry off the list has
+    // p below the proven bound, under the threshold, so it adds only to histogram bins
+    // below each pass's cut bin and never to the kept set.
+    fast = count <= kN16ListCap;
   }
   // every entry of this CTA's set, as f(p) (list entries, or every logit)
   auto each = [&](auto&& f) {
@@ -1025,8 +1070,8 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
   int i_cut = 0x7fffffff;  // ties at tbits are kept below this global index
   if (cut) {
     unsigned long long above;
-    uint32_t ties;
-    tbits = n16_radix_select<C, true>(sh, limit, each, above, ties);
+    uint32_t ties, ties_before, ties_mine;
+    tbits = n16_radix_select<C, true>(sh, limit, each, above, ties, ties_before, ties_mine);
     const unsigned long long tq = to_q31(__uint_as_float(tbits));
     uint32_t keep_ties = ties;
     if (tq > 0) {
@@ -1034,27 +1079,18 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
       if (room < keep_ties) keep_ties = static_cast<uint32_t>(room);
     }
     if (keep_ties < ties) {
-      // the first dropped tie is the keep_ties-th tie in index order
-      unsigned long long mine = 0;
-      each([&](float v) { mine += __float_as_uint(v) == tbits ? 1u : 0u; });
-      mine = block_sum_u64(sh, mine);
-      if (tid == 0) sh.x_u = mine;
-      samp_cluster_sync();
-      unsigned long long before = 0;
-      for (uint32_t r = 0; r < rank; ++r) before += ld_cl_u64(&sh.x_u, r);
-      samp_cluster_sync();
-      int local_cut = -1;
-      if (keep_ties >= before && keep_ties < before + mine) {
-        const unsigned long long k = keep_ties - before;
-        local_cut = fast ? n16_kth(sh, count, k, [&](int j) { return __float_as_uint(lp[j]) == tbits; })
-                         : n16_kth(sh, n, k, [&](int i) { return __float_as_uint(prob(i)) == tbits; });
+      // the ties are kept in index order: the first keep_ties of them, of which this CTA
+      // (after ties_before in lower-ranked CTAs) keeps its first keep_mine
+      const uint32_t keep_mine =
+          keep_ties <= ties_before ? 0u : min(ties_mine, keep_ties - ties_before);
+      if (keep_mine == 0) {
+        i_cut = static_cast<int>(lo);  // none of this CTA's ties
+      } else if (keep_mine < ties_mine) {
+        int local_cut = fast ? n16_kth(sh, count, keep_mine, [&](int j) { return __float_as_uint(lp[j]) == tbits; })
+                             : n16_kth(sh, n, keep_mine, [&](int i) { return __float_as_uint(prob(i)) == tbits; });
         if (fast && local_cut >= 0) local_cut = lidx[local_cut];
+        if (local_cut >= 0) i_cut = static_cast<int>(lo) + local_cut;
       }
-      if (tid == 0) sh.x_i = local_cut >= 0 ? static_cast<int>(lo) + local_cut : 0x7fffffff;
-      samp_cluster_sync();
-#pragma unroll
-      for (int r = 0; r < C; ++r) i_cut = min(i_cut, static_cast<int>(ld_cl_u32(&sh.x_i, r)));
-      samp_cluster_sync();
     }
   }
   auto kept = [&](float v, int gi) {
@@ -1076,16 +1112,15 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
     }
   }
   local = block_sum_u64(sh, local);
-  if (tid == 0) sh.x_u = local;
+  if (tid == 0) sh.x_kept = local;
   samp_cluster_sync();
   unsigned long long base = 0, total = 0;
 #pragma unroll
   for (int r = 0; r < C; ++r) {
-    const unsigned long long v = ld_cl_u64(&sh.x_u, r);
+    const unsigned long long v = ld_cl_u64(&sh.x_kept, r);
     if (r < static_cast<int>(rank)) base += v;
     total += v;
   }
-  samp_cluster_sync();
 
   // ---- phase 5: renormalised probabilities
   if (out) {
@@ -1114,14 +1149,12 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
   }
 
   // ---- phase 6: one draw, inverse CDF in index order over the kept masses
-  if (p.tokens) {
-    if (total == 0) {
-      if (rank == 0 && tid == 0) {
-        p.tokens[row] = -1;
-        report_error(p.error_word, INFERD_ERR_INVALID_ARGUMENT);
-      }
-      return;
+  if (p.tokens && total == 0) {
+    if (rank == 0 && tid == 0) {
+      p.tokens[row] = -1;
+      report_error(p.error_word, INFERD_ERR_INVALID_ARGUMENT);
     }
+  } else if (p.tokens) {
     const unsigned long long target = __umul64hi(philox_u64(p.seed, p.offset + static_cast<uint64_t>(row)), total);
     if (target >= base && target < base + local) {
       // weights of the entries of this CTA in index order (candidates or every logit)
@@ -1163,6 +1196,8 @@ __global__ void __launch_bounds__(kN16Threads, 2) nucleus16_kernel(const SampPar
       }
     }
   }
+  // no CTA leaves while another may still read its exchange slots
+  samp_cluster_sync();
 }
 
 template <int C, typename In>

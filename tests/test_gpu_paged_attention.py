@@ -303,6 +303,25 @@ def test_verify_window_sizes(cuda_device, q_len):
     assert_bf16_close(out, ref, f"verify q_len {q_len}")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_verify_stale_pool_bytes_and_empty_sequences(cuda_device, dtype):
+    # NaN in every pool byte past each sequence end (and in unused blocks) must not reach
+    # the output; a sequence without keys gives zero rows
+    lens = [0, 5, 16, 23, 64, 65, 300, 1000]
+    out, ref = run_batched(cuda_device, lens, 5, 32, 8, dtype, seed=21, poison=True)
+    assert np.isfinite(out).all()
+    assert_bf16_close(out, ref, "poisoned pool, verify")
+    assert np.all(out[0] == 0)
+
+
+@pytest.mark.parametrize("q_len,hq,hkv", [(2, 64, 8), (4, 64, 8), (3, 24, 8), (8, 32, 8)])
+def test_verify_row_counts(cuda_device, q_len, hq, hkv):
+    # 16, 32, 9 and 32 query rows per kv head
+    lens = [1, 9, 63, 64, 129, 2000]
+    out, ref = run_batched(cuda_device, lens, q_len, hq, hkv, torch.bfloat16, seed=30 + q_len)
+    assert_bf16_close(out, ref, f"q_len {q_len}, {hq}/{hkv} heads")
+
+
 def test_verify_short_context_rows_are_zero(cuda_device):
     # queries whose position is negative (context shorter than the window) see no keys
     out, ref = run_batched(cuda_device, [2, 30], 5, 16, 4, torch.bfloat16, seed=20)

@@ -221,6 +221,24 @@ def test_bf16_tied_group_cut_across_ctas_in_index_order(cuda_device):
         np.testing.assert_allclose(got[r][kept], 1.0 / n_keep, rtol=1e-6)
 
 
+@pytest.mark.parametrize("cta,tied", [(0, True), (1, False), (3, True)])
+def test_bf16_one_cta_overflows_its_candidate_list(cuda_device, cta, tied):
+    # 6000 high entries inside one CTA's slice (four CTAs per 151936-entry row) overflow that
+    # CTA's 4096-entry candidate list: it takes the full path while the other CTAs keep
+    # their lists, and the kept set still follows the one rule (ties in index order)
+    vocab = 151936
+    per = ((vocab + 3) // 4 + 7) // 8 * 8
+    g = torch.Generator().manual_seed(40 + cta)
+    logits = torch.randn(2, vocab, generator=g) * 3.0
+    idx = per * cta + torch.randperm(per, generator=g)[:6000]
+    logits[:, idx] = 7.0 if tied else 6.0 + torch.rand(2, 6000, generator=g)
+    logits = logits.to(torch.bfloat16)
+    got = nucleus_probs(logits.to(cuda_device), 0.7, 0.9).cpu().numpy()
+    _boundary_ok(got, logits.float().numpy(), 0.7, 0.9)
+    np.testing.assert_allclose(got.sum(axis=1), 1.0, rtol=1e-5)
+    assert np.count_nonzero(got[:, idx.numpy()]) > 0  # the overflowing CTA holds kept entries
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_greedy_rows_half_logits(cuda_device, dtype):
     logits = torch.randn(4, 151936, device=cuda_device).to(dtype)
