@@ -781,22 +781,25 @@ __global__ void __launch_bounds__(kHeadDim) merge_cut_segments_kernel(const Fast
 // Windows of several query rows per kv head (speculative verify: q_len x group rows, 9 to
 // 32 of them).  One persistent CTA per SM streams the balanced page range of its unit
 // (CTA) in chunks of up to four pages of one segment:
-//   warp 0      lane 0 issues the TMA loads of a chunk (K and V, 128-byte swizzle) into a
-//               4-stage ring; each stage holds K lo | K hi | V lo | V hi, 64 rows x 128 B
-//               each, so the chunk's keys form one K-major (and one MN-major) operand;
-//   warp 1      lane 0 issues tcgen05.mma: S = Q K^T (M = 128 rows, N = 64 keys, K = 128,
-//               into one of two 64-column tensor-memory buffers), and O += P V (M = 128,
-//               N = 128, one K = 16 step per page, V as an MN-major operand) into 128
-//               columns that hold O for the whole segment;
-//   warps 2-5   one thread per query row (row r in tensor-memory lane 32 (r % 4) + r / 4):
-//               read the row's 64 scores, mask, online softmax in base 2 with a lazy
-//               rescale (O and l are rescaled only when the running maximum grows by more
-//               than 2^8), write P (16-bit, K-major, swizzled) for the P V MMA, and at the
-//               end of a segment piece read O, normalise and store (or leave a partial for
-//               merge_cut_segments_kernel).
+//   warp 0      issues the TMA loads of a chunk (K and V, 128-byte swizzle; 16 boxes, one
+//               per lane) into a 4-stage ring; each stage holds K lo | K hi | V lo | V hi,
+//               64 rows x 128 B each, so the chunk's keys form one K-major (and one
+//               MN-major) operand;
+//   warp 1      lane 0 issues tcgen05.mma: S = Q K^T (M = 128, N = 64 keys, K = 128, into
+//               one of two 64-column tensor-memory buffers) and O += P V (M = 128, N = 128,
+//               one K = 16 step per page, V as an MN-major operand) into 128 columns that
+//               hold O for the whole segment piece, each as soon as its inputs are ready;
+//   warps 2-5   softmax.  Query row i (i < nq) sits in all four tensor-memory lane
+//               quarters (MMA rows 32 q + i, Q replicated); the warp of quarter q reads
+//               keys [16 q, 16 q + 16) of the chunk, the four agree on the chunk maximum
+//               through shared memory, and each writes its 16 probabilities (16-bit) into
+//               row i of the P tile, whose rows 32 .. 127 stay zero.  So one P V MMA
+//               accumulates row i's whole O in quarter 0.  Online softmax in base 2 with a
+//               lazy rescale (O and l are rescaled only when the running maximum grows by
+//               more than 2^8).  At the end of a segment piece quarter 0 reads O,
+//               normalises and stores (or leaves a partial for merge_cut_segments_kernel).
 // The Q tile of the next segment is written as soon as the last S of the current one has
-// been read, so the MMA warp runs one chunk ahead of the softmax warps (S(i+1) is computed
-// while softmax(i) runs) and the ring keeps four chunks of loads in flight.
+// been read.
 constexpr int kVPages = 4;                       // pages per chunk
 constexpr int kVKeys = kVPages * kPage;          // 64 keys: N of S, K of P V
 constexpr int kVStages = 4;
@@ -804,7 +807,7 @@ constexpr int kVRegion = kVPages * kHalfBytes;   // 8 KiB: 64 rows x 128 B
 constexpr int kVStageBytes = 4 * kVRegion;       // K lo | K hi | V lo | V hi
 constexpr int kVQBytes = 2 * 128 * 128;          // Q tile, 128 rows x 256 B (lo | hi halves)
 constexpr int kVPBytes = 128 * 128;              // P tile, 128 rows x 64 keys x 2 B
-constexpr int kVThreads = 192;
+constexpr int kVThreads = 192;                 // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
 constexpr int kVTmemCols = 256;                  // S0 [0, 64) | S1 [64, 128) | O [128, 256)
 constexpr float kVRescale = 8.f;                 // lazy rescale threshold (log2 units)
 constexpr int kVBarOffset = kVStages * kVStageBytes + kVQBytes + 2 * kVPBytes;
@@ -817,9 +820,6 @@ __host__ __device__ constexpr uint32_t f16_idesc(bool bf16, bool b_mn_major, int
          ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(128 >> 4) << 24);
 }
-
-// tensor-memory lane (= MMA row) of query row r
-__device__ __forceinline__ int vrow_lane(int r) { return 32 * (r & 3) + (r >> 2); }
 
 // The unit's page range [g0, g1) walked in chunks: at most kVPages pages, never across a
 // segment or past the range.  Every role walks the same sequence.
@@ -866,6 +866,8 @@ __global__ void __launch_bounds__(kVThreads, 1)
   __shared__ int warp_tot[kVThreads / 32];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
+  __shared__ float rmax[2 * 128];  // [chunk parity][key subset][row] chunk maxima
+  __shared__ float rsum[128];      // [key subset][row] l at the end of a piece
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* ring = smem;
@@ -958,19 +960,22 @@ __global__ void __launch_bounds__(kVThreads, 1)
         }
         uint8_t* st = ring + s * kVStageBytes;
         if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(np) * kStageBytes);
-        for (int q = 0; q < np; ++q) {
-          const int64_t gq = cw.g + q;
-          if (gq >= batch0 + 32) {  // rotate the batches (warp-uniform)
+        __syncwarp();
+        {
+          // lane 4q + t issues box t (K lo, K hi, V lo, V hi) of page q of the chunk; the
+          // chunk starts inside the current batch and ends at most 3 pages past it
+          const int q = lane >> 2, box = lane & 3;
+          const int idx = static_cast<int>(cw.g - batch0) + q;
+          const int32_t rc = __shfl_sync(0xffffffffu, rows_cur, idx & 31);
+          const int32_t rn = __shfl_sync(0xffffffffu, rows_next, idx & 31);
+          const int32_t r = idx < 32 ? rc : rn;
+          if (q < np)
+            tma_load_2d(st + box * kVRegion + q * kHalfBytes, box < 2 ? &kmap : &vmap, (box & 1) * 64, r,
+                        &full[s], policy);
+          if (cw.g + np >= batch0 + 32) {  // rotate the batches (warp-uniform)
             batch0 += 32;
             rows_cur = rows_next;
             rows_next = batch0 + 32 + lane < g1 ? row_of(batch0 + 32 + lane) : 0;
-          }
-          const int32_t r = __shfl_sync(0xffffffffu, rows_cur, static_cast<int>(gq - batch0));
-          if (lane == 0) {
-            tma_load_2d(st + q * kHalfBytes, &kmap, 0, r, &full[s], policy);
-            tma_load_2d(st + kVRegion + q * kHalfBytes, &kmap, 64, r, &full[s], policy);
-            tma_load_2d(st + 2 * kVRegion + q * kHalfBytes, &vmap, 0, r, &full[s], policy);
-            tma_load_2d(st + 3 * kVRegion + q * kHalfBytes, &vmap, 64, r, &full[s], policy);
           }
         }
         ++fills;
@@ -978,56 +983,67 @@ __global__ void __launch_bounds__(kVThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer (one thread)
+    // ---------------- MMA issuer (one thread): S(i) = Q K^T as soon as chunk i's K has
+    // landed and S buffer i % 2 is free; O += P(j) V(j) as soon as P(j) is written.  Both
+    // are polled without blocking, so a P V never waits for a later chunk's data.
     if (active && lane == 0) {
       const uint32_t idesc_s = f16_idesc(kBf16, false, kVKeys);
       const uint32_t idesc_o = f16_idesc(kBf16, true, kHeadDim);
       const uint32_t q_base = smem_u32(qtile), p_base = smem_u32(ptile), r_base = smem_u32(ring);
-      ChunkWalk cw;
-      cw.init(p, prefix, g0, g1);
-      int piece = 0;
-      int prev_np = 0, prev_first = 0;
+      ChunkWalk ws, wp;  // the next S chunk, the next P V chunk
+      ws.init(p, prefix, g0, g1);
+      wp.init(p, prefix, g0, g1);
+      int ns = 0, npv = 0, piece = 0;
       bool ok = true;
-      // O += P(j) V(j), one K = 16 step per page of chunk j
-      auto issue_pv = [&](int j, int np, bool first) -> bool {
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1)) return false;
-        tc_fence_after();
-        const uint32_t pa = p_base + (j & 1) * kVPBytes;
-        const uint32_t va = r_base + (j % kVStages) * kVStageBytes + 2 * kVRegion;
-        for (int q = 0; q < np; ++q)
-          mma_f16_1(tmem + 128, sw128_desc(pa + q * 32), sw128_mn_desc(va + q * kHalfBytes, kVRegion, 1024),
-                    idesc_o, (first && q == 0) ? 0u : 1u);
-        mma_commit1(&o_done[j & 1]);
-        mma_commit1(&empty[j % kVStages]);
-        return true;
-      };
-      int i = 0;
-      for (; !cw.done() && ok; ++i) {
-        const int np = cw.pages();
-        const bool first = cw.first();
-        if (*vabort) { ok = false; break; }
-        if (first) {
-          ok = mbar_wait(q_full, piece & 1);
-          ++piece;
+      uint64_t t_last = globaltimer();
+      uint32_t spins = 0;
+      while (ok) {
+        bool did = false;
+        if (npv < ns && mbar_test_wait(&p_full[npv & 1], (npv >> 1) & 1)) {
+          tc_fence_after();
+          const int np = wp.pages();
+          const bool first = wp.first();
+          const uint32_t pa = p_base + (npv & 1) * kVPBytes;
+          const uint32_t va = r_base + (npv % kVStages) * kVStageBytes + 2 * kVRegion;
+          for (int q = 0; q < np; ++q)
+            mma_f16_1(tmem + 128, sw128_desc(pa + q * 32), sw128_mn_desc(va + q * kHalfBytes, kVRegion, 1024),
+                      idesc_o, (first && q == 0) ? 0u : 1u);
+          mma_commit1(&o_done[npv & 1]);
+          mma_commit1(&empty[npv % kVStages]);
+          wp.advance(p, prefix, np);
+          ++npv;
+          did = true;
         }
-        if (ok) ok = mbar_wait(&full[i % kVStages], (i / kVStages) & 1);
-        if (ok && i >= 2) ok = mbar_wait(&s_free[i & 1], ((i >> 1) - 1) & 1);
-        if (!ok) break;
-        tc_fence_after();
-        // S(i) = Q K^T over the 128 dims: 8 K-steps of 16 (lo half, then hi half)
-        const uint32_t ka = r_base + (i % kVStages) * kVStageBytes;
-        const uint32_t sc = tmem + (i & 1) * kVKeys;
+        if (!ws.done()) {
+          const bool first = ws.first();
+          if ((!first || mbar_test_wait(q_full, piece & 1)) &&
+              mbar_test_wait(&full[ns % kVStages], (ns / kVStages) & 1) &&
+              (ns < 2 || mbar_test_wait(&s_free[ns & 1], ((ns >> 1) - 1) & 1))) {
+            tc_fence_after();
+            const uint32_t ka = r_base + (ns % kVStages) * kVStageBytes;
+            const uint32_t sc = tmem + (ns & 1) * kVKeys;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_f16_1(sc, sw128_desc(q_base + (kk >> 2) * (kVQBytes / 2) + (kk & 3) * 32),
-                    sw128_desc(ka + (kk >> 2) * kVRegion + (kk & 3) * 32), idesc_s, kk > 0 ? 1u : 0u);
-        mma_commit1(&s_full[i & 1]);
-        if (i > 0) ok = issue_pv(i - 1, prev_np, prev_first != 0);
-        prev_np = np;
-        prev_first = first ? 1 : 0;
-        cw.advance(p, prefix, np);
+            for (int kk = 0; kk < 8; ++kk)
+              mma_f16_1(sc, sw128_desc(q_base + (kk >> 2) * (kVQBytes / 2) + (kk & 3) * 32),
+                        sw128_desc(ka + (kk >> 2) * kVRegion + (kk & 3) * 32), idesc_s, kk > 0 ? 1u : 0u);
+            mma_commit1(&s_full[ns & 1]);
+            if (first) ++piece;
+            ws.advance(p, prefix, ws.pages());
+            ++ns;
+            did = true;
+          }
+        } else if (npv == ns) {
+          break;  // every S and every P V issued
+        }
+        if (did) {
+          t_last = globaltimer();
+          spins = 0;
+        } else {
+          // back off: this warp shares its scheduler with a softmax warp
+          __nanosleep(64);
+          if ((++spins & 63u) == 0u && (*vabort || globaltimer() - t_last > kWaitTimeoutNs)) ok = false;
+        }
       }
-      if (ok && i > 0) ok = issue_pv(i - 1, prev_np, prev_first != 0);
       if (!ok) {
         report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
         *vabort = 1;
@@ -1037,38 +1053,52 @@ __global__ void __launch_bounds__(kVThreads, 1)
       mbar_wait(m_done, 0);
     }
   } else {
-    // ---------------- softmax / epilogue: one thread per query row
+    // ---------------- softmax / epilogue.  Query row i (< nq <= 32) is replicated in the
+    // four tensor-memory lane quarters (MMA rows 32 q + i); the warp of quarter q reads keys
+    // [16 q, 16 q + 16) of each chunk from its replica and writes their p into the P row of
+    // replica 0, whose other replicas' P rows stay zero.  So P V accumulates the whole O of
+    // row i in quarter 0, and the softmax work of a row is spread over four threads.
     const int t = tid - 64;                  // 0..127
-    const int qd = warp & 3;                 // tensor-memory lane quarter of this warp
-    const int r = 4 * lane + qd;             // query row of this thread
-    const int m_lane = 32 * qd + lane;       // its MMA row
-    const bool live = r < p.nq;
-    const int qi = live ? r / p.group : 0, gi = live ? r - qi * p.group : 0;
+    const int qd = warp & 3;                 // lane quarter = key subset of this warp
+    const int i = lane;                      // query row of this thread
+    const bool live = i < p.nq;
+    const int qi = live ? i / p.group : 0, gi = live ? i - qi * p.group : 0;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * qd) << 16);
     const T* qptr = static_cast<const T*>(p.query);
     T* optr = static_cast<T*>(p.out);
     const int nqp = nq_pad(p.nq);            // column count of the partial layout
 
-    // Q rows of segment (b, h) into the Q tile (K-major, 128-byte swizzle, lo | hi halves)
+    // Q rows of segment (b, h) into rows 32 q + i of the Q tile (K-major, 128-byte swizzle,
+    // lo | hi halves), all four replicas
     auto write_q = [&](int b, int h) {
       for (int it = t; it < p.nq * 16; it += 128) {
         const int rr = it >> 4, c = it & 15;
         const int q2 = rr / p.group, g2 = rr - q2 * p.group;
         const uint4 v = __ldg(reinterpret_cast<const uint4*>(
             qptr + ((static_cast<int64_t>(b) * p.q_len + q2) * p.num_q_heads + h * p.group + g2) * kHeadDim) + c);
-        const int ml = vrow_lane(rr);
-        *reinterpret_cast<uint4*>(qtile + (c >> 3) * (kVQBytes / 2) + ml * 128 + (((c & 7) ^ (ml & 7)) << 4)) = v;
+#pragma unroll
+        for (int rep = 0; rep < 4; ++rep) {
+          const int ml = 32 * rep + rr;
+          *reinterpret_cast<uint4*>(qtile + (c >> 3) * (kVQBytes / 2) + ml * 128 + (((c & 7) ^ (ml & 7)) << 4)) = v;
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_full);
     };
+    // P rows 32 .. 127 (the replicas) of both buffers are zero for the whole launch
+    for (int it = t; it < 2 * 96 * 8; it += 128) {
+      const int buf = it / (96 * 8), rem = it - buf * (96 * 8);
+      *reinterpret_cast<uint4*>(ptile + buf * kVPBytes + (32 + (rem >> 3)) * 128 + ((rem & 7) << 4)) =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
 
     if (active) {
       ChunkWalk cw;
       cw.init(p, prefix, g0, g1);
       write_q(cw.b, cw.h);
-      float m_run = -INFINITY, l_run = 0.f;
+      float m_run = -INFINITY, l_run = 0.f;  // l_run: this thread's 16 keys of each chunk
       int lim = 0;
       bool ok = true;
       for (int j = 0; !cw.done(); ++j) {
@@ -1079,16 +1109,21 @@ __global__ void __launch_bounds__(kVThreads, 1)
           l_run = 0.f;
           lim = live ? cw.L - p.q_len + qi : -1;
         }
+        // After a failed wait a warp stays in the loop without waiting, touching tensor
+        // memory or storing results, so all four warps meet every named barrier.
         if (ok && *vabort) ok = false;
         if (ok) ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1);
-        if (!__all_sync(0xffffffffu, ok)) ok = false;
-        if (!ok) break;
-        tc_fence_after();
-        uint32_t sv[kVKeys];
-        tmem_ld32(lane_addr + (j & 1) * kVKeys, sv);
-        tmem_ld32(lane_addr + (j & 1) * kVKeys + 32, sv + 32);
-        tmem_ld_wait();
-        tc_fence_before();
+        ok = __all_sync(0xffffffffu, ok);
+        uint32_t sv[16];
+        if (ok) {
+          tc_fence_after();
+          tmem_ld16(lane_addr + (j & 1) * kVKeys + 16 * qd, sv);
+          tmem_ld_wait();
+          tc_fence_before();
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) sv[k] = 0u;
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[j & 1]);
         // the next piece's Q: every S of this piece has completed
@@ -1097,17 +1132,21 @@ __global__ void __launch_bounds__(kVThreads, 1)
           nx.advance(p, prefix, np);
           write_q(nx.b, nx.h);
         }
-        // masked scores in base 2; keys past the piece's pages, the sequence end or the
-        // causal limit of this row are -inf
+        // masked scores in base 2 (keys past the piece's pages, the sequence end or the
+        // row's causal limit are -inf), and the chunk maximum over the four key subsets
         const int key0 = static_cast<int>(cw.g - cw.seg_start) * kPage;
-        const int kmax = min(np * kPage - 1, lim - key0);
-        float mx = -INFINITY;
+        const int kmax = min(np * kPage - 1, lim - key0) - 16 * qd;
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int k = 0; k < kVKeys; ++k) {
+        for (int k = 0; k < 16; ++k) {
           const float x = k <= kmax ? __uint_as_float(sv[k]) * p.scale_log2 : -INFINITY;
           sv[k] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+          m4[k & 3] = fmaxf(m4[k & 3], x);
         }
+        rmax[(j & 1) * 128 + qd * 32 + i] = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        named_barrier_sync(1, 128);
+        const float* rm = rmax + (j & 1) * 128 + i;
+        const float mx = fmaxf(fmaxf(rm[0], rm[32]), fmaxf(rm[64], rm[96]));
         // lazy rescale: O and l keep the old reference unless the maximum grew by > 2^8
         bool need = false;
         float factor = 1.f;
@@ -1119,10 +1158,10 @@ __global__ void __launch_bounds__(kVThreads, 1)
           m_run = mx;
           l_run *= factor;
         }
-        if (j >= 1 && !first && __any_sync(0xffffffffu, need)) {
-          // O holds P(j-1) V(j-1) only once those MMAs are done
-          if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) ok = false;
-          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        // O (quarter 0) holds P(j-1) V(j-1) only once those MMAs are done
+        const bool rescale = qd == 0 && j >= 1 && !first && __any_sync(0xffffffffu, need);
+        if (ok && rescale) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1));
+        if (ok && rescale) {
           tc_fence_after();
 #pragma unroll 1
           for (int c0 = 0; c0 < kHeadDim; c0 += 32) {
@@ -1137,28 +1176,25 @@ __global__ void __launch_bounds__(kVThreads, 1)
         }
         const float mref = m_run == -INFINITY ? 0.f : m_run;
         // P(j) into its buffer once P(j-2) V(j-2) is done reading it
-        if (j >= 2) {
-          if (!mbar_wait(&o_done[j & 1], ((j - 2) >> 1) & 1)) ok = false;
-          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-        }
-        uint8_t* prow = ptile + (j & 1) * kVPBytes + m_lane * 128;
-        float lsum = 0.f;
+        if (ok && j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[j & 1], ((j - 2) >> 1) & 1));
+        uint8_t* prow = ptile + (j & 1) * kVPBytes + i * 128;
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < 2; ++c) {
           float e8[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             e8[e] = live ? ex2(__uint_as_float(sv[8 * c + e]) - mref) : 0.f;
-            lsum += e8[e];
+            l4[e & 3] += e8[e];
           }
           uint4 v;
           v.x = pack2<kBf16>(e8[0], e8[1]);
           v.y = pack2<kBf16>(e8[2], e8[3]);
           v.z = pack2<kBf16>(e8[4], e8[5]);
           v.w = pack2<kBf16>(e8[6], e8[7]);
-          *reinterpret_cast<uint4*>(prow + ((c ^ (m_lane & 7)) << 4)) = v;
+          *reinterpret_cast<uint4*>(prow + (((2 * qd + c) ^ (i & 7)) << 4)) = v;
         }
-        l_run += lsum;
+        l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
         // V rows past the sequence end hold stale pool bytes: zero them (P is 0 there,
         // but 0 * NaN would not be)
         const int tail = cw.L - key0;  // valid keys of this chunk
@@ -1177,65 +1213,65 @@ __global__ void __launch_bounds__(kVThreads, 1)
         if (lane == 0) mbar_arrive(&p_full[j & 1]);
 
         if (last) {
-          // ---- end of a segment piece: O after the piece's last P V
-          if (!mbar_wait(&o_done[j & 1], (j >> 1) & 1)) ok = false;
-          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-          tc_fence_after();
-          const bool whole_seg = (cw.g + np == cw.seg_end) && (cw.seg_start >= cw.g0);
-          const int seg_id = cw.b * Hkv + cw.h;
-          if (whole_seg) {
-            const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-            T* orow = optr + ((static_cast<int64_t>(cw.b) * p.q_len + qi) * p.num_q_heads + cw.h * p.group + gi) * kHeadDim;
+          // ---- end of a segment piece: l from the four key subsets; quarter 0 reads O
+          rsum[qd * 32 + i] = l_run;
+          named_barrier_sync(1, 128);
+          const float l_tot = (rsum[i] + rsum[32 + i]) + (rsum[64 + i] + rsum[96 + i]);
+          named_barrier_sync(1, 128);  // every warp has read before the next write
+          if (qd == 0) {
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[j & 1], (j >> 1) & 1));
+            if (ok) {
+              tc_fence_after();
+              const bool whole_seg = (cw.g + np == cw.seg_end) && (cw.seg_start >= cw.g0);
+              const int seg_id = cw.b * Hkv + cw.h;
+              const int64_t slot = static_cast<int64_t>(u) + seg_id;
+              float* po = p.part_o + slot * kHeadDim * nqp;
+              const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+              const int64_t row0 =
+                  ((static_cast<int64_t>(cw.b) * p.q_len + qi) * p.num_q_heads + cw.h * p.group + gi) * kHeadDim;
 #pragma unroll 1
-            for (int c0 = 0; c0 < kHeadDim; c0 += 32) {
-              uint32_t ov[32];
-              tmem_ld32(lane_addr + 128 + c0, ov);
-              tmem_ld_wait();
-              if (live) {
+              for (int c0 = 0; c0 < kHeadDim; c0 += 32) {
+                uint32_t ov[32];
+                tmem_ld32(lane_addr + 128 + c0, ov);
+                tmem_ld_wait();
+                if (whole_seg) {
+                  if (live) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                  uint4 v;
-                  v.x = pack2<kBf16>(__uint_as_float(ov[8 * c + 0]) * inv, __uint_as_float(ov[8 * c + 1]) * inv);
-                  v.y = pack2<kBf16>(__uint_as_float(ov[8 * c + 2]) * inv, __uint_as_float(ov[8 * c + 3]) * inv);
-                  v.z = pack2<kBf16>(__uint_as_float(ov[8 * c + 4]) * inv, __uint_as_float(ov[8 * c + 5]) * inv);
-                  v.w = pack2<kBf16>(__uint_as_float(ov[8 * c + 6]) * inv, __uint_as_float(ov[8 * c + 7]) * inv);
-                  reinterpret_cast<uint4*>(orow + c0)[c] = v;
-                  for (int i2 = 0; i2 < p.num_peers; ++i2)  // the gather slots
-                    reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[i2]) + p.peer_offset +
-                                             (orow - optr) + c0)[c] = v;
+                    for (int c = 0; c < 4; ++c) {
+                      uint4 v;
+                      v.x = pack2<kBf16>(__uint_as_float(ov[8 * c + 0]) * inv, __uint_as_float(ov[8 * c + 1]) * inv);
+                      v.y = pack2<kBf16>(__uint_as_float(ov[8 * c + 2]) * inv, __uint_as_float(ov[8 * c + 3]) * inv);
+                      v.z = pack2<kBf16>(__uint_as_float(ov[8 * c + 4]) * inv, __uint_as_float(ov[8 * c + 5]) * inv);
+                      v.w = pack2<kBf16>(__uint_as_float(ov[8 * c + 6]) * inv, __uint_as_float(ov[8 * c + 7]) * inv);
+                      reinterpret_cast<uint4*>(optr + row0 + c0)[c] = v;
+                      for (int i2 = 0; i2 < p.num_peers; ++i2)  // the gather slots
+                        reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[i2]) + p.peer_offset + row0 + c0)[c] = v;
+                    }
+                  }
+                } else if (i < nqp) {
+                  // partial: unnormalised O in the merge kernel's layout, slot = unit +
+                  // segment id; rows nq .. nqp-1 are padding with O = 0
+#pragma unroll
+                  for (int e = 0; e < 32; ++e) po[(c0 + e) * nqp + i] = live ? __uint_as_float(ov[e]) : 0.f;
                 }
               }
-            }
-          } else {
-            // partial: unnormalised O and (m, l) in the merge kernel's layout, slot = unit +
-            // segment id; rows nq .. nqp-1 are padding with (m, l) = (-inf, 0) and O = 0
-            const int64_t slot = static_cast<int64_t>(u) + seg_id;
-            float* po = p.part_o + slot * kHeadDim * nqp;
-#pragma unroll 1
-            for (int c0 = 0; c0 < kHeadDim; c0 += 32) {
-              uint32_t ov[32];
-              tmem_ld32(lane_addr + 128 + c0, ov);
-              tmem_ld_wait();
-              if (r < nqp) {
-#pragma unroll
-                for (int e = 0; e < 32; ++e) po[(c0 + e) * nqp + r] = live ? __uint_as_float(ov[e]) : 0.f;
+              if (!whole_seg) {
+                if (i < nqp)
+                  *reinterpret_cast<float2*>(p.part_ml + (slot * nqp + i) * 2) =
+                      live ? make_float2(m_run, l_tot) : make_float2(-INFINITY, 0.f);
+                if (lane == 0) {
+                  const int u_first = unit_of(cw.seg_start, T_pages, U), u_last = unit_of(cw.seg_end - 1, T_pages, U);
+                  p.counters[seg_id] = ((u_last - u_first + 1) << 20) | u_first;
+                }
               }
-            }
-            if (r < nqp)
-              *reinterpret_cast<float2*>(p.part_ml + (slot * nqp + r) * 2) =
-                  live ? make_float2(m_run, l_run) : make_float2(-INFINITY, 0.f);
-            if (t == 0) {
-              const int64_t ss = cw.seg_start, se = cw.seg_end;
-              const int u_first = unit_of(ss, T_pages, U), u_last = unit_of(se - 1, T_pages, U);
-              p.counters[seg_id] = ((u_last - u_first + 1) << 20) | u_first;
+              tc_fence_before();
             }
           }
-          tc_fence_before();
         }
         cw.advance(p, prefix, np);
       }
       if (!ok) {
-        if (t == 0) report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
+        if (lane == 0) report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
         *vabort = 1;
       }
     }
@@ -1247,10 +1283,10 @@ __global__ void __launch_bounds__(kVThreads, 1)
         const int64_t n16 = static_cast<int64_t>(p.q_len) * p.num_q_heads * kHeadDim * sizeof(T) / 16;
         const int64_t base = static_cast<int64_t>(b) * p.q_len * p.num_q_heads * kHeadDim;
         uint4* dst = reinterpret_cast<uint4*>(optr + base);
-        for (int64_t i = t; i < n16; i += 128) dst[i] = make_uint4(0, 0, 0, 0);
-        for (int i2 = 0; i2 < p.num_peers; ++i2) {
-          uint4* pd = reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[i2]) + p.peer_offset + base);
-          for (int64_t i = t; i < n16; i += 128) pd[i] = make_uint4(0, 0, 0, 0);
+        for (int64_t i2 = t; i2 < n16; i2 += 128) dst[i2] = make_uint4(0, 0, 0, 0);
+        for (int k = 0; k < p.num_peers; ++k) {
+          uint4* pd = reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[k]) + p.peer_offset + base);
+          for (int64_t i2 = t; i2 < n16; i2 += 128) pd[i2] = make_uint4(0, 0, 0, 0);
         }
       }
     }
