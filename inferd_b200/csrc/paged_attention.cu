@@ -55,13 +55,6 @@ constexpr float kLog2e = 1.4426950408889634f;
 #define INFERD_STAGES_PER_WARP 3  // pages in flight per warp (3 x 8 KiB)
 #endif
 constexpr int kStagesPerWarp = INFERD_STAGES_PER_WARP;
-#ifndef INFERD_NT3_CTAS
-#define INFERD_NT3_CTAS 2
-#endif
-// CTAs per SM and pages in flight per warp for NT n-tiles: three CTAs of 4 warps need
-// <= 170 registers a thread and 2-page rings (3 x 4 x 2 x 8 KiB of shared memory).
-constexpr int ctas_per_sm(int nt) { return nt == 3 ? INFERD_NT3_CTAS : kCtasPerSm; }
-constexpr int stages_for(int nt) { return ctas_per_sm(nt) >= 3 ? 2 : kStagesPerWarp; }
 
 // query rows per (sequence, kv head), rounded up to whole 8-column MMA tiles
 __host__ __device__ constexpr int nq_pad(int nq) { return ((nq + 7) / 8) * 8; }
@@ -202,7 +195,7 @@ __device__ __forceinline__ void load_q_frags(uint32_t (&qf)[8][NT][2], const T* 
 }
 
 template <bool kBf16, int NT, int STAGES>
-__global__ void __launch_bounds__(kWarps * 32, ctas_per_sm(NT))
+__global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
     paged_attn_tc_kernel(const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap, const FastParams p) {
   using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
@@ -777,540 +770,6 @@ __global__ void __launch_bounds__(kHeadDim) merge_cut_segments_kernel(const Fast
   if (d == 0) p.counters[seg_id] = 0;
 }
 
-// ------------------------------------------------------------------ tensor-memory path
-// Windows of several query rows per kv head (speculative verify: q_len x group rows, 9 to
-// 32 of them).  One persistent CTA per SM streams the balanced page range of its unit
-// (CTA) in chunks of up to four pages of one segment:
-//   warp 0      issues the TMA loads of a chunk (K and V, 128-byte swizzle; 16 boxes, one
-//               per lane) into a 4-stage ring; each stage holds K lo | K hi | V lo | V hi,
-//               64 rows x 128 B each, so the chunk's keys form one K-major (and one
-//               MN-major) operand;
-//   warp 1      lane 0 issues tcgen05.mma: S = Q K^T (M = 128, N = 64 keys, K = 128, into
-//               one of two 64-column tensor-memory buffers) and O += P V (M = 128, N = 128,
-//               one K = 16 step per page, V as an MN-major operand) into 128 columns that
-//               hold O for the whole segment piece, each as soon as its inputs are ready;
-//   warps 2-5   softmax.  Query row i (i < nq) sits in all four tensor-memory lane
-//               quarters (MMA rows 32 q + i, Q replicated); the warp of quarter q reads
-//               keys [16 q, 16 q + 16) of the chunk, the four agree on the chunk maximum
-//               through shared memory, and each writes its 16 probabilities (16-bit) into
-//               row i of the P tile, whose rows 32 .. 127 stay zero.  So one P V MMA
-//               accumulates row i's whole O in quarter 0.  Online softmax in base 2 with a
-//               lazy rescale (O and l are rescaled only when the running maximum grows by
-//               more than 2^8).  At the end of a segment piece quarter 0 reads O,
-//               normalises and stores (or leaves a partial for merge_cut_segments_kernel).
-// The Q tile of the next segment is written as soon as the last S of the current one has
-// been read.
-constexpr int kVPages = 4;                       // pages per chunk
-constexpr int kVKeys = kVPages * kPage;          // 64 keys: N of S, K of P V
-constexpr int kVStages = 4;
-constexpr int kVRegion = kVPages * kHalfBytes;   // 8 KiB: 64 rows x 128 B
-constexpr int kVStageBytes = 4 * kVRegion;       // K lo | K hi | V lo | V hi
-constexpr int kVQBytes = 2 * 128 * 128;          // Q tile, 128 rows x 256 B (lo | hi halves)
-constexpr int kVPBytes = 128 * 128;              // P tile, 128 rows x 64 keys x 2 B
-constexpr int kVThreads = 192;                 // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
-constexpr int kVTmemCols = 256;                  // S0 [0, 64) | S1 [64, 128) | O [128, 256)
-constexpr float kVRescale = 8.f;                 // lazy rescale threshold (log2 units)
-constexpr int kVBarOffset = kVStages * kVStageBytes + kVQBytes + 2 * kVPBytes;
-constexpr int kVPrefixOffset = kVBarOffset + 512;
-
-// Instruction descriptor, kind::f16: A and B 16-bit (bf16 or f16), D f32, A K-major, B
-// K-major or MN-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t f16_idesc(bool bf16, bool b_mn_major, int n) {
-  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
-         ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(128 >> 4) << 24);
-}
-
-// The unit's page range [g0, g1) walked in chunks: at most kVPages pages, never across a
-// segment or past the range.  Every role walks the same sequence.
-struct ChunkWalk {
-  int64_t g, g0, g1, seg_start, seg_end;
-  int b, h, pb, L;
-  __device__ void init(const FastParams& p, const int* prefix, int64_t a, int64_t e) {
-    g0 = g = a;
-    g1 = e;
-    const int Hkv = p.num_kv_heads;
-    b = find_seq(prefix, p.num_seqs, a / Hkv);
-    pb = prefix[b + 1] - prefix[b];
-    seg_start = static_cast<int64_t>(Hkv) * prefix[b];
-    h = static_cast<int>((a - seg_start) / pb);
-    seg_start += static_cast<int64_t>(h) * pb;
-    seg_end = seg_start + pb;
-    L = seq_len_of(p, b, false);
-  }
-  __device__ bool done() const { return g >= g1; }
-  __device__ int pages() const { return static_cast<int>(min64(kVPages, min64(seg_end, g1) - g)); }
-  __device__ bool first() const { return g == g0 || g == seg_start; }
-  __device__ bool last(int np) const { return g + np == seg_end || g + np == g1; }
-  __device__ void advance(const FastParams& p, const int* prefix, int np) {
-    g += np;
-    if (g == seg_end && g < g1) {
-      if (++h == p.num_kv_heads) {
-        h = 0;
-        do { ++b; } while (prefix[b + 1] == prefix[b]);
-        L = seq_len_of(p, b, false);
-      }
-      pb = prefix[b + 1] - prefix[b];
-      seg_start = g;
-      seg_end = g + pb;
-    }
-  }
-};
-
-template <bool kBf16>
-__global__ void __launch_bounds__(kVThreads, 1)
-    paged_verify_tmem_kernel(const __grid_constant__ CUtensorMap kmap,
-                             const __grid_constant__ CUtensorMap vmap, const FastParams p) {
-  using T = typename std::conditional<kBf16, __nv_bfloat16, __half>::type;
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ int warp_tot[kVThreads / 32];
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
-  __shared__ float rmax[2 * 128];  // [chunk parity][key subset][row] chunk maxima
-  __shared__ float rsum[128];      // [key subset][row] l at the end of a piece
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* ring = smem;
-  uint8_t* qtile = smem + kVStages * kVStageBytes;
-  uint8_t* ptile = qtile + kVQBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kVBarOffset);
-  uint64_t* full = bars;        // [4] TMA bytes of a stage landed
-  uint64_t* empty = bars + 4;   // [4] the P V MMAs of a stage are done
-  uint64_t* s_full = bars + 8;  // [2] S of a chunk is in tensor memory
-  uint64_t* s_free = bars + 10; // [2] the softmax threads have read it
-  uint64_t* p_full = bars + 12; // [2] P written (and O rescaled)
-  uint64_t* o_done = bars + 14; // [2] the P V MMAs of a chunk are done
-  uint64_t* q_full = bars + 16; // Q tile of the next segment piece written
-  uint64_t* m_done = bars + 17; // every MMA of the CTA is done
-  int* prefix = reinterpret_cast<int*>(smem + kVPrefixOffset);
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int B = p.num_seqs, Hkv = p.num_kv_heads;
-
-  if (tid == 0) {
-    for (int s = 0; s < kVStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);  // one arrival per softmax warp
-      mbar_init(&p_full[i], 4);
-      mbar_init(&o_done[i], 1);
-    }
-    mbar_init(q_full, 4);
-    mbar_init(m_done, 1);
-    fence_mbar_init();
-    abort_flag = 0;
-  }
-  if (warp == 1) {
-    tmem_alloc1(&tmem_slot, kVTmemCols);
-    tmem_relinquish1();
-  }
-  page_prefix<kVThreads>(p, prefix, warp_tot);  // ends with __syncthreads
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-
-  const int64_t T_pages = static_cast<int64_t>(Hkv) * prefix[B];
-  const int U = static_cast<int>(min64(gridDim.x, max64(T_pages, 1)));
-  const int u = blockIdx.x;
-  const bool active = u < U && T_pages > 0;
-  const int64_t g0 = static_cast<int64_t>(u) * T_pages / U;
-  const int64_t g1 = static_cast<int64_t>(u + 1) * T_pages / U;
-  volatile int* vabort = &abort_flag;
-  int fills = 0;  // chunks whose loads the producer issued (warp 0)
-
-  if (warp == 0) {
-    // ---------------- producer
-    if (active) {
-      if (lane == 0) {
-        prefetch_tensormap(&kmap);
-        prefetch_tensormap(&vmap);
-      }
-      const uint64_t policy = l2_policy_evict_first();
-      // pool row (block * Hkv + head) * 16 of global page g
-      auto row_of = [&](int64_t g) -> int32_t {
-        const int b = find_seq(prefix, B, g / Hkv);
-        const int pb = prefix[b + 1] - prefix[b];
-        const int64_t off = g - static_cast<int64_t>(Hkv) * prefix[b];
-        const int h = static_cast<int>(off / pb);
-        int64_t blk = block_id(p, b, static_cast<int>(off - static_cast<int64_t>(h) * pb));
-        if (blk < 0 || blk >= p.num_blocks) {
-          report_error(p.error_word, INFERD_ERR_DEVICE_INDEX);
-          blk = 0;
-        }
-        return static_cast<int32_t>((blk * Hkv + h) * kPage);
-      };
-      // rows of the unit's pages 32 at a time: lane l of rows_cur holds page batch0 + l, and
-      // rows_next the batch after, loaded one batch ahead of its use
-      int64_t batch0 = g0;
-      int32_t rows_cur = g0 + lane < g1 ? row_of(g0 + lane) : 0;
-      int32_t rows_next = g0 + 32 + lane < g1 ? row_of(g0 + 32 + lane) : 0;
-      ChunkWalk cw;
-      cw.init(p, prefix, g0, g1);
-      for (int i = 0; !cw.done(); ++i) {
-        const int np = cw.pages();
-        const int s = i % kVStages, round = i / kVStages;
-        bool ok = *vabort == 0;
-        if (ok && round > 0 && lane == 0) ok = mbar_wait(&empty[s], (round - 1) & 1);
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-        if (!ok) {
-          if (lane == 0) { report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT); *vabort = 1; }
-          break;
-        }
-        uint8_t* st = ring + s * kVStageBytes;
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(np) * kStageBytes);
-        __syncwarp();
-        {
-          // lane 4q + t issues box t (K lo, K hi, V lo, V hi) of page q of the chunk; the
-          // chunk starts inside the current batch and ends at most 3 pages past it
-          const int q = lane >> 2, box = lane & 3;
-          const int idx = static_cast<int>(cw.g - batch0) + q;
-          const int32_t rc = __shfl_sync(0xffffffffu, rows_cur, idx & 31);
-          const int32_t rn = __shfl_sync(0xffffffffu, rows_next, idx & 31);
-          const int32_t r = idx < 32 ? rc : rn;
-          if (q < np)
-            tma_load_2d(st + box * kVRegion + q * kHalfBytes, box < 2 ? &kmap : &vmap, (box & 1) * 64, r,
-                        &full[s], policy);
-          if (cw.g + np >= batch0 + 32) {  // rotate the batches (warp-uniform)
-            batch0 += 32;
-            rows_cur = rows_next;
-            rows_next = batch0 + 32 + lane < g1 ? row_of(batch0 + 32 + lane) : 0;
-          }
-        }
-        ++fills;
-        cw.advance(p, prefix, np);
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer (one thread): S(i) = Q K^T as soon as chunk i's K has
-    // landed and S buffer i % 2 is free; O += P(j) V(j) as soon as P(j) is written.  Both
-    // are polled without blocking, so a P V never waits for a later chunk's data.
-    if (active && lane == 0) {
-      const uint32_t idesc_s = f16_idesc(kBf16, false, kVKeys);
-      const uint32_t idesc_o = f16_idesc(kBf16, true, kHeadDim);
-      const uint32_t q_base = smem_u32(qtile), p_base = smem_u32(ptile), r_base = smem_u32(ring);
-      ChunkWalk ws, wp;  // the next S chunk, the next P V chunk
-      ws.init(p, prefix, g0, g1);
-      wp.init(p, prefix, g0, g1);
-      int ns = 0, npv = 0, piece = 0;
-      bool ok = true;
-      uint64_t t_last = globaltimer();
-      uint32_t spins = 0;
-      while (ok) {
-        bool did = false;
-        if (npv < ns && mbar_test_wait(&p_full[npv & 1], (npv >> 1) & 1)) {
-          tc_fence_after();
-          const int np = wp.pages();
-          const bool first = wp.first();
-          const uint32_t pa = p_base + (npv & 1) * kVPBytes;
-          const uint32_t va = r_base + (npv % kVStages) * kVStageBytes + 2 * kVRegion;
-          for (int q = 0; q < np; ++q)
-            mma_f16_1(tmem + 128, sw128_desc(pa + q * 32), sw128_mn_desc(va + q * kHalfBytes, kVRegion, 1024),
-                      idesc_o, (first && q == 0) ? 0u : 1u);
-          mma_commit1(&o_done[npv & 1]);
-          mma_commit1(&empty[npv % kVStages]);
-          wp.advance(p, prefix, np);
-          ++npv;
-          did = true;
-        }
-        if (!ws.done()) {
-          const bool first = ws.first();
-          if ((!first || mbar_test_wait(q_full, piece & 1)) &&
-              mbar_test_wait(&full[ns % kVStages], (ns / kVStages) & 1) &&
-              (ns < 2 || mbar_test_wait(&s_free[ns & 1], ((ns >> 1) - 1) & 1))) {
-            tc_fence_after();
-            const uint32_t ka = r_base + (ns % kVStages) * kVStageBytes;
-            const uint32_t sc = tmem + (ns & 1) * kVKeys;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              mma_f16_1(sc, sw128_desc(q_base + (kk >> 2) * (kVQBytes / 2) + (kk & 3) * 32),
-                        sw128_desc(ka + (kk >> 2) * kVRegion + (kk & 3) * 32), idesc_s, kk > 0 ? 1u : 0u);
-            mma_commit1(&s_full[ns & 1]);
-            if (first) ++piece;
-            ws.advance(p, prefix, ws.pages());
-            ++ns;
-            did = true;
-          }
-        } else if (npv == ns) {
-          break;  // every S and every P V issued
-        }
-        if (did) {
-          t_last = globaltimer();
-          spins = 0;
-        } else {
-          // back off: this warp shares its scheduler with a softmax warp
-          __nanosleep(64);
-          if ((++spins & 63u) == 0u && (*vabort || globaltimer() - t_last > kWaitTimeoutNs)) ok = false;
-        }
-      }
-      if (!ok) {
-        report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
-        *vabort = 1;
-      }
-      // every MMA issued by this thread is complete before tensor memory is released
-      mma_commit1(m_done);
-      mbar_wait(m_done, 0);
-    }
-  } else {
-    // ---------------- softmax / epilogue.  Query row i (< nq <= 32) is replicated in the
-    // four tensor-memory lane quarters (MMA rows 32 q + i); the warp of quarter q reads keys
-    // [16 q, 16 q + 16) of each chunk from its replica and writes their p into the P row of
-    // replica 0, whose other replicas' P rows stay zero.  So P V accumulates the whole O of
-    // row i in quarter 0, and the softmax work of a row is spread over four threads.
-    const int t = tid - 64;                  // 0..127
-    const int qd = warp & 3;                 // lane quarter = key subset of this warp
-    const int i = lane;                      // query row of this thread
-    const bool live = i < p.nq;
-    const int qi = live ? i / p.group : 0, gi = live ? i - qi * p.group : 0;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * qd) << 16);
-    const T* qptr = static_cast<const T*>(p.query);
-    T* optr = static_cast<T*>(p.out);
-    const int nqp = nq_pad(p.nq);            // column count of the partial layout
-
-    // Q rows of segment (b, h) into rows 32 q + i of the Q tile (K-major, 128-byte swizzle,
-    // lo | hi halves), all four replicas
-    auto write_q = [&](int b, int h) {
-      for (int it = t; it < p.nq * 16; it += 128) {
-        const int rr = it >> 4, c = it & 15;
-        const int q2 = rr / p.group, g2 = rr - q2 * p.group;
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(
-            qptr + ((static_cast<int64_t>(b) * p.q_len + q2) * p.num_q_heads + h * p.group + g2) * kHeadDim) + c);
-#pragma unroll
-        for (int rep = 0; rep < 4; ++rep) {
-          const int ml = 32 * rep + rr;
-          *reinterpret_cast<uint4*>(qtile + (c >> 3) * (kVQBytes / 2) + ml * 128 + (((c & 7) ^ (ml & 7)) << 4)) = v;
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(q_full);
-    };
-    // P rows 32 .. 127 (the replicas) of both buffers are zero for the whole launch
-    for (int it = t; it < 2 * 96 * 8; it += 128) {
-      const int buf = it / (96 * 8), rem = it - buf * (96 * 8);
-      *reinterpret_cast<uint4*>(ptile + buf * kVPBytes + (32 + (rem >> 3)) * 128 + ((rem & 7) << 4)) =
-          make_uint4(0u, 0u, 0u, 0u);
-    }
-    fence_proxy_async_smem();
-
-    if (active) {
-      ChunkWalk cw;
-      cw.init(p, prefix, g0, g1);
-      write_q(cw.b, cw.h);
-      float m_run = -INFINITY, l_run = 0.f;  // l_run: this thread's 16 keys of each chunk
-      int lim = 0;
-      bool ok = true;
-      for (int j = 0; !cw.done(); ++j) {
-        const int np = cw.pages();
-        const bool first = cw.first(), last = cw.last(np);
-        if (first) {
-          m_run = -INFINITY;
-          l_run = 0.f;
-          lim = live ? cw.L - p.q_len + qi : -1;
-        }
-        // After a failed wait a warp stays in the loop without waiting, touching tensor
-        // memory or storing results, so all four warps meet every named barrier.
-        if (ok && *vabort) ok = false;
-        if (ok) ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1);
-        ok = __all_sync(0xffffffffu, ok);
-        uint32_t sv[16];
-        if (ok) {
-          tc_fence_after();
-          tmem_ld16(lane_addr + (j & 1) * kVKeys + 16 * qd, sv);
-          tmem_ld_wait();
-          tc_fence_before();
-        } else {
-#pragma unroll
-          for (int k = 0; k < 16; ++k) sv[k] = 0u;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[j & 1]);
-        // the next piece's Q: every S of this piece has completed
-        if (last && cw.g + np < cw.g1) {
-          ChunkWalk nx = cw;
-          nx.advance(p, prefix, np);
-          write_q(nx.b, nx.h);
-        }
-        // masked scores in base 2 (keys past the piece's pages, the sequence end or the
-        // row's causal limit are -inf), and the chunk maximum over the four key subsets
-        const int key0 = static_cast<int>(cw.g - cw.seg_start) * kPage;
-        const int kmax = min(np * kPage - 1, lim - key0) - 16 * qd;
-        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float x = k <= kmax ? __uint_as_float(sv[k]) * p.scale_log2 : -INFINITY;
-          sv[k] = __float_as_uint(x);
-          m4[k & 3] = fmaxf(m4[k & 3], x);
-        }
-        rmax[(j & 1) * 128 + qd * 32 + i] = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-        named_barrier_sync(1, 128);
-        const float* rm = rmax + (j & 1) * 128 + i;
-        const float mx = fmaxf(fmaxf(rm[0], rm[32]), fmaxf(rm[64], rm[96]));
-        // lazy rescale: O and l keep the old reference unless the maximum grew by > 2^8
-        bool need = false;
-        float factor = 1.f;
-        if (first) {
-          m_run = mx;
-        } else if (mx > m_run + kVRescale) {
-          factor = ex2(m_run - mx);
-          need = true;
-          m_run = mx;
-          l_run *= factor;
-        }
-        // O (quarter 0) holds P(j-1) V(j-1) only once those MMAs are done
-        const bool rescale = qd == 0 && j >= 1 && !first && __any_sync(0xffffffffu, need);
-        if (ok && rescale) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1));
-        if (ok && rescale) {
-          tc_fence_after();
-#pragma unroll 1
-          for (int c0 = 0; c0 < kHeadDim; c0 += 32) {
-            uint32_t ov[32];
-            tmem_ld32(lane_addr + 128 + c0, ov);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * factor);
-            tmem_st32(lane_addr + 128 + c0, ov);
-          }
-          tmem_st_wait();
-        }
-        const float mref = m_run == -INFINITY ? 0.f : m_run;
-        // P(j) into its buffer once P(j-2) V(j-2) is done reading it
-        if (ok && j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[j & 1], ((j - 2) >> 1) & 1));
-        uint8_t* prow = ptile + (j & 1) * kVPBytes + i * 128;
-        float l4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float e8[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            e8[e] = live ? ex2(__uint_as_float(sv[8 * c + e]) - mref) : 0.f;
-            l4[e & 3] += e8[e];
-          }
-          uint4 v;
-          v.x = pack2<kBf16>(e8[0], e8[1]);
-          v.y = pack2<kBf16>(e8[2], e8[3]);
-          v.z = pack2<kBf16>(e8[4], e8[5]);
-          v.w = pack2<kBf16>(e8[6], e8[7]);
-          *reinterpret_cast<uint4*>(prow + (((2 * qd + c) ^ (i & 7)) << 4)) = v;
-        }
-        l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
-        // V rows past the sequence end hold stale pool bytes: zero them (P is 0 there,
-        // but 0 * NaN would not be)
-        const int tail = cw.L - key0;  // valid keys of this chunk
-        if (tail < np * kPage) {
-          uint8_t* vb = ring + (j % kVStages) * kVStageBytes + 2 * kVRegion;
-          const int zr = np * kPage - tail;  // rows tail .. np*16-1, all in the last page
-          for (int it = t; it < zr * 16; it += 128) {
-            const int rowi = tail + (it >> 4), c = it & 15;
-            *reinterpret_cast<uint4*>(vb + (c >> 3) * kVRegion + rowi * 128 + ((c & 7) << 4)) =
-                make_uint4(0u, 0u, 0u, 0u);
-          }
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[j & 1]);
-
-        if (last) {
-          // ---- end of a segment piece: l from the four key subsets; quarter 0 reads O
-          rsum[qd * 32 + i] = l_run;
-          named_barrier_sync(1, 128);
-          const float l_tot = (rsum[i] + rsum[32 + i]) + (rsum[64 + i] + rsum[96 + i]);
-          named_barrier_sync(1, 128);  // every warp has read before the next write
-          if (qd == 0) {
-            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[j & 1], (j >> 1) & 1));
-            if (ok) {
-              tc_fence_after();
-              const bool whole_seg = (cw.g + np == cw.seg_end) && (cw.seg_start >= cw.g0);
-              const int seg_id = cw.b * Hkv + cw.h;
-              const int64_t slot = static_cast<int64_t>(u) + seg_id;
-              float* po = p.part_o + slot * kHeadDim * nqp;
-              const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
-              const int64_t row0 =
-                  ((static_cast<int64_t>(cw.b) * p.q_len + qi) * p.num_q_heads + cw.h * p.group + gi) * kHeadDim;
-#pragma unroll 1
-              for (int c0 = 0; c0 < kHeadDim; c0 += 32) {
-                uint32_t ov[32];
-                tmem_ld32(lane_addr + 128 + c0, ov);
-                tmem_ld_wait();
-                if (whole_seg) {
-                  if (live) {
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                      uint4 v;
-                      v.x = pack2<kBf16>(__uint_as_float(ov[8 * c + 0]) * inv, __uint_as_float(ov[8 * c + 1]) * inv);
-                      v.y = pack2<kBf16>(__uint_as_float(ov[8 * c + 2]) * inv, __uint_as_float(ov[8 * c + 3]) * inv);
-                      v.z = pack2<kBf16>(__uint_as_float(ov[8 * c + 4]) * inv, __uint_as_float(ov[8 * c + 5]) * inv);
-                      v.w = pack2<kBf16>(__uint_as_float(ov[8 * c + 6]) * inv, __uint_as_float(ov[8 * c + 7]) * inv);
-                      reinterpret_cast<uint4*>(optr + row0 + c0)[c] = v;
-                      for (int i2 = 0; i2 < p.num_peers; ++i2)  // the gather slots
-                        reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[i2]) + p.peer_offset + row0 + c0)[c] = v;
-                    }
-                  }
-                } else if (i < nqp) {
-                  // partial: unnormalised O in the merge kernel's layout, slot = unit +
-                  // segment id; rows nq .. nqp-1 are padding with O = 0
-#pragma unroll
-                  for (int e = 0; e < 32; ++e) po[(c0 + e) * nqp + i] = live ? __uint_as_float(ov[e]) : 0.f;
-                }
-              }
-              if (!whole_seg) {
-                if (i < nqp)
-                  *reinterpret_cast<float2*>(p.part_ml + (slot * nqp + i) * 2) =
-                      live ? make_float2(m_run, l_tot) : make_float2(-INFINITY, 0.f);
-                if (lane == 0) {
-                  const int u_first = unit_of(cw.seg_start, T_pages, U), u_last = unit_of(cw.seg_end - 1, T_pages, U);
-                  p.counters[seg_id] = ((u_last - u_first + 1) << 20) | u_first;
-                }
-              }
-              tc_fence_before();
-            }
-          }
-        }
-        cw.advance(p, prefix, np);
-      }
-      if (!ok) {
-        if (lane == 0) report_error(p.error_word, INFERD_ERR_DEVICE_TIMEOUT);
-        *vabort = 1;
-      }
-    }
-    // sequences without keys: zero output rows
-    if (u < U || T_pages == 0) {
-      const int U0 = T_pages == 0 ? static_cast<int>(gridDim.x) : U;
-      for (int b = u; b < B; b += U0) {
-        if (prefix[b + 1] != prefix[b]) continue;
-        const int64_t n16 = static_cast<int64_t>(p.q_len) * p.num_q_heads * kHeadDim * sizeof(T) / 16;
-        const int64_t base = static_cast<int64_t>(b) * p.q_len * p.num_q_heads * kHeadDim;
-        uint4* dst = reinterpret_cast<uint4*>(optr + base);
-        for (int64_t i2 = t; i2 < n16; i2 += 128) dst[i2] = make_uint4(0, 0, 0, 0);
-        for (int k = 0; k < p.num_peers; ++k) {
-          uint4* pd = reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[k]) + p.peer_offset + base);
-          for (int64_t i2 = t; i2 < n16; i2 += 128) pd[i2] = make_uint4(0, 0, 0, 0);
-        }
-      }
-    }
-  }
-
-  // ---- teardown: no TMA write may still be in flight into this CTA's ring, and every
-  // tensor-memory access is complete before the columns are released
-  tc_fence_before();
-  __syncthreads();
-  grid_launch_dependents();
-  if (warp == 0 && lane == 0) {
-    // drain (after an abort the MMA warp may not have consumed every stage): wait, bounded,
-    // for the last phase of every stage the producer filled
-    for (int s = 0; s < kVStages && s < fills; ++s) {
-      const int rounds = (fills - s + kVStages - 1) / kVStages;
-      mbar_wait(&full[s], static_cast<uint32_t>((rounds - 1) & 1));
-    }
-  }
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc1(tmem, kVTmemCols);
-  }
-}
-
 // ------------------------------------------------------------------ generic path
 struct GenericParams {
   void* out;
@@ -1471,10 +930,10 @@ inline WorkspaceLayout workspace_layout(int num_seqs, int num_kv_heads, int nqp,
   return w;
 }
 
-inline int fast_grid(int sm_count, int nqp) { return sm_count * ctas_per_sm(nqp / 8); }
+inline int fast_grid(int sm_count) { return sm_count * kCtasPerSm; }
 
-inline size_t fast_smem_bytes(int num_seqs, int nqp) {
-  return 1024 + static_cast<size_t>(kWarps) * stages_for(nqp / 8) * (kStageBytes + 8) +
+inline size_t fast_smem_bytes(int num_seqs) {
+  return 1024 + static_cast<size_t>(kWarps) * kStagesPerWarp * (kStageBytes + 8) +
          (static_cast<size_t>(num_seqs) + 1) * 4;
 }
 
@@ -1525,7 +984,7 @@ int pool_map(const void* pool, int64_t rows, CUtensorMap* out) {
   return INFERD_OK;
 }
 
-template <bool kBf16, int NT, int STAGES = stages_for(NT)>
+template <bool kBf16, int NT, int STAGES = kStagesPerWarp>
 int launch_fast_t(const CUtensorMap& km, const CUtensorMap& vm, const FastParams& fp, int grid,
                   size_t smem, cudaStream_t s) {
   static bool configured[64] = {false};
@@ -1553,30 +1012,6 @@ int launch_fast(const CUtensorMap& km, const CUtensorMap& vm, const FastParams& 
     case 3: return launch_fast_t<kBf16, 3>(km, vm, fp, grid, smem, s);
     default: return launch_fast_t<kBf16, 4>(km, vm, fp, grid, smem, s);
   }
-}
-
-#ifndef INFERD_VERIFY_TMEM
-#define INFERD_VERIFY_TMEM 0
-#endif
-
-inline size_t verify_smem_bytes(int num_seqs) {
-  return 1024 + kVPrefixOffset + (static_cast<size_t>(num_seqs) + 1) * 4;
-}
-
-template <bool kBf16>
-int launch_verify_tmem(const CUtensorMap& km, const CUtensorMap& vm, const FastParams& fp, int grid,
-                       size_t smem, cudaStream_t s) {
-  static bool configured[64] = {false};
-  const int dev = current_device();
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(paged_verify_tmem_kernel<kBf16>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(verify_smem_bytes(kMaxSeqsFast)));
-    if (e != cudaSuccess) return cuda_status(e);
-    configured[dev] = true;
-  }
-  paged_verify_tmem_kernel<kBf16><<<grid, kVThreads, smem, s>>>(km, vm, fp);
-  return launch_status();
 }
 
 template <bool kBf16, int NQP>
@@ -1643,7 +1078,7 @@ extern "C" size_t inferd_paged_attention_workspace_bytes(int32_t num_seqs, int32
   const int group = num_q_heads / (num_kv_heads > 0 ? num_kv_heads : 1);
   const int nqp = nq_pad(q_len * (group > 0 ? group : 1));
   const int chunk = num_seqs < kMaxSeqsFast ? num_seqs : kMaxSeqsFast;
-  return workspace_layout(chunk, num_kv_heads, nqp, fast_grid(sms, nqp)).total;
+  return workspace_layout(chunk, num_kv_heads, nqp, fast_grid(sms)).total;
 }
 
 static int paged_attention_impl(void* out, const void* query, const void* key_cache,
@@ -1713,7 +1148,7 @@ static int paged_attention_impl(void* out, const void* query, const void* key_ca
   }
 
   const int nqp = nq_pad(nq);
-  const int grid = fast_grid(current_sm_count(), nqp);
+  const int grid = fast_grid(current_sm_count());
   // the cut-segment marker of the merge kernel packs a piece count below 2^11
   if (nqp > 8 && grid * kWarps >= (1 << 11)) return INFERD_ERR_UNSUPPORTED;
   const int chunk_max = kMaxSeqsFast;
@@ -1760,21 +1195,12 @@ static int paged_attention_impl(void* out, const void* query, const void* key_ca
     // grid: persistent, but no more CTAs than pages can feed (upper bound from the host)
     const int64_t pages_ub = static_cast<int64_t>(nb) * num_kv_heads *
                              ((static_cast<int64_t>(max_context_len) + kPage - 1) / kPage);
-    if (INFERD_VERIFY_TMEM && nqp > 8) {
-      // several query rows per kv head: the tensor-memory kernel, one CTA per SM
-      int g = current_sm_count();
-      if (pages_ub < g) g = pages_ub > 0 ? static_cast<int>(pages_ub) : 1;
-      const size_t smem = verify_smem_bytes(nb);
-      st = dtype == INFERD_BF16 ? launch_verify_tmem<true>(km, vm, fp, g, smem, s)
-                                : launch_verify_tmem<false>(km, vm, fp, g, smem, s);
-    } else {
-      int g = grid;
-      const int64_t ctas_ub = (pages_ub + kWarps - 1) / kWarps;  // one warp per page at most
-      if (ctas_ub < g) g = ctas_ub > 0 ? static_cast<int>(ctas_ub) : 1;
-      const size_t smem = fast_smem_bytes(nb, nqp);
-      st = dtype == INFERD_BF16 ? launch_fast<true>(km, vm, fp, nqp / 8, g, smem, s)
-                                : launch_fast<false>(km, vm, fp, nqp / 8, g, smem, s);
-    }
+    int g = grid;
+    const int64_t ctas_ub = (pages_ub + kWarps - 1) / kWarps;  // one warp per page at most
+    if (ctas_ub < g) g = ctas_ub > 0 ? static_cast<int>(ctas_ub) : 1;
+    const size_t smem = fast_smem_bytes(nb);
+    st = dtype == INFERD_BF16 ? launch_fast<true>(km, vm, fp, nqp / 8, g, smem, s)
+                              : launch_fast<false>(km, vm, fp, nqp / 8, g, smem, s);
     if (st != INFERD_OK) return st;
     if (defer_merge) {
       st = dtype == INFERD_BF16 ? launch_merge<true>(fp, nqp / 8, nb * num_kv_heads, s)
