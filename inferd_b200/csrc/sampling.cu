@@ -69,6 +69,13 @@ __device__ __forceinline__ uint32_t samp_rank() {
 __device__ __forceinline__ void samp_cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// the two halves of samp_cluster_sync, with independent work between them
+__device__ __forceinline__ void samp_cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void samp_cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 // Generic address of this CTA's shared variable *p as seen in CTA `rank` of the cluster.
 // Reads through it are ordinary loads, so several can be in flight; the cluster barriers
 // (with memory clobbers) order them against the writes they read.
@@ -867,16 +874,19 @@ __global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(c
   const float temp = p.temps ? p.temps[row] : p.temp;
   const float top_p = p.top_ps ? p.top_ps[row] : p.top_p;
   const bool greedy = !(temp > 0.f);
+  grid_dependency_wait();  // launched early behind the previous kernel on the stream
 
   // ---- phase 1: stage the raw logits; per thread the running max of x and the sum z of
-  // 2^((x/T - y(max)) log2 e) relative to it (rescaled when the max grows), so one pass
-  // and one cluster exchange give the row max and z.  The terms of z come from the ex2
-  // unit: each differs from expf by a few parts in 10^7 at most.
+  // 2^(x log2(e)/T - y(max) log2 e) relative to it (rescaled when the max grows), so one
+  // pass and one cluster exchange give the row max and z.  A term costs one fma and one
+  // ex2: it differs from expf(x/T - y(max)) by a few parts in 10^6 at most, and z is a sum
+  // of such terms (the probabilities themselves are computed exactly below).
   N16Prob pr;
   pr.temp = temp;
   pr.rt = greedy ? 0.f : __frcp_rn(temp);
   pr.t_ok = !greedy && div_ok(temp);
   constexpr float kLog2e = 1.4426950408889634f;
+  const float c1 = greedy ? 0.f : kLog2e * pr.rt;  // log2(e) / T
   float mx = -INFINITY, zs = 0.f;
   // fold cnt values whose max is cm into (mx, zs)
   auto absorb = [&](const float* f, int cnt, float cm) {
@@ -889,8 +899,8 @@ __global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(c
       mx = cm;
     }
     if (mx == -INFINITY) return;
-    const float ym = pr.y(mx);
-    for (int j = 0; j < cnt; ++j) zs += ex2(__fmul_rn(pr.y(f[j]) - ym, kLog2e));
+    const float c2 = pr.y(mx) * kLog2e;
+    for (int j = 0; j < cnt; ++j) zs += ex2(fmaf(f[j], c1, -c2));
   };
   {
     int done = 0;
@@ -933,6 +943,7 @@ __global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(c
     sh.x_mz[0] = bmax;
     sh.x_mz[1] = bz;
   }
+  grid_launch_dependents();  // the next call's CTAs may launch as this one's retire
   samp_cluster_sync();
   float xmax = -INFINITY;
 #pragma unroll
@@ -995,10 +1006,12 @@ __global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(c
     }
     __syncthreads();
     const float thr = sh.thr;
-    // The candidate indices in index order: warp w owns the contiguous entries
-    // [w * per_w, (w + 1) * per_w), lanes take 8 consecutive entries per 256-entry chunk.
-    // One pass counts (per warp), one block barrier gives every warp its offset, a second
-    // pass writes; then the candidates' p in one dense pass over the list.
+    // The candidate indices in index order, in one pass: warp w owns the contiguous
+    // entries [w * per_w, (w + 1) * per_w) and list slots [w * kWarpCap, (w + 1) * kWarpCap);
+    // lanes take 8 consecutive entries per 256-entry chunk, a warp scan places them.  Slots
+    // past a warp's candidates hold p = 0, which every later step skips (no mass, below any
+    // threshold), so the list is read as kN16ListCap slots in index order.
+    constexpr int kWarpCap = kN16ListCap / kSampWarps;
     const int warp = tid >> 5, lane = tid & 31;
     const int per_w = ((n + kSampWarps - 1) / kSampWarps + 7) / 8 * 8;
     const int w0 = min(n, warp * per_w), w1 = min(n, w0 + per_w);
@@ -1016,18 +1029,8 @@ __global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(c
       }
       return bits;
     };
-    int wc = 0;
-    for (int c = w0; c < w1; c += 256) wc += __popc(lane_bits(c + 8 * lane));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) wc += __shfl_xor_sync(0xffffffffu, wc, o);
-    if (lane == 0) sh.wi[warp] = wc;
-    __syncthreads();
-    int pos = 0;
-    count = 0;
-    for (int w = 0; w < kSampWarps; ++w) {
-      if (w < warp) pos += sh.wi[w];
-      count += sh.wi[w];
-    }
+    N16Idx* wl = lidx + warp * kWarpCap;
+    int wc = 0;  // this warp's candidates so far
     for (int c = w0; c < w1; c += 256) {
       uint32_t bits = lane_bits(c + 8 * lane);
       const int mine = __popc(bits);
@@ -1037,23 +1040,29 @@ __global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(c
         const int t = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += t;
       }
-      int at = pos + incl - mine;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if ((bits >> j) & 1u) {
-          if (at < kN16ListCap) lidx[at] = static_cast<N16Idx>(c + 8 * lane + j);
-          ++at;
-        }
+      int at = wc + incl - mine;
+      while (bits) {
+        const int j = __ffs(bits) - 1;
+        bits &= bits - 1;
+        if (at < kWarpCap) wl[at] = static_cast<N16Idx>(c + 8 * lane + j);
+        ++at;
       }
-      pos += __shfl_sync(0xffffffffu, incl, 31);
+      wc += __shfl_sync(0xffffffffu, incl, 31);
     }
+    if (lane == 0) sh.wi[warp] = wc;
     __syncthreads();
-    for (int j = tid; j < count && j < kN16ListCap; j += kN16Threads) lp[j] = prob(lidx[j]);
+    bool over = false;
+    for (int w = 0; w < kSampWarps; ++w) over |= sh.wi[w] > kWarpCap;
+    for (int j = tid; j < kN16ListCap; j += kN16Threads) {
+      const int w = j / kWarpCap;
+      lp[j] = j - w * kWarpCap < sh.wi[w] ? prob(lidx[j]) : 0.f;
+    }
     __syncthreads();
     // A CTA whose list overflowed takes the full path alone: every entry off the list has
     // p below the proven bound, under the threshold, so it adds only to histogram bins
     // below each pass's cut bin and never to the kept set.
-    fast = count <= kN16ListCap;
+    fast = !over;
+    count = kN16ListCap;
   }
   // every entry of this CTA's set, as f(p) (list entries, or every logit)
   auto each = [&](auto&& f) {
@@ -1113,7 +1122,21 @@ __global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(c
   }
   local = block_sum_u64(sh, local);
   if (tid == 0) sh.x_kept = local;
-  samp_cluster_sync();
+  // split cluster barrier: the zero fill of the output (which needs no total) runs between
+  // this CTA's arrival and its wait for the others'
+  samp_cluster_arrive();
+  if (out && fast) {
+    int done = 0;
+    if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+      const int nv = n / 4;
+      float4* out4 = reinterpret_cast<float4*>(out);
+      for (int v = tid; v < nv; v += kN16Threads) out4[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      done = nv * 4;
+    }
+    for (int i = done + tid; i < n; i += kN16Threads) out[i] = 0.f;
+  }
+  __syncthreads();  // every zero store of this CTA's slice before any scatter into it
+  samp_cluster_wait();
   unsigned long long base = 0, total = 0;
 #pragma unroll
   for (int r = 0; r < C; ++r) {
@@ -1126,16 +1149,7 @@ __global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(c
   if (out) {
     const float s = static_cast<float>(static_cast<double>(total) / kFixedOne);
     if (fast) {
-      // zeros everywhere, then the kept candidates (the barrier orders the two stores)
-      int done = 0;
-      if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
-        const int nv = n / 4;
-        float4* out4 = reinterpret_cast<float4*>(out);
-        for (int v = tid; v < nv; v += kN16Threads) out4[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-        done = nv * 4;
-      }
-      for (int i = done + tid; i < n; i += kN16Threads) out[i] = 0.f;
-      __syncthreads();
+      // zeros everywhere (above), then the kept candidates
       for (int j = tid; j < count; j += kN16Threads) {
         const float v = lp[j];
         if (v > 0.f && kept(v, static_cast<int>(lo) + lidx[j])) out[lidx[j]] = __fdiv_rn(v, s);
@@ -1219,13 +1233,15 @@ int launch_nucleus16(const SampParams& p, cudaStream_t s) {
   cfg.blockDim = dim3(kN16Threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = C;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cuda_status(cudaLaunchKernelEx(&cfg, nucleus16_kernel<C, In>, p));
 }
 
