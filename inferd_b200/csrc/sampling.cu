@@ -620,6 +620,8 @@ using N16Idx = std::conditional<(kN16MaxPerCta > 65536), uint32_t, uint16_t>::ty
 constexpr int kN16Chunk = kN16Threads * 8;  // index-ordered passes: 8 consecutive per thread
 static_assert(kN16Threads / 32 == kSampWarps, "the block reductions assume 16 warps");
 
+constexpr int kN16Fin = 64;  // entries the select finishes by sorting (cluster-wide)
+
 struct N16Shared {
   __align__(16) uint32_t hist_m[2][256];
   __align__(16) uint32_t hist_c[2][256];
@@ -634,6 +636,15 @@ struct N16Shared {
   unsigned long long x_u;
   float x_mz[2];              // block max of the logits, block sum z relative to it
   unsigned long long x_kept;  // kept mass of the CTA
+  // the CTA's entries sharing the threshold's 16-bit prefix (finish of the select)
+  uint32_t fin_bits[kN16Fin];
+  int fin_idx[kN16Fin];
+  int fin_n;
+  // their cluster-wide order (warp 0 of each CTA)
+  unsigned long long fin_key[kN16Fin];
+  uint32_t fin_cut_bits;
+  int fin_cut_idx;
+  int fin_found;
   // broadcasts
   uint32_t b_prefix;
   unsigned long long b_mass;
@@ -695,18 +706,23 @@ struct N16Prob {
 template <int C, bool kCluster, class Each>
 __device__ uint32_t n16_radix_select(N16Shared& sh, unsigned long long limit, Each each,
                                      unsigned long long& above_out, uint32_t& ties_out,
-                                     uint32_t& ties_before_out, uint32_t& ties_mine_out) {
+                                     uint32_t& ties_before_out, uint32_t& ties_mine_out,
+                                     int shift_hi = 24, int shift_lo = 0, uint32_t prefix_in = 0,
+                                     unsigned long long above_in = 0) {
   constexpr int R = kCluster ? C : 1;  // CTAs whose histograms are summed
   const int tid = threadIdx.x, lane = tid & 31;
-  for (int b = tid; b < 2 * 256; b += kN16Threads) {
-    (&sh.hist_m[0][0])[b] = 0;
-    (&sh.hist_c[0][0])[b] = 0;
+  if (shift_hi == 24) {
+    // a continuation (shift_hi < 24) finds its buffer cleared by the previous pass
+    for (int b = tid; b < 2 * 256; b += kN16Threads) {
+      (&sh.hist_m[0][0])[b] = 0;
+      (&sh.hist_c[0][0])[b] = 0;
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  uint32_t prefix = 0;
-  unsigned long long above = 0;
+  uint32_t prefix = prefix_in;
+  unsigned long long above = above_in;
   uint32_t ties = 0;
-  for (int shift = 24; shift >= 0; shift -= 8) {
+  for (int shift = shift_hi; shift >= shift_lo; shift -= 8) {
     const int buf = (shift >> 3) & 1;
     uint32_t* hm = sh.hist_m[buf];
     uint32_t* hc = sh.hist_c[buf];
@@ -1077,10 +1093,108 @@ __global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(c
   constexpr float kFx = 4503599627370496.0f;
   uint32_t tbits = 0;
   int i_cut = 0x7fffffff;  // ties at tbits are kept below this global index
+  bool finished = false;
+  unsigned long long above = 0;
+  uint32_t ties = 0, ties_before = 0, ties_mine = 0;
   if (cut) {
-    unsigned long long above;
-    uint32_t ties, ties_before, ties_mine;
-    tbits = n16_radix_select<C, true>(sh, limit, each, above, ties, ties_before, ties_mine);
+    // two 8-bit passes locate the threshold's 16-bit prefix (exponent and 7 mantissa bits)
+    const uint32_t pre = n16_radix_select<C, true>(sh, limit, each, above, ties, ties_before, ties_mine, 24, 16);
+    if (ties <= static_cast<uint32_t>(kN16Fin)) {
+      // Few entries share it (bf16 logits make them largely exact ties): every CTA lists its
+      // own, and warp 0 of each CTA orders all of them by (p desc, index asc) and walks
+      // their masses from `above`.  The first entry whose exclusive mass exceeds the limit
+      // is the first one dropped: the kept set is everything before it in that order.
+      if (tid == 0) sh.fin_n = 0;
+      __syncthreads();
+      auto take = [&](float v, int gi) {
+        const uint32_t b = __float_as_uint(v);
+        if ((b >> 16) == (pre >> 16)) {
+          const int at = atomicAdd(&sh.fin_n, 1);
+          if (at < kN16Fin) {
+            sh.fin_bits[at] = b;
+            sh.fin_idx[at] = gi;
+          }
+        }
+      };
+      if (fast) {
+        for (int j = tid; j < count; j += kN16Threads) take(lp[j], static_cast<int>(lo) + lidx[j]);
+      } else {
+        for (int i = tid; i < n; i += kN16Threads) take(prob(i), static_cast<int>(lo) + i);
+      }
+      __syncthreads();
+      samp_cluster_sync();  // every CTA's list is complete
+      if (tid < 32) {
+        const int lane = tid;
+        // entries e = lane and lane + 32 of the cluster's lists in rank order
+        unsigned long long key[2] = {~0ull, ~0ull};
+        int tot = 0;
+#pragma unroll
+        for (int r = 0; r < C; ++r) {
+          const int nr = min(static_cast<int>(ld_cl_u32(&sh.fin_n, r)), kN16Fin);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int e = lane + 32 * h - tot;
+            if (e >= 0 && e < nr) {
+              const uint32_t b = *cl_ptr(sh.fin_bits + e, r);
+              const int gi = *cl_ptr(sh.fin_idx + e, r);
+              key[h] = (static_cast<unsigned long long>(~b) << 32) | static_cast<uint32_t>(gi);
+            }
+          }
+          tot += nr;
+        }
+        // rank of each entry among the (at most 64) keys, then the keys in order (unused
+        // slots keep the largest key)
+        sh.fin_key[lane] = ~0ull;
+        sh.fin_key[lane + 32] = ~0ull;
+        __syncwarp();
+        int rank[2] = {0, 0};
+        for (int src = 0; src < 64; ++src) {
+          const unsigned long long k = __shfl_sync(0xffffffffu, key[src >> 5], src & 31);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) rank[h] += k < key[h] ? 1 : 0;
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          if (key[h] != ~0ull) sh.fin_key[rank[h]] = key[h];  // distinct: the index is in the key
+        __syncwarp();
+        // exclusive masses in order: lane holds positions 2 lane, 2 lane + 1
+        const unsigned long long k0 = sh.fin_key[2 * lane], k1 = sh.fin_key[2 * lane + 1];
+        const uint32_t m0 = k0 == ~0ull ? 0u : to_q31(__uint_as_float(~static_cast<uint32_t>(k0 >> 32)));
+        const uint32_t m1 = k1 == ~0ull ? 0u : to_q31(__uint_as_float(~static_cast<uint32_t>(k1 >> 32)));
+        unsigned long long incl = static_cast<unsigned long long>(m0) + m1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const unsigned long long t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const unsigned long long ex0 = above + incl - m0 - m1, ex1 = ex0 + m0;
+        int first = 64;
+        if (k1 != ~0ull && ex1 > limit) first = 2 * lane + 1;
+        if (k0 != ~0ull && ex0 > limit) first = 2 * lane;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
+        if (lane == 0) {
+          sh.fin_found = first < tot ? 1 : 0;
+          if (first < tot) {
+            const unsigned long long kc = sh.fin_key[first];
+            sh.fin_cut_bits = ~static_cast<uint32_t>(kc >> 32);
+            sh.fin_cut_idx = static_cast<int>(static_cast<uint32_t>(kc));
+          }
+        }
+      }
+      __syncthreads();
+      if (sh.fin_found) {
+        tbits = sh.fin_cut_bits;
+        i_cut = sh.fin_cut_idx;
+        finished = true;
+      }
+    }
+    if (!finished) {
+      // the last two passes, from the 16-bit prefix
+      tbits = n16_radix_select<C, true>(sh, limit, each, above, ties, ties_before, ties_mine, 8, 0, pre, above);
+    }
+  }
+  if (cut && !finished) {
     const unsigned long long tq = to_q31(__uint_as_float(tbits));
     uint32_t keep_ties = ties;
     if (tq > 0) {

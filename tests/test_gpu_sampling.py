@@ -200,21 +200,24 @@ def test_nucleus_probs_bf16_rows(cuda_device, scale, t, top_p):
         np.testing.assert_allclose(a / a.sum(), b / b.sum(), rtol=1e-5)
 
 
-def test_bf16_tied_group_cut_across_ctas_in_index_order(cuda_device):
-    # 256 equal logits scattered over a 151936 vocabulary (four CTAs), everything else so far
-    # below that z rounds to 256 exactly: each tied p is 2^-8, q = 2^23 units of 2^-31, so
-    # top_p = 0.3 keeps floor(0.3 * 2^31 / 2^23) + 1 = 77 of them, the first 77 in index order
+@pytest.mark.parametrize("n_ties,n_expect", [(256, 77), (32, 10)])
+def test_bf16_tied_group_cut_across_ctas_in_index_order(cuda_device, n_ties, n_expect):
+    # n_ties equal logits scattered over a 151936 vocabulary (four CTAs), everything else so
+    # far below that z rounds to n_ties exactly: each tied p is 1/n_ties, so top_p = 0.3 keeps
+    # the first floor(0.3 * 2^31 / q) + 1 of them in index order (256 ties: q = 2^23, 77
+    # kept; 32 ties: 10 kept).  32 ties share the threshold's 16-bit prefix with nothing else,
+    # so the select finishes by sorting them; 256 are too many and it runs all four passes.
     vocab = 151936
     logits = torch.full((2, vocab), -40.0)
     g = torch.Generator().manual_seed(11)
-    pos = torch.randperm(vocab, generator=g)[:256].sort().values
+    pos = torch.randperm(vocab, generator=g)[:n_ties].sort().values
     logits[:, pos] = 10.0
     logits = logits.to(torch.bfloat16)
     got = nucleus_probs(logits.to(cuda_device), 1.0, 0.3).cpu().numpy()
     p = oracle.nucleus_probs(logits[0].float().numpy(), 1.0, 1.0)
-    assert np.all(p[pos.numpy()] == np.float32(2.0 ** -8))
+    assert np.all(p[pos.numpy()] == np.float32(1.0 / n_ties))
     n_keep = int(oracle.kept_mask_fixed(p, 0.3).sum())
-    assert n_keep == 77
+    assert n_keep == n_expect
     for r in range(2):
         kept = np.nonzero(got[r])[0]
         assert kept.tolist() == pos[:n_keep].tolist()
