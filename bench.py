@@ -689,7 +689,7 @@ def run_sampling(args, device: torch.device) -> list[dict]:
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
                          "bytes_per_call": nbytes, "peak_source": peaks["source"],
-                         "kernel": "sampling_kernel"},
+                         "kernel": "nucleus16_kernel"},  # the bf16 logits' kernel
             "l2": "eight rotating logits copies (156 MB) and outputs",
             "calls_timed": args.steps,
         })
