@@ -608,11 +608,8 @@ __global__ void __launch_bounds__(kSampThreads) sampling_kernel(const SampParams
 // other entry without computing p; each candidate's exact p goes into a per-CTA list in
 // index order.  Rows whose candidates overflow a list, and rows with top_p >= 1, take the
 // full path: the same steps over every entry, p recomputed in each pass.
-#ifndef INFERD_N16_CTAS_PER_SM
-#define INFERD_N16_CTAS_PER_SM 2
-#endif
 constexpr int kN16Threads = 512;
-constexpr int kN16CtasPerSm = INFERD_N16_CTAS_PER_SM;
+constexpr int kN16CtasPerSm = 2;
 constexpr int kN16MaxPerCta = 38912 * 2 / kN16CtasPerSm;  // 16-bit logits per CTA (76 KB at 2 / SM)
 constexpr int kN16ListCap = 4096 * 2 / kN16CtasPerSm;  // candidates per CTA: local index + p (f32)
 // local index of a candidate: 16 bits while a CTA's slice fits them
