@@ -985,10 +985,16 @@ __global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(c
   // ---- phase 2: z = sum of exp(x / T - ymax), the CTAs' sums moved to the row max
   pr.ymax = __fdiv_rn(xmax, temp);
   float z = 0.f;
+  {
+    float cm[C], cz[C];  // every CTA's (max, z) loaded first, so the remote loads overlap
 #pragma unroll
-  for (int r = 0; r < C; ++r) {
-    const float cz = ld_cl_f32(&sh.x_mz[1], r);
-    if (cz != 0.f) z += cz * ex2(__fmul_rn(pr.y(ld_cl_f32(&sh.x_mz[0], r)) - pr.ymax, kLog2e));
+    for (int r = 0; r < C; ++r) {
+      cm[r] = ld_cl_f32(&sh.x_mz[0], r);
+      cz[r] = ld_cl_f32(&sh.x_mz[1], r);
+    }
+#pragma unroll
+    for (int r = 0; r < C; ++r)
+      if (cz[r] != 0.f) z += cz[r] * ex2(__fmul_rn(pr.y(cm[r]) - pr.ymax, kLog2e));
   }
   pr.z = z;
   pr.rz = __frcp_rn(z);
@@ -1044,6 +1050,7 @@ __global__ void __launch_bounds__(kN16Threads, kN16CtasPerSm) nucleus16_kernel(c
     };
     N16Idx* wl = lidx + warp * kWarpCap;
     int wc = 0;  // this warp's candidates so far
+#pragma unroll 2
     for (int c = w0; c < w1; c += 256) {
       uint32_t bits = lane_bits(c + 8 * lane);
       const int mine = __popc(bits);
