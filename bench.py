@@ -67,6 +67,17 @@ def context_lengths(workload: str, world: int, seed: int = 0) -> np.ndarray:
     return rng.integers(w["lo"], w["hi"] + 1, size=w["seqs"] * world)
 
 
+def rank_shards(workload: str, world: int) -> tuple[np.ndarray, list[list[int]]]:
+    """The job's lengths and each rank's sequences: longest first onto the rank with the
+    fewest tokens (inferd_b200.sharded.assign_by_tokens), so every GPU streams about the
+    same KV bytes; a contiguous split of the same random lengths left one of four GPUs
+    8.7 % above the mean, and every step waits for the slowest rank."""
+    from inferd_b200.sharded import assign_by_tokens
+
+    lens = context_lengths(workload, world)
+    return lens, assign_by_tokens(lens.tolist(), world)
+
+
 def step_bytes(ctx_lens, q_len: int) -> dict:
     """Algorithmic bytes of one step for sequences whose context (after the append) is
     ctx_lens: K and V of every visible key, query read, output write, block-table and
@@ -162,11 +173,9 @@ class DeviceWorkload:
         self.workload = workload
         self.device = device
         self.q_len = w["q_len"]
-        from inferd_b200.sharded import shard_range
-
-        all_lens = context_lengths(workload, world)
-        lo, hi = shard_range(all_lens.size, world, rank)  # w["seqs"] per rank
-        self.base = all_lens[lo:hi].astype(np.int64)
+        all_lens, owners = rank_shards(workload, world)
+        self.counts = [len(o) for o in owners]  # sequences per rank (w["seqs"] here)
+        self.base = all_lens[owners[rank]].astype(np.int64)
         self.b = self.base.size
         # context after the append = base + q_len (the appended tokens sit at base .. )
         self.ctx = self.base + self.q_len
@@ -253,12 +262,14 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     if world > 1 and args.gather == "nccl":
         # NCCL all-gather of step N's outputs on NCCL's stream, overlapping step N + 1 (the
         # faster of the two on measurement)
-        gather = OutputGather(tuple(wl.out.shape[1:]), wl.out.dtype, device, [wl.b] * world)
+        gather = OutputGather(tuple(wl.out.shape[1:]), wl.out.dtype, device, wl.counts)
     elif world > 1:
         # p2p: every rank pushes its outputs into every rank's memory over NVLink and waits
         # for the others' pushes.  fused: the attention kernel's epilogue stores them there
         # itself and a one-CTA kernel publishes the step; the wait for step N - 1 comes at
         # the start of step N, where every rank has long published it.
+        if len(set(wl.counts)) != 1:
+            raise ValueError(f"--gather {args.gather} needs equal rows per rank, not {wl.counts}")
         peer = PeerGather(tuple(wl.out.shape[1:]), wl.out.dtype, device, wl.b)
     fused = peer is not None and args.gather == "fused"
     stream = torch.cuda.current_stream(device)
@@ -341,8 +352,9 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
                 peer.wait()
             gathered = peer._slots[peer._epoch & 1]
         # every rank's rows of the gathered output equal that rank's own output, on every rank
-        ref = torch.empty_like(gathered)
-        dist.all_gather_into_tensor(ref, wl.out.contiguous())
+        from inferd_b200.sharded import gather_outputs
+
+        ref = gather_outputs(wl.out, wl.counts)
         mine = torch.equal(gathered, ref)
         flag = torch.tensor([int(mine and checks["append_bit_exact"])], device=device)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
@@ -434,7 +446,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
 def config_block(workload: str, world: int) -> dict:
     """The `config` object of both arms' lines: the workload and its sizes per GPU."""
     w = WORKLOADS[workload]
-    ctx = context_lengths(workload, world)[:w["seqs"]] + w["q_len"]
+    lens, owners = rank_shards(workload, world)
+    ctx = lens[owners[0]] + w["q_len"]
     pages = (ctx + BS - 1) // BS
     grow = (POOL_GROWTH + w["q_len"] + BS - 1) // BS + 1
     attn_gb = step_bytes(ctx, w["q_len"])["attention"] / 1e9
@@ -487,7 +500,7 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
         q_h.copy_(dwl.q.cpu())
         k_h.copy_(dwl.k_new.cpu())
         v_h.copy_(dwl.v_new.cpu())
-    out_rows = dwl.b * world
+    out_rows = sum(dwl.counts)
     out_h = torch.empty((out_rows, ql, HQ, D), dtype=torch.bfloat16).pin_memory()
     gathered = torch.empty((out_rows, ql, HQ, D), dtype=torch.bfloat16, device=device)
     stream = torch.cuda.current_stream(device)
@@ -501,7 +514,7 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
             peer.push(graph.output)
             out_h.copy_(peer.wait(), non_blocking=True)
         elif world > 1:
-            gather_outputs(graph.output, out=gathered)
+            gather_outputs(graph.output, dwl.counts, out=gathered)
             out_h.copy_(gathered, non_blocking=True)
         if ql == 1:
             graph.prepare()  # step N + 1's pages and slots while step N runs

@@ -175,6 +175,29 @@ def test_fp8_linear_ragged_shapes(cuda_device, n, k):
             assert_linear_close(y.float().cpu().numpy()[:, rows], ref, f"n={n} k={k} m={m} packed={packed}")
 
 
+@pytest.mark.parametrize("m", [1, 3, 13, 16])
+def test_fp8_linear_decode_tile_equals_rows_of_a_wider_tile(cuda_device, m):
+    # decode token counts on the whole-tile plan: a 16-token tile (MMA N = 32) and the
+    # 32-token tile of a 17-token call (N = 64) give the same rows bit for bit (same codes,
+    # scales and K order; rows past M and the K tail zero), within tolerance of the oracle
+    n, k = 17408 - 128, 272   # 68 tile pairs; K = 2 * 128 + 16
+    g = torch.Generator().manual_seed(90 + m)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    q, s = quantize_fp8_per_channel(w.to(cuda_device))
+    packed = pack_fp8_weight(q)
+    x = (torch.randn(17, k, generator=g) * torch.logspace(-3, 2, 17)[:, None]).to(torch.bfloat16)
+    xd = x.to(cuda_device)
+    for wt, shape in ((packed, (n, k)), (q, None)):
+        y17 = fp8_linear(xd, wt, s, packed_shape=shape)
+        y = fp8_linear(xd[:m], wt, s, packed_shape=shape)
+        torch.cuda.synchronize()
+        assert torch.equal(y, y17[:m])
+    rows = slice(n - 1536, n)
+    ref = oracle.fp8_linear(x[:m].float().numpy(), q.view(torch.uint8).cpu().numpy()[rows],
+                            s.cpu().numpy()[rows])
+    assert_linear_close(y.float().cpu().numpy()[:, rows], ref, f"m={m}")
+
+
 def test_fp8_linear_out_must_be_on_device(cuda_device):
     # the GEMM writes `out` through its raw pointer: host tensors and wrong dtypes or sizes
     # are refused before anything is launched
