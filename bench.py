@@ -262,7 +262,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     if world > 1 and args.gather == "nccl":
         # NCCL all-gather of step N's outputs on NCCL's stream, overlapping step N + 1 (the
         # faster of the two on measurement)
-        gather = OutputGather(tuple(wl.out.shape[1:]), wl.out.dtype, device, wl.counts)
+        gather = OutputGather(tuple(wl.out.shape[1:]), wl.out.dtype, device, wl.counts,
+                              max_ctas=args.gather_ctas)
     elif world > 1:
         # p2p: every rank pushes its outputs into every rank's memory over NVLink and waits
         # for the others' pushes.  fused: the attention kernel's epilogue stores them there
@@ -385,6 +386,8 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     if not all(checks.values()) or (parity is not None and not parity["ok"]):
         raise RuntimeError(f"output check failed: {checks} {parity}")
 
+    if gather is not None:
+        gather.close()  # the end-to-end leg gathers on the compute stream, with full grids
     e2e = run_e2e(args, wl, rank, world, device, peer=peer)
     if peer is not None:
         peer.close()
@@ -426,6 +429,7 @@ def run_ours(args, rank: int, world: int, device: torch.device) -> dict | None:
     line["checks"] = checks
     if gather_us is not None:
         line["gather"] = {"kind": args.gather, "us_per_step_alone": gather_us,
+                          "nccl_max_ctas": args.gather_ctas if args.gather == "nccl" else None,
                           "bytes_per_rank": int(wl.out.numel() * wl.out.element_size()),
                           "how": {"nccl": "NCCL all_gather_into_tensor on NCCL's stream, "
                                           "overlapping the next step",
@@ -870,6 +874,9 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--gather", choices=["p2p", "nccl", "fused"], default="nccl",
                     help="N > 1: how each step's outputs reach every GPU")
+    ap.add_argument("--gather-ctas", type=int, default=0,
+                    help="--gather nccl: NCCL CTAs for the overlapped all-gather, and as many "
+                         "SMs left out of the attention grid (0: NCCL's default, full grid)")
     ap.add_argument("--e2e-steps", type=int, default=E2E_STEPS)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -362,6 +362,21 @@ INFERD_API int inferd_paged_attention_gather(
 INFERD_API int inferd_gather_publish(uint32_t* const* flags, int32_t rank, int32_t world,
                                      uint32_t epoch, void* stream);
 
+/*
+ * Room beside the attention for a collective on another stream.  The tensor-core
+ * attention is a persistent grid that fills every SM and splits the pages statically, so
+ * a CTA that cannot start because another kernel holds its SM (an NCCL all-gather of the
+ * previous step's outputs) delays the whole call.  After this call, attention grids
+ * launched later by this process size themselves for (SM count - sms) SMs, leaving room
+ * for a kernel of at most sms CTAs (NCCL's max_ctas).  Process-wide, default 0;
+ * 0 <= sms < the SM count of the current device (INFERD_ERR_INVALID_ARGUMENT otherwise).
+ * Grids already captured in a CUDA graph keep the size they were captured with.
+ * inferd_paged_attention_reserved_sms returns the current value.  No counterpart in the
+ * reference, which runs one process on one GPU.
+ */
+INFERD_API int inferd_paged_attention_reserve_sms(int32_t sms);
+INFERD_API int32_t inferd_paged_attention_reserved_sms(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,6 +21,7 @@ from .paged_attn import (  # noqa: F401
     paged_attention_reference,
     paged_decode,
     paged_verify,
+    reserve_sms,
     sdpa_reference,
 )
 from .paged_cache import (  # noqa: F401

@@ -98,6 +98,8 @@ _SIGNATURES = {
         _i32, _i32, _i32, _i32, _i32, _i64, _i32, _f32, _i32, _c_void_p, _sz, _c_void_p, _i32,
         _i64, _c_void_p, _c_void_p]),
     "inferd_gather_publish": (ctypes.c_int, [_c_void_p, _i32, _i32, ctypes.c_uint32, _c_void_p]),
+    "inferd_paged_attention_reserve_sms": (ctypes.c_int, [_i32]),
+    "inferd_paged_attention_reserved_sms": (_i32, []),
     "inferd_gather_wait": (ctypes.c_int, [
         _c_void_p, _i32, ctypes.c_uint32, _u64, _c_void_p, _c_void_p]),
 }

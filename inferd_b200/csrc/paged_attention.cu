@@ -30,6 +30,7 @@
 // default scale 1/sqrt(head_dim), fp32 softmax, probabilities rounded to the working
 // dtype before P.V) except that Q.K is accumulated in fp32 rather than rounded to the
 // working dtype.
+#include <atomic>
 #include <type_traits>
 
 #include <mutex>
@@ -932,6 +933,16 @@ inline WorkspaceLayout workspace_layout(int num_seqs, int num_kv_heads, int nqp,
 
 inline int fast_grid(int sm_count) { return sm_count * kCtasPerSm; }
 
+// SMs that persistent grids leave free for a collective beside them (process-wide)
+std::atomic<int> g_reserved_sms{0};
+
+// SMs the persistent grid of a call launched now may fill
+inline int grid_sms() {
+  const int sms = current_sm_count();
+  const int r = g_reserved_sms.load(std::memory_order_relaxed);
+  return r < sms ? sms - r : 1;
+}
+
 inline size_t fast_smem_bytes(int num_seqs) {
   return 1024 + static_cast<size_t>(kWarps) * kStagesPerWarp * (kStageBytes + 8) +
          (static_cast<size_t>(num_seqs) + 1) * 4;
@@ -1058,6 +1069,16 @@ bool paged_attention_fast_path(int32_t dtype, int32_t head_dim, int32_t block_si
 
 using namespace inferd;
 
+extern "C" int inferd_paged_attention_reserve_sms(int32_t sms) {
+  if (sms < 0 || sms >= current_sm_count()) return INFERD_ERR_INVALID_ARGUMENT;
+  g_reserved_sms.store(sms, std::memory_order_relaxed);
+  return INFERD_OK;
+}
+
+extern "C" int32_t inferd_paged_attention_reserved_sms(void) {
+  return g_reserved_sms.load(std::memory_order_relaxed);
+}
+
 extern "C" size_t inferd_paged_attention_counter_bytes(int32_t num_seqs, int32_t num_kv_heads) {
   if (num_seqs <= 0 || num_kv_heads <= 0) return 0;
   const size_t seqs = num_seqs < kMaxSeqsFast ? num_seqs : kMaxSeqsFast;
@@ -1148,7 +1169,7 @@ static int paged_attention_impl(void* out, const void* query, const void* key_ca
   }
 
   const int nqp = nq_pad(nq);
-  const int grid = fast_grid(current_sm_count());
+  const int grid = fast_grid(grid_sms());
   // the cut-segment marker of the merge kernel packs a piece count below 2^11
   if (nqp > 8 && grid * kWarps >= (1 << 11)) return INFERD_ERR_UNSUPPORTED;
   const int chunk_max = kMaxSeqsFast;

@@ -35,6 +35,17 @@ def set_sync_checks(enabled: bool) -> bool:
     return prev
 
 
+def reserve_sms(sms: int) -> int:
+    """Leave `sms` SMs out of the persistent attention grids launched from now on
+    (process-wide; 0 restores full grids), for a collective that runs beside the attention
+    on another stream with at most that many CTAs, so that none of the attention's
+    statically assigned CTAs waits for it.  Returns the previous value."""
+    lib = _lib.load()
+    prev = int(lib.inferd_paged_attention_reserved_sms())
+    _lib.check(lib.inferd_paged_attention_reserve_sms(int(sms)), "paged_attention_reserve_sms")
+    return prev
+
+
 def _check_blocks(key_blocks: torch.Tensor, value_blocks: torch.Tensor) -> None:
     if key_blocks.shape != value_blocks.shape:
         raise ValueError("key/value block tensors must have identical shape")

@@ -19,7 +19,9 @@ sequence order, after each step.  The reference runs one process on one GPU
 every shard has the same size, else a padded all-gather (also what gloo ranks on CPU use).
 `OutputGather` preallocates everything and overlaps step N's all-gather with step N + 1's
 compute: local outputs alternate between two buffers, so the collective reading step N's
-buffer never races the kernels writing step N + 1's.
+buffer never races the kernels writing step N + 1's.  With max_ctas=k it runs NCCL on at
+most k CTAs in a process group of its own and leaves k SMs out of the persistent attention
+grid (paged_attn.reserve_sms), so the overlapped all-gather never delays an attention CTA.
 """
 
 from __future__ import annotations
@@ -108,7 +110,21 @@ class OutputGather:
     """
 
     def __init__(self, tail: tuple[int, ...], dtype: torch.dtype, device: torch.device,
-                 counts: list[int] | None = None, *, group=None) -> None:
+                 counts: list[int] | None = None, *, group=None, max_ctas: int = 0) -> None:
+        self._own_group = None
+        self._prev_reserve = None
+        if max_ctas and dist.get_backend(group) == "nccl":
+            # NCCL on at most max_ctas CTAs, in a group of its own, and as many SMs left
+            # out of the persistent attention grid: the overlapped all-gather then holds
+            # no SM that a statically assigned attention CTA waits for
+            from .paged_attn import reserve_sms
+
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.config.max_ctas = int(max_ctas)
+            opts.config.min_ctas = 1
+            ranks = dist.get_process_group_ranks(group) if group is not None else None
+            group = self._own_group = dist.new_group(ranks, backend="nccl", pg_options=opts)
+            self._prev_reserve = reserve_sms(int(max_ctas))
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -181,6 +197,20 @@ class OutputGather:
             if self._work[i] is not None:
                 self._work[i].wait()
                 self._work[i] = None
+
+    def close(self) -> None:
+        """Order every started collective, give the attention its full grid back and
+        destroy the gather's own process group (if max_ctas made one); collective, like
+        the constructor."""
+        self.wait_all()
+        if self._prev_reserve is not None:
+            from .paged_attn import reserve_sms
+
+            reserve_sms(self._prev_reserve)
+            self._prev_reserve = None
+        if self._own_group is not None:
+            dist.destroy_process_group(self._own_group)
+            self._own_group = None
 
 
 class _DeviceBytes:

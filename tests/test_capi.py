@@ -76,3 +76,16 @@ def test_argument_validation_without_device():
         _lib.check(_lib.ERR_DEVICE_INDEX, "x")
     with pytest.raises(RuntimeError):
         _lib.check(_lib.ERR_WORKSPACE, "x")
+
+
+def test_reserved_sms_bounds_without_device():
+    # the reserve is host state: negative counts and counts of every SM are refused, a
+    # valid one reads back and 0 restores full grids
+    lib = _lib.load()
+    assert lib.inferd_paged_attention_reserved_sms() == 0
+    assert lib.inferd_paged_attention_reserve_sms(-1) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.inferd_paged_attention_reserve_sms(1 << 20) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.inferd_paged_attention_reserve_sms(8) == _lib.OK
+    assert lib.inferd_paged_attention_reserved_sms() == 8
+    assert lib.inferd_paged_attention_reserve_sms(0) == _lib.OK
+    assert lib.inferd_paged_attention_reserved_sms() == 0

@@ -177,6 +177,25 @@ def test_single_long_sequence_split_across_ctas(cuda_device):
     assert_bf16_close(out, ref, "long sequence")
 
 
+@pytest.mark.parametrize("reserve,q_len", [(8, 1), (100, 1), (12, 4)])
+def test_grid_with_reserved_sms(cuda_device, reserve, q_len):
+    # a grid that leaves SMs to a collective splits the pages differently (other cut
+    # segments and merges); the results stay within the same bound of the oracle
+    from inferd_b200 import reserve_sms
+
+    rng = np.random.default_rng(40 + reserve)
+    lens = rng.integers(300, 6000, size=12).tolist()
+    prev = reserve_sms(reserve)
+    try:
+        assert _lib.load().inferd_paged_attention_reserved_sms() == reserve
+        out, ref = run_batched(cuda_device, lens, q_len, 32, 8, torch.bfloat16, seed=40 + reserve)
+    finally:
+        reserve_sms(prev)
+    assert_bf16_close(out, ref, f"{reserve} SMs reserved")
+    with pytest.raises(ValueError):
+        reserve_sms(torch.cuda.get_device_properties(cuda_device).multi_processor_count)
+
+
 @pytest.mark.parametrize("hq,hkv", [(8, 8), (16, 2), (64, 8), (32, 4)])
 def test_gqa_ratios(cuda_device, hq, hkv):
     lens = [5, 64, 333, 1024]
