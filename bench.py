@@ -558,6 +558,10 @@ def run_e2e(args, dwl: DeviceWorkload, rank: int, world: int, device: torch.devi
     return {"value": round(total_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "steps": steps, "ms_per_step": round(ms / steps, 5),
+            "d2h": ("the attention's epilogue stores the output rows to pinned host memory "
+                    "as the grid runs" if graph._host_rows is not None else
+                    "one device-to-host copy after the attention") if world == 1 else
+                   "all-gather, then one device-to-host copy",
             "note": "one DecodeGraph replay per step (inputs H2D from pinned memory, page-table "
                     "update, KV append, attention, output D2H); contexts grow by one token per "
                     "step (verify: the window is appended, verified, and all but one token "

@@ -61,6 +61,16 @@ INFERD_API const char* inferd_status_string(int status);
 INFERD_API const char* inferd_last_cuda_error(void);
 
 /*
+ * Device address of page-locked host memory (cudaHostAlloc / cudaMallocHost), which
+ * kernels may read and write directly; under unified addressing it equals the host
+ * address.  INFERD_ERR_CUDA for pageable or unregistered memory.  A caller can hand it
+ * to inferd_paged_attention_gather as a destination, so that the attention's epilogue
+ * copies its output rows to the host while the grid still runs instead of a separate
+ * device-to-host copy after it.  No counterpart in the reference.
+ */
+INFERD_API int inferd_host_device_pointer(const void* host, void** device_ptr);
+
+/*
  * reshape_and_cache: write num_tokens new K/V rows into their pool slots.
  * Replaces the write loop of PagedKVCache.append_tokens, core/paged_cache.py:177-183
  * (key_cache[layer][block, :, offset, :] = layer_keys[layer][rel_pos]); the page-table

@@ -46,6 +46,7 @@ _SIGNATURES = {
     "inferd_version": (ctypes.c_int, []),
     "inferd_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "inferd_last_cuda_error": (ctypes.c_char_p, []),
+    "inferd_host_device_pointer": (ctypes.c_int, [_c_void_p, _c_void_p]),
     "inferd_reshape_and_cache": (ctypes.c_int, [
         _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64,
         _i32, _i32, _i32, _i64, _i32, _c_void_p, _c_void_p]),

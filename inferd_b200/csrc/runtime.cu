@@ -80,4 +80,17 @@ const char* inferd_status_string(int status) {
 
 const char* inferd_last_cuda_error(void) { return inferd::g_last_cuda_error; }
 
+int inferd_host_device_pointer(const void* host, void** device_ptr) {
+  if (host == nullptr || device_ptr == nullptr) return INFERD_ERR_INVALID_ARGUMENT;
+  void* d = nullptr;
+  const cudaError_t e = cudaHostGetDevicePointer(&d, const_cast<void*>(host), 0);
+  if (e != cudaSuccess) {
+    const int st = inferd::cuda_status(e);
+    cudaGetLastError();  // not sticky: leave no error for the next launch check
+    return st;
+  }
+  *device_ptr = d;
+  return INFERD_OK;
+}
+
 }  // extern "C"

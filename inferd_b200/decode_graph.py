@@ -7,8 +7,10 @@ step of a whole batch is one graph replay:
     one host->device copy of the step's inputs (queries, new K and V, slots, lengths and
     page-table changes) from pinned memory
     -> sparse page-table update of a device-resident [B, capacity] table
-    -> KV append (reshape_and_cache) -> paged attention over the table
-    -> device->host copy of the output
+    -> KV append (reshape_and_cache) -> paged attention over the table, whose epilogue
+       copies each finished block of output rows to pinned host memory as the grid runs
+       (a device->host copy after the grid where the kernel's tensor-core path does not
+       apply)
 
 The host side of a step -- reserving pages, computing slots, lengths and the table changes --
 runs in C (csrc/host_ops.cpp) on the PagedKVCache's own page tables and lands in pinned
@@ -34,6 +36,7 @@ grows) before the replay.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import numpy as np
@@ -42,6 +45,30 @@ import torch
 from . import _lib
 from .paged_attn import paged_attention_batched
 from .paged_cache import _CLEAN, PagedKVCache, _hostops
+
+
+class _HostRows:
+    """A step's pinned host output as the one destination of the attention's epilogue copy
+    (paged_attention_batched's `gather` protocol: device, rows, tail, dtype, begin,
+    publish).  The kernel stores every finished block of rows to the host as 16-byte
+    vectors while the rest of the grid runs, so no device-to-host copy follows the grid."""
+
+    def __init__(self, host: torch.Tensor, device: torch.device) -> None:
+        lib = _lib.load()
+        dptr = ctypes.c_void_p()
+        _lib.check(lib.inferd_host_device_pointer(host.data_ptr(), ctypes.byref(dptr)),
+                   "host_device_pointer")
+        self.device = device
+        self.rows = host.shape[0]
+        self.tail = tuple(host.shape[1:])
+        self.dtype = host.dtype
+        self._dst = torch.tensor([dptr.value], dtype=torch.int64, device=device)
+
+    def begin(self) -> tuple[int, int, int]:
+        return self._dst.data_ptr(), 1, 0
+
+    def publish(self) -> None:
+        pass
 
 
 class DecodeGraph:
@@ -90,6 +117,14 @@ class DecodeGraph:
             self._meta_h[i].zero_()
         self._out_h = [torch.empty((b, ql, num_q_heads, d), dtype=dt, pin_memory=True) for _ in range(2)]
         self._out_d = torch.empty((b, ql, num_q_heads, d), dtype=dt, device=dev)
+        # the attention writes the pinned outputs itself when its tensor-core path applies
+        # (decided by the first warm-up step); otherwise one copy follows it in the graph
+        self._host_rows = None
+        if copy_out:
+            try:
+                self._host_rows = [_HostRows(h, self._out_d.device) for h in self._out_h]
+            except (ValueError, RuntimeError):
+                self._host_rows = None
         self._events = [torch.cuda.Event(), torch.cuda.Event()]
         self._recorded = [False, False]
         self._set = 0            # staging set the next prepare/launch uses
@@ -157,9 +192,16 @@ class DecodeGraph:
         k = self._inp_d[self._nq:self._nq + self._nk].view(b * ql, cache.num_kv_heads, d)
         v = self._inp_d[self._nq + self._nk:].view(b * ql, cache.num_kv_heads, d)
         cache._write(self.layer, k, v, self._slots_d)
-        paged_attention_batched(q, cache.key_cache[self.layer], cache.value_cache[self.layer], self._master,
-                                self._meta_d[:b], scale=self.scale,
-                                max_context_len=self._cap * cache.block_size, out=self._out_d)
+        args = (q, cache.key_cache[self.layer], cache.value_cache[self.layer], self._master,
+                self._meta_d[:b])
+        kw = dict(scale=self.scale, max_context_len=self._cap * cache.block_size, out=self._out_d)
+        if self._host_rows is not None:
+            try:
+                paged_attention_batched(*args, gather=self._host_rows[i], **kw)
+                return
+            except ValueError:  # shapes outside the tensor-core path: copy after the grid
+                self._host_rows = None
+        paged_attention_batched(*args, **kw)
         if self.copy_out:
             self._out_h[i].copy_(self._out_d, non_blocking=True)
 

@@ -58,6 +58,7 @@ def test_graph_steps_equal_eager_steps(cuda_device, q_len, max_pairs):
     graph._upload_dense = counted_upload
     rng = np.random.default_rng(q_len)
     caps = set()
+    assert graph._host_rows is not None  # the attention writes the pinned output itself
     for step in range(60):
         q = torch.randn(len(ids), q_len, HQ, D, generator=g).to(torch.bfloat16)
         k = torch.randn(len(ids) * q_len, HKV, D, generator=g).to(torch.bfloat16)
@@ -140,3 +141,56 @@ def test_abort_and_exhausted_pool(cuda_device):
     lens_after = [a.sequence_length(s) for s in ids]
     assert lens_after == [30 + steps, 31 + steps]
     a.assert_consistent()
+
+
+def test_host_device_pointer_of_pinned_and_pageable_memory(cuda_device):
+    import ctypes
+
+    from inferd_b200 import _lib
+
+    lib = _lib.load()
+    dptr = ctypes.c_void_p()
+    pinned = torch.empty(4096, dtype=torch.uint8, pin_memory=True)
+    assert lib.inferd_host_device_pointer(pinned.data_ptr(), ctypes.byref(dptr)) == _lib.OK
+    assert dptr.value is not None
+    pageable = torch.empty(4096, dtype=torch.uint8)
+    assert lib.inferd_host_device_pointer(pageable.data_ptr(), ctypes.byref(dptr)) == _lib.ERR_CUDA
+    assert lib.inferd_host_device_pointer(None, ctypes.byref(dptr)) == _lib.ERR_INVALID_ARGUMENT
+    x = torch.arange(10, device=cuda_device)
+    assert int(x.sum()) == 45  # no error is left behind for later launches
+
+
+def test_fp32_pool_copies_the_output_after_the_grid(cuda_device):
+    # fp32 pools take the generic attention kernel, which has no epilogue copy: the graph
+    # falls back to a device-to-host copy after the grid, with the same results
+    g = torch.Generator().manual_seed(3)
+    lens = [5, 40, 77]
+    caches = [PagedKVCache(num_layers=1, num_blocks=64, block_size=BS, num_kv_heads=HKV, head_dim=D,
+                           dtype=torch.float32, device=cuda_device) for _ in range(2)]
+    for s, n in enumerate(lens):
+        k = torch.randn(n, HKV, D, generator=g).to(cuda_device)
+        v = torch.randn(n, HKV, D, generator=g).to(cuda_device)
+        for c in caches:
+            c.create_sequence(s)
+            c.append_tokens(s, [k], [v])
+    a, b = caches
+    ids = list(range(len(lens)))
+    graph = DecodeGraph(a, ids, num_q_heads=HQ, q_len=1)
+    assert graph._host_rows is None
+    for step in range(3):
+        q = torch.randn(len(ids), 1, HQ, D, generator=g)
+        k = torch.randn(len(ids), HKV, D, generator=g)
+        v = torch.randn(len(ids), HKV, D, generator=g)
+        graph.prepare()
+        gq, gk, gv = graph.inputs()
+        gq.copy_(q)
+        gk.copy_(k)
+        gv.copy_(v)
+        graph.launch()
+        torch.cuda.synchronize()
+        plan = b.plan_append(ids, 1)
+        b.commit_append(plan, [k.to(cuda_device)], [v.to(cuda_device)])
+        out_e = paged_attention_batched(q.to(cuda_device), b.key_cache[0], b.value_cache[0],
+                                        plan.block_tables, plan.context_lens,
+                                        max_context_len=graph._cap * BS).cpu()
+        assert torch.equal(graph.result(), out_e), f"step {step}"
